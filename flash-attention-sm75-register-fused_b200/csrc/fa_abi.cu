@@ -1,0 +1,303 @@
+// Host side of the C ABI declared in include/fa_b200.h: argument checks,
+// TMA descriptor construction, launch of the sm_100a kernel, the
+// reference-compatible blocking launchers, and the materialised ("naive")
+// attention that the reference exports for API completeness.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "fa_b200.h"
+#include "fa_fwd.h"
+
+namespace {
+
+std::atomic<unsigned> g_epoch{1};
+std::atomic<unsigned long long> g_timeout_ns{1000000000ull};
+std::atomic<int> g_debug_flags{0};
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// [rows = B*H*N, d] tensor viewed as 3-D (d, N, B*H) so that a 128-row box
+// never crosses into the next head: rows >= N read as zeros.
+bool make_map(CUtensorMap* map, const void* base, int d, int n, long long bh, bool bf16) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n),
+                              static_cast<cuuint64_t>(bh)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
+                                 static_cast<cuuint64_t>(n) * static_cast<cuuint64_t>(d) * 2};
+  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r =
+      fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  static int major_cache[64] = {0};
+  int major = (dev >= 0 && dev < 64) ? major_cache[dev] : 0;
+  if (major == 0) {
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return FA_ERR_CUDA;
+    if (dev >= 0 && dev < 64) major_cache[dev] = major;
+  }
+  return major == 10 ? FA_OK : FA_ERR_DEVICE;
+}
+
+// ------------------------------------------------------------------ naive
+// S = Q K^T * scale (masked entries = -1e9, as reference naive_attention.cu:31-34),
+// row softmax in place, O = P V.  One thread per output element; fp32 math.
+__global__ void naive_qk_kernel(const __half* __restrict__ Q, const __half* __restrict__ K,
+                                float* __restrict__ S, int n, int d, float scale, int causal) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;  // key
+  const int i = blockIdx.y * blockDim.y + threadIdx.y;  // query
+  const long long bh = blockIdx.z;
+  if (i >= n || j >= n) return;
+  float* out = S + (bh * n + i) * static_cast<long long>(n) + j;
+  if (causal && j > i) {
+    *out = -1e9f;
+    return;
+  }
+  const __half* q = Q + (bh * n + i) * d;
+  const __half* k = K + (bh * n + j) * d;
+  float acc = 0.f;
+  for (int c = 0; c < d; ++c) acc = fmaf(__half2float(q[c]), __half2float(k[c]), acc);
+  *out = acc * scale;
+}
+
+__global__ void naive_softmax_kernel(float* __restrict__ S, int n) {
+  // one warp per row
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const long long bh = blockIdx.y;
+  if (row >= n) return;
+  float* s = S + (bh * n + row) * static_cast<long long>(n);
+  float mx = -INFINITY;
+  for (int c = lane; c < n; c += 32) mx = fmaxf(mx, s[c]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int c = lane; c < n; c += 32) {
+    const float e = expf(s[c] - mx);
+    s[c] = e;
+    sum += e;
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.0f / sum;
+  for (int c = lane; c < n; c += 32) s[c] *= inv;
+}
+
+__global__ void naive_pv_kernel(const float* __restrict__ P, const __half* __restrict__ V,
+                                __half* __restrict__ O, int n, int d) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;  // head-dim column
+  const int i = blockIdx.y * blockDim.y + threadIdx.y;  // query
+  const long long bh = blockIdx.z;
+  if (i >= n || c >= d) return;
+  const float* p = P + (bh * n + i) * static_cast<long long>(n);
+  const __half* v = V + bh * n * static_cast<long long>(d) + c;
+  float acc = 0.f;
+  for (int j = 0; j < n; ++j) acc = fmaf(p[j], __half2float(v[static_cast<long long>(j) * d]), acc);
+  O[(bh * n + i) * d + c] = __float2half_rn(acc);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+           int Hkv, int N, int head_dim, float scale, int causal, int dtype, void* stream) {
+  if (B < 0 || Hq < 0 || Hkv < 0 || N < 0) return FA_ERR_INVALID_ARG;
+  if (head_dim != 64 && head_dim != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_DTYPE;
+  if (causal != 0 && causal != 1) return FA_ERR_INVALID_ARG;
+  if (B == 0 || Hq == 0 || N == 0) return FA_OK;
+  if (Hkv == 0) return FA_ERR_INVALID_ARG;
+  if (Hq % Hkv != 0) return FA_ERR_GQA_DIVISIBILITY;
+  if (!Q || !K || !V || !O) return FA_ERR_INVALID_ARG;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) ||
+      (reinterpret_cast<uintptr_t>(lse) & 3u))
+    return FA_ERR_ALIGNMENT;
+  if (!std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  const long long bhq = static_cast<long long>(B) * Hq;
+  const long long n_qpairs = (static_cast<long long>(N) + 255) / 256;
+  if (bhq * n_qpairs > 0x7fffffffLL || static_cast<long long>(N) + 256 > 0x7fffffffLL)
+    return FA_ERR_TOO_LARGE;
+  if (int rc = check_device()) return rc;
+
+  fa::FwdParams p;
+  const bool bf16 = dtype == FA_DTYPE_BF16;
+  if (!make_map(&p.tm_q, Q, head_dim, N, bhq, bf16) ||
+      !make_map(&p.tm_k, K, head_dim, N, static_cast<long long>(B) * Hkv, bf16) ||
+      !make_map(&p.tm_v, V, head_dim, N, static_cast<long long>(B) * Hkv, bf16))
+    return FA_ERR_TENSOR_MAP;
+  p.o = O;
+  p.lse = lse;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.N = N;
+  p.group = Hq / Hkv;
+  p.n_qpairs = static_cast<int>(n_qpairs);
+  p.n_kv_tiles = (N + 127) / 128;
+  p.causal = causal;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.debug_flags = g_debug_flags.load(std::memory_order_relaxed);
+  p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
+  p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+  const cudaError_t e = fa::launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+static void legacy_fwd(const char* tag, const void* Q, const void* K, const void* V, void* O,
+                       int batch, int heads, int seq_len, int head_dim, float scale, bool causal) {
+  const int rc = fa_fwd(Q, K, V, O, nullptr, batch, heads, heads, seq_len, head_dim, scale,
+                        causal ? 1 : 0, FA_DTYPE_F16, nullptr);
+  if (rc != FA_OK) {
+    if (rc == FA_ERR_UNSUPPORTED_HEAD_DIM)
+      fprintf(stderr, "[%s] head_dim=%d not supported\n", tag, head_dim);
+    else
+      fprintf(stderr, "[%s] %s\n", tag, fa_error_string(rc));
+    return;
+  }
+  cudaDeviceSynchronize();
+}
+
+void launch_flash_attention_forward(const void* Q, const void* K, const void* V, void* O,
+                                    int batch, int heads, int seq_len, int head_dim, float scale,
+                                    bool causal) {
+  legacy_fwd("flash_attn", Q, K, V, O, batch, heads, seq_len, head_dim, scale, causal);
+}
+
+void launch_flash_attention_forward_scalar(const void* Q, const void* K, const void* V, void* O,
+                                           int batch, int heads, int seq_len, int head_dim,
+                                           float scale, bool causal) {
+  if (head_dim != 64) {
+    fprintf(stderr, "[flash_attn_scalar] head_dim=%d not supported\n", head_dim);
+    return;
+  }
+  legacy_fwd("flash_attn_scalar", Q, K, V, O, batch, heads, seq_len, head_dim, scale, causal);
+}
+
+void launch_flash_attention_forward_wmma_qk(const void* Q, const void* K, const void* V, void* O,
+                                            int batch, int heads, int seq_len, int head_dim,
+                                            float scale, bool causal) {
+  if (head_dim != 64) {
+    fprintf(stderr, "[flash_attn_wmma_qk] head_dim=%d not supported\n", head_dim);
+    return;
+  }
+  legacy_fwd("flash_attn_wmma_qk", Q, K, V, O, batch, heads, seq_len, head_dim, scale, causal);
+}
+
+int fa_naive_fwd(const void* Q, const void* K, const void* V, void* O, int batch, int heads,
+                 int seq_len, int head_dim, float scale, int causal, float* workspace,
+                 void* stream) {
+  if (batch < 0 || heads < 0 || seq_len < 0 || head_dim <= 0) return FA_ERR_INVALID_ARG;
+  if (batch == 0 || heads == 0 || seq_len == 0) return FA_OK;
+  if (!Q || !K || !V || !O || !workspace) return FA_ERR_INVALID_ARG;
+  const long long bh = static_cast<long long>(batch) * heads;
+  if (bh > 65535) return FA_ERR_TOO_LARGE;  // grid.z limit
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* q = static_cast<const __half*>(Q);
+  const __half* k = static_cast<const __half*>(K);
+  const __half* v = static_cast<const __half*>(V);
+  {
+    dim3 block(32, 8);
+    dim3 grid((seq_len + 31) / 32, (seq_len + 7) / 8, static_cast<unsigned>(bh));
+    naive_qk_kernel<<<grid, block, 0, s>>>(q, k, workspace, seq_len, head_dim, scale, causal);
+  }
+  {
+    dim3 block(256);
+    dim3 grid((seq_len + 7) / 8, static_cast<unsigned>(bh));
+    naive_softmax_kernel<<<grid, block, 0, s>>>(workspace, seq_len);
+  }
+  {
+    dim3 block(32, 8);
+    dim3 grid((head_dim + 31) / 32, (seq_len + 7) / 8, static_cast<unsigned>(bh));
+    naive_pv_kernel<<<grid, block, 0, s>>>(workspace, v, static_cast<__half*>(O), seq_len,
+                                           head_dim);
+  }
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+void launch_naive_attention(const void* Q, const void* K, const void* V, void* O, int batch,
+                            int heads, int seq_len, int head_dim, float scale, bool causal,
+                            float* workspace) {
+  const int rc = fa_naive_fwd(Q, K, V, O, batch, heads, seq_len, head_dim, scale, causal ? 1 : 0,
+                              workspace, nullptr);
+  if (rc != FA_OK) fprintf(stderr, "[naive_attention] %s\n", fa_error_string(rc));
+  cudaDeviceSynchronize();
+}
+
+int flatargs_launch(const void* Q, const void* K, const void* V, void* O, int B, int H, int N,
+                    float scale, void* stream) {
+  return fa_fwd(Q, K, V, O, nullptr, B, H, H, N, 64, scale, 0, FA_DTYPE_F16, stream);
+}
+
+int launch_v2(const void* Q, const void* K, const void* V, void* O, int B, int H, int N,
+              float scale, int mode, void* stream) {
+  if (mode != 0 && mode != 1) return FA_ERR_INVALID_ARG;
+  return fa_fwd(Q, K, V, O, nullptr, B, H, H, N, 64, scale, mode, FA_DTYPE_F16, stream);
+}
+
+int fa_device_status(int reset) {
+  unsigned long long st = 0;
+  if (fa::read_status(&st, reset != 0) != cudaSuccess) return FA_ERR_CUDA;
+  return static_cast<int>(st & 0xffffffffull);
+}
+
+void fa_set_watchdog_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1ull); }
+
+void fa_set_debug_flags(int flags) { g_debug_flags.store(flags); }
+
+const char* fa_error_string(int code) {
+  switch (code) {
+    case FA_OK: return "ok";
+    case FA_ERR_INVALID_ARG: return "invalid argument";
+    case FA_ERR_UNSUPPORTED_HEAD_DIM: return "supports head_dim=64 or 128 only";
+    case FA_ERR_GQA_DIVISIBILITY: return "Q heads not divisible by K/V heads";
+    case FA_ERR_ALIGNMENT: return "Q/K/V/O must be 16-byte aligned (LSE 4-byte)";
+    case FA_ERR_DTYPE: return "dtype must be FA_DTYPE_F16 or FA_DTYPE_BF16";
+    case FA_ERR_TENSOR_MAP: return "TMA descriptor creation failed";
+    case FA_ERR_LAUNCH: return "kernel launch failed";
+    case FA_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case FA_ERR_CUDA: return "CUDA runtime call failed";
+    case FA_ERR_TOO_LARGE: return "problem size exceeds the kernel's index range";
+    default: break;
+  }
+  if (code >= FA_ERR_TIMEOUT_BASE) return "device watchdog: an in-kernel wait timed out";
+  return "unknown error";
+}
+
+int fa_smem_bytes(int head_dim) {
+  if (head_dim != 64 && head_dim != 128) return -1;
+  return fa::smem_bytes_for(head_dim);
+}
+
+const char* fa_version(void) { return "fa_b200 0.1.0 (sm_100a tcgen05)"; }
+
+}  // extern "C"

@@ -1,0 +1,521 @@
+// FlashAttention forward for B200 (sm_100a).
+//
+//   O = softmax(Q K^T * scale) V      (+ LSE = logsumexp(Q K^T * scale) per row)
+//
+// Replaces the sm_75 WMMA kernels of the reference
+// (src/kernels/flash_attention_forward.cu:345-791,
+//  flash-attention-sm75-fused/src/flash_mha_flatargs.cu:86-226,
+//  flash-attention-sm75-fused/src/flash_mha_v2.cu:165-361) with one
+// warp-specialised tcgen05 kernel.  The math is the same online softmax
+// (flash-attention-sm75-fused/include/online_step.cuh:36-126): running row
+// max m, running sum l, O rescaled by exp(m_old - m_new), O / l at the end.
+//
+// One CTA owns a "Q pair": two 128-row tiles of one (batch, query-head).
+//   warps 0-3  softmax group 0  (rows   0..127 of the pair, one row / thread)
+//   warps 4-7  softmax group 1  (rows 128..255)
+//   warp  8    TMA producer     (Q once, K/V through a kStages ring)
+//   warp  9    MMA issuer       (tcgen05.mma, one thread) + TMEM owner
+//
+// Tensor memory (512 columns x 128 lanes, lane = query row of a tile):
+//   S_g  = Q_g K_j^T        fp32, 128 columns per group
+//   P_g  = exp2(S_g - m)    f16/bf16 pairs, 64 columns (aliases S_g when d=128)
+//   O_g += P_g V_j          fp32, d columns per group
+// QK^T reads both operands from shared memory; PV reads P from TMEM.
+//
+// Causal masking is top-left aligned (key j visible to query i iff j <= i),
+// as in src/reference/attention_ref.py:33-40.  Tiles above the diagonal are
+// never loaded or multiplied; the diagonal tile is masked in registers.
+// GQA maps query head h to KV head h / (Hq/Hkv), the mapping that
+// repeat_interleave gives in src/flash_attention_sm75/ops.py:24-26, without
+// materialising the repeated K/V.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "fa_fwd.h"
+#include "sm100_ptx.cuh"
+
+namespace fa {
+
+// Sticky device status: high 32 bits = launch epoch, low 32 bits = error code.
+// Written only when a bounded wait expires; read by fa_device_status().
+__device__ unsigned long long g_fa_status = 0ull;
+
+namespace {
+
+constexpr int kBlockM = 128;  // query rows per tile (one TMEM lane each)
+constexpr int kBlockN = 128;  // keys per K/V tile
+constexpr int kThreads = 320;
+constexpr int kWarpLoad = 8;
+constexpr int kWarpMma = 9;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows > 2^8
+
+template <int D>
+struct Layout {
+  static constexpr int kColBlocks = D / 64;       // 128-byte swizzle column blocks
+  static constexpr int kBlockBytes = kBlockM * 128;  // one 64-column block of a 128-row tile
+  static constexpr int kTile = kBlockM * D * 2;   // bytes of a 128-row f16 tile
+  static constexpr int kStages = (D == 128) ? 2 : 4;
+  // shared memory (offsets from a 1024-aligned base)
+  static constexpr int kOffQ = 0;                 // Q0, Q1
+  static constexpr int kOffKV = 2 * kTile;        // stage s: K at +2s*kTile, V at +(2s+1)*kTile
+  static constexpr int kOffBar = kOffKV + kStages * 2 * kTile;
+  // barrier indices
+  static constexpr int kBarQ = 0;                       // 2
+  static constexpr int kBarK = 2;                       // kStages
+  static constexpr int kBarV = kBarK + kStages;         // kStages
+  static constexpr int kBarEmpty = kBarV + kStages;     // kStages
+  static constexpr int kBarS = kBarEmpty + kStages;     // 2
+  static constexpr int kBarP = kBarS + 2;               // 2
+  static constexpr int kBarO = kBarP + 2;               // 2
+  static constexpr int kBarDrain = kBarO + 2;           // 1
+  static constexpr int kNumBars = kBarDrain + 1;
+  static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
+  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kDynBytes = kBytes + 1024;  // slack for 1024-byte alignment
+  // tensor memory columns
+  static constexpr uint32_t kTmemCols = 512;
+  __host__ __device__ static constexpr uint32_t tS(int g) { return g ? 128u : 0u; }
+  __host__ __device__ static constexpr uint32_t tO(int g) { return g ? 256u + D : 256u; }
+  // d=128 fills TMEM, so P overwrites the S columns it was computed from;
+  // d=64 leaves room for separate P columns.
+  static constexpr bool kAliasP = (D == 128);
+  __host__ __device__ static constexpr uint32_t tP(int g) {
+    return kAliasP ? tS(g) : (g ? 448u : 384u);
+  }
+  static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct WaitCtl {
+  volatile int* abort;        // CTA-wide abort flag in shared memory
+  unsigned long long timeout_ns;
+  unsigned epoch;
+};
+
+__device__ void record_error(unsigned epoch, int code) {
+  const unsigned long long want =
+      (static_cast<unsigned long long>(epoch) << 32) | static_cast<unsigned>(code);
+  unsigned long long old = atomicAdd(&g_fa_status, 0ull);
+  while (true) {
+    if ((old >> 32) == epoch && (old & 0xffffffffull) != 0ull) return;  // first error wins
+    const unsigned long long prev = atomicCAS(&g_fa_status, old, want);
+    if (prev == old) return;
+    old = prev;
+  }
+}
+
+__device__ __forceinline__ bool bar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                           int site, bool respect_abort) {
+  const uint64_t t0 = ptx::global_timer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((++it & 15u) == 0u) {
+      if (respect_abort && *c.abort) return false;
+      if (ptx::global_timer_ns() - t0 > c.timeout_ns) {
+        *c.abort = 1;
+        record_error(c.epoch, FA_ERR_TIMEOUT_BASE + site);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded mbarrier wait.  Returns false if the CTA is aborting or the wait
+// exceeded the watchdog deadline (which also records the error and aborts).
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, const WaitCtl& c, int site,
+                                         bool respect_abort = true) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  return bar_wait_slow(bar, parity, c, site, respect_abort);
+}
+
+// Make the values produced by tcgen05.ld visible to ordinary instructions
+// only after tcgen05.wait::ld (the empty volatile asm cannot move above it).
+template <int N>
+__device__ __forceinline__ void pin_after_wait(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_constant__ FwdParams p) {
+  using L = Layout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
+
+  // ---- work item: (batch*head, Q pair); causal pairs of one head run heaviest first
+  const int bh = blockIdx.x / p.n_qpairs;
+  int qp = blockIdx.x % p.n_qpairs;
+  if (p.causal) qp = p.n_qpairs - 1 - qp;
+  const int b = bh / p.Hq;
+  const int hq = bh % p.Hq;
+  const int bh_kv = b * p.Hkv + hq / p.group;
+  const int q_row0 = qp * 2 * kBlockM;
+  const bool has_q1 = q_row0 + kBlockM < p.N;
+  int n_kv[2];
+  if (p.causal) {
+    n_kv[0] = min(2 * qp + 1, p.n_kv_tiles);
+    n_kv[1] = has_q1 ? min(2 * qp + 2, p.n_kv_tiles) : 0;
+  } else {
+    n_kv[0] = p.n_kv_tiles;
+    n_kv[1] = has_q1 ? p.n_kv_tiles : 0;
+  }
+  const int n_loop = max(n_kv[0], n_kv[1]);
+
+  // ---- set-up: skip the CTA if this launch already failed elsewhere
+  if (threadIdx.x == 0) {
+    const unsigned long long st = *reinterpret_cast<volatile unsigned long long*>(&g_fa_status);
+    *abort_flag = ((st >> 32) == p.epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
+    for (int i = 0; i < L::kNumBars; ++i) {
+      const bool is_p = (i == L::kBarP || i == L::kBarP + 1);
+      ptx::mbar_init(bar(i), is_p ? 128u : 1u);
+    }
+    ptx::fence_barrier_init();
+  }
+  __syncthreads();
+  if (*abort_flag) return;
+  if (warp == kWarpMma) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), L::kTmemCols);
+    ptx::tmem_relinquish();
+    ptx::tc_fence_before();
+  }
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
+
+  if (warp == kWarpLoad) {
+    // ===================================================== TMA producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&p.tm_q);
+      ptx::prefetch_tmap(&p.tm_k);
+      ptx::prefetch_tmap(&p.tm_v);
+      const uint64_t pol_q = ptx::policy_evict_first();
+      const uint64_t pol_kv = ptx::policy_evict_last();
+      const bool skip_q = (p.debug_flags & FA_DEBUG_SKIP_Q_LOAD) != 0;
+      for (int g = 0; g < 2; ++g) {
+        if (g == 1 && !has_q1) break;
+        if (skip_q) break;  // test hook: nothing ever arrives on the Q barriers
+        ptx::mbar_arrive_expect_tx(bar(L::kBarQ + g), L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kColBlocks; ++c)
+          ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
+                           bar(L::kBarQ + g), c * 64, q_row0 + g * kBlockM, bh, pol_q);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_loop; ++j) {
+        const int s = j % L::kStages;
+        if (j >= L::kStages && !bar_wait(bar(L::kBarEmpty + s), ((j / L::kStages) - 1) & 1, wc, 1))
+          break;
+        const uint32_t k_dst = sbase + L::kOffKV + (2 * s) * L::kTile;
+        const uint32_t v_dst = k_dst + L::kTile;
+        ptx::mbar_arrive_expect_tx(bar(L::kBarK + s), L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kColBlocks; ++c)
+          ptx::tma_load_3d(k_dst + c * L::kBlockBytes, &p.tm_k, bar(L::kBarK + s), c * 64,
+                           j * kBlockN, bh_kv, pol_kv);
+        ptx::mbar_arrive_expect_tx(bar(L::kBarV + s), L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kColBlocks; ++c)
+          ptx::tma_load_3d(v_dst + c * L::kBlockBytes, &p.tm_v, bar(L::kBarV + s), c * 64,
+                           j * kBlockN, bh_kv, pol_kv);
+        issued = j + 1;
+      }
+      // Drain: every copy this thread started must land before the CTA exits.
+      for (int j = max(0, issued - L::kStages); j < issued; ++j) {
+        const int s = j % L::kStages;
+        bar_wait(bar(L::kBarK + s), (j / L::kStages) & 1, wc, 2, false);
+        bar_wait(bar(L::kBarV + s), (j / L::kStages) & 1, wc, 2, false);
+      }
+      if (!skip_q) {
+        bar_wait(bar(L::kBarQ), 0, wc, 2, false);
+        if (has_q1) bar_wait(bar(L::kBarQ + 1), 0, wc, 2, false);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ===================================================== MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t fmt = BF16 ? 1u : 0u;
+      constexpr uint32_t idesc_qk = ptx::make_idesc_f16(kBlockM, kBlockN, fmt, 0, 0);
+      constexpr uint32_t idesc_pv = ptx::make_idesc_f16(kBlockM, D, fmt, 0, 1);
+
+      auto issue_s = [&](int g, int s) {
+        const uint32_t qa = sbase + L::kOffQ + g * L::kTile;
+        const uint32_t ka = sbase + L::kOffKV + (2 * s) * L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk / 4) * L::kBlockBytes + (kk % 4) * 32;
+          ptx::mma_ss(tmem + L::tS(g), ptx::smem_desc_sw128(qa + off, 16, 1024),
+                      ptx::smem_desc_sw128(ka + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int g, int s, bool accumulate) {
+        const uint32_t va = sbase + L::kOffKV + (2 * s + 1) * L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk) {
+          ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
+                      ptx::smem_desc_sw128(va + kk * 2048, L::kBlockBytes, 1024), idesc_pv,
+                      (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+
+      bool ok = bar_wait(bar(L::kBarQ), 0, wc, 10);
+      if (ok && has_q1) ok = bar_wait(bar(L::kBarQ + 1), 0, wc, 10);
+      if (ok) ok = bar_wait(bar(L::kBarK), 0, wc, 11);
+      if (ok) {
+        issue_s(0, 0);
+        ptx::mma_commit(bar(L::kBarS));
+        if (n_kv[1] > 0) {
+          issue_s(1, 0);
+          ptx::mma_commit(bar(L::kBarS + 1));
+        }
+      }
+      for (int j = 0; ok && j < n_loop; ++j) {
+        const int s = j % L::kStages;
+        const uint32_t ph = (j / L::kStages) & 1;
+        const int s1 = (j + 1) % L::kStages;
+        const uint32_t ph1 = ((j + 1) / L::kStages) & 1;
+        if (!(ok = bar_wait(bar(L::kBarV + s), ph, wc, 12))) break;
+        if (j < n_kv[0]) {
+          if (!(ok = bar_wait(bar(L::kBarP), j & 1, wc, 13))) break;
+          ptx::tc_fence_after();
+          issue_pv(0, s, j > 0);
+          ptx::mma_commit(bar(L::kBarO));
+          if (j + 1 < n_kv[0]) {
+            if (!(ok = bar_wait(bar(L::kBarK + s1), ph1, wc, 14))) break;
+            if (L::kAliasP && !(ok = bar_wait(bar(L::kBarO), j & 1, wc, 15))) break;
+            issue_s(0, s1);
+            ptx::mma_commit(bar(L::kBarS));
+          }
+        }
+        if (j < n_kv[1]) {
+          if (!(ok = bar_wait(bar(L::kBarP + 1), j & 1, wc, 16))) break;
+          ptx::tc_fence_after();
+          issue_pv(1, s, j > 0);
+          ptx::mma_commit(bar(L::kBarO + 1));
+        }
+        ptx::mma_commit(bar(L::kBarEmpty + s));
+        if (j + 1 < n_kv[1]) {
+          if (!(ok = bar_wait(bar(L::kBarK + s1), ph1, wc, 17))) break;
+          if (L::kAliasP && !(ok = bar_wait(bar(L::kBarO + 1), j & 1, wc, 18))) break;
+          issue_s(1, s1);
+          ptx::mma_commit(bar(L::kBarS + 1));
+        }
+      }
+      // Drain: all MMAs issued above complete before TMEM is released.
+      ptx::mma_commit(bar(L::kBarDrain));
+      bar_wait(bar(L::kBarDrain), 0, wc, 19, false);
+    }
+  } else {
+    // ===================================================== softmax groups
+    const int g = warp >> 2;
+    const int n_tiles = n_kv[g];
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;               // row within the tile == TMEM lane
+    const int tile = 2 * qp + g;                // global 128-row tile index
+    const int q_row = tile * kBlockM + r;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + L::tS(g);
+    const uint32_t tP = tmem + lane_off + L::tP(g);
+    const uint32_t tO = tmem + lane_off + L::tO(g);
+    const float sl = p.scale_log2;
+
+    float m = -INFINITY;  // running max of the scaled scores (log2 units)
+    float l = 0.f;        // running sum of exp2(s - m)
+    bool ok = n_tiles > 0;
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), j & 1, wc, 20 + g));
+      if (!ok) break;
+      ptx::tc_fence_after();
+
+      float x[kBlockN];
+      {
+        uint32_t u0[32], u1[32], u2[32], u3[32];
+        ptx::tmem_ld32(tS + 0, u0);
+        ptx::tmem_ld32(tS + 32, u1);
+        ptx::tmem_ld32(tS + 64, u2);
+        ptx::tmem_ld32(tS + 96, u3);
+        ptx::tmem_wait_ld();
+        pin_after_wait<32>(u0);
+        pin_after_wait<32>(u1);
+        pin_after_wait<32>(u2);
+        pin_after_wait<32>(u3);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          x[c] = __uint_as_float(u0[c]) * sl;
+          x[32 + c] = __uint_as_float(u1[c]) * sl;
+          x[64 + c] = __uint_as_float(u2[c]) * sl;
+          x[96 + c] = __uint_as_float(u3[c]) * sl;
+        }
+      }
+
+      const int key0 = j * kBlockN;
+      const bool diag = p.causal && (j == tile);
+      const bool ragged = key0 + kBlockN > p.N;
+      if (diag || ragged) {
+        int lim = p.N - key0;
+        if (diag) lim = min(lim, r + 1);
+#pragma unroll
+        for (int c = 0; c < kBlockN; ++c)
+          if (c >= lim) x[c] = -INFINITY;
+      }
+
+      float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
+#pragma unroll
+      for (int c = 4; c < kBlockN; c += 4) {
+        mx0 = fmaxf(mx0, x[c]);
+        mx1 = fmaxf(mx1, x[c + 1]);
+        mx2 = fmaxf(mx2, x[c + 2]);
+        mx3 = fmaxf(mx3, x[c + 3]);
+      }
+      const float m_new = fmaxf(m, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+      const bool grow = m_new > m + kRescaleThreshold;
+      if (j == 0) {
+        m = m_new;
+      } else {
+        // O_g holds PV of tiles < j (their MMAs completed before S_g(j) was
+        // signalled) and is not written again until this group arrives on P.
+        if (__any_sync(0xffffffffu, grow)) {
+          const float alpha = grow ? ptx::ex2_approx(m - m_new) : 1.0f;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld32(tO + c * 32, o);
+            ptx::tmem_wait_ld();
+            pin_after_wait<32>(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            ptx::tmem_st32(tO + c * 32, o);
+          }
+          ptx::tmem_wait_st();
+          if (grow) l *= alpha;
+        }
+        if (grow) m = m_new;
+      }
+      const float m_use = (m == -INFINITY) ? 0.f : m;
+
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float e0 = ptx::ex2_approx(x[64 * h + 2 * c] - m_use);
+          const float e1 = ptx::ex2_approx(x[64 * h + 2 * c + 1] - m_use);
+          s0 += e0;
+          s1 += e1;
+          pk[c] = pack2<BF16>(e0, e1);
+        }
+        ptx::tmem_st32(tP + 32 * h, pk);
+      }
+      l += s0 + s1;
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(L::kBarP + g));
+    }
+
+    // ---- epilogue: O / l -> global, LSE
+    if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarO + g), (n_tiles - 1) & 1, wc, 22 + g));
+    if (ok) {
+      ptx::tc_fence_after();
+      const bool row_ok = q_row < p.N;
+      const float inv_l = (l > 0.f) ? 1.0f / l : 0.f;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = reinterpret_cast<T*>(p.o) + (static_cast<size_t>(bh) * p.N + q_row) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        ptx::tmem_ld32(tO + c * 32, o);
+        ptx::tmem_wait_ld();
+        pin_after_wait<32>(o);
+        uint32_t h[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          h[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+        }
+      }
+      if (row_ok && p.lse != nullptr) {
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        p.lse[static_cast<size_t>(bh) * p.N + q_row] =
+            (l > 0.f) ? (m_use + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+      }
+    }
+  }
+
+  // ---- teardown
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+}  // namespace
+
+template <int D, bool BF16>
+static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream) {
+  auto kern = fa_fwd_kernel<D, BF16>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Layout<D>::kDynBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
+  }
+  kern<<<grid, kThreads, Layout<D>::kDynBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
+  const int grid = p.n_qpairs * p.B * p.Hq;
+  if (head_dim == 64) return bf16 ? launch_impl<64, true>(p, grid, stream) : launch_impl<64, false>(p, grid, stream);
+  return bf16 ? launch_impl<128, true>(p, grid, stream) : launch_impl<128, false>(p, grid, stream);
+}
+
+int smem_bytes_for(int head_dim) {
+  return head_dim == 64 ? Layout<64>::kDynBytes : Layout<128>::kDynBytes;
+}
+
+cudaError_t read_status(unsigned long long* out, bool reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_fa_status, sizeof(*out));
+  if (e != cudaSuccess) return e;
+  if (reset) {
+    const unsigned long long zero = 0ull;
+    e = cudaMemcpyToSymbol(g_fa_status, &zero, sizeof(zero));
+  }
+  return e;
+}
+
+}  // namespace fa

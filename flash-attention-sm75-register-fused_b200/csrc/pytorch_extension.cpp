@@ -1,0 +1,141 @@
+// pybind module `flash_attn_sm75_cuda` — the reference's L3 binding
+// (src/bindings/pytorch_extension.cpp:1-129) re-implemented over the C ABI in
+// include/fa_b200.h.  Same four exported functions with the same argument
+// lists and input checks; the kernels run asynchronously on PyTorch's
+// current CUDA stream instead of the legacy stream + cudaDeviceSynchronize.
+//
+// Additions: native GQA (K/V may have fewer heads than Q), bf16 inputs,
+// flash_attention_forward_lse returning (O, LSE), and diagnostics.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "fa_b200.h"
+
+namespace {
+
+void check_tensor(const torch::Tensor& t, const char* name, bool allow_bf16) {
+  TORCH_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
+  if (allow_bf16) {
+    TORCH_CHECK(t.dtype() == torch::kFloat16 || t.dtype() == torch::kBFloat16,
+                std::string(name) + " must be FP16 or BF16");
+  } else {
+    TORCH_CHECK(t.dtype() == torch::kFloat16, std::string(name) + " must be FP16");
+  }
+  TORCH_CHECK(t.is_contiguous(), std::string(name) + " must be contiguous");
+  TORCH_CHECK(t.dim() == 4, std::string(name) + " must be [B, H, N, D]");
+}
+
+void* stream_of(const torch::Tensor& t) {
+  return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+std::tuple<torch::Tensor, torch::Tensor> fwd_impl(const torch::Tensor& Q, const torch::Tensor& K,
+                                                  const torch::Tensor& V, bool causal, float scale,
+                                                  bool want_lse) {
+  check_tensor(Q, "Q", true);
+  check_tensor(K, "K", true);
+  check_tensor(V, "V", true);
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype(), "Q, K, V must share a dtype");
+  TORCH_CHECK(Q.device() == K.device() && Q.device() == V.device(),
+              "Q, K, V must be on the same device");
+  TORCH_CHECK(Q.size(0) == K.size(0), "batch mismatch");
+  TORCH_CHECK(Q.size(2) == K.size(2), "seq_len mismatch");
+  TORCH_CHECK(Q.size(3) == K.size(3), "head_dim mismatch");
+  TORCH_CHECK(K.sizes() == V.sizes(), "K and V must have identical shapes");
+  const auto head_dim = Q.size(3);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && Q.size(1) <= INT32_MAX && Q.size(2) <= INT32_MAX,
+              "size exceeds int32");
+
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::empty_like(Q);
+  torch::Tensor lse;
+  if (want_lse)
+    lse = torch::empty({Q.size(0), Q.size(1), Q.size(2)},
+                       Q.options().dtype(torch::kFloat32));
+  const int rc = fa_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                        want_lse ? lse.data_ptr<float>() : nullptr, static_cast<int>(Q.size(0)),
+                        static_cast<int>(Q.size(1)), static_cast<int>(K.size(1)),
+                        static_cast<int>(Q.size(2)), static_cast<int>(head_dim), scale,
+                        causal ? 1 : 0,
+                        Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16,
+                        stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_forward: ", fa_error_string(rc));
+  return {O, lse};
+}
+
+torch::Tensor flash_attention_forward(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                      bool causal, float scale) {
+  return std::get<0>(fwd_impl(Q, K, V, causal, scale, false));
+}
+
+std::tuple<torch::Tensor, torch::Tensor> flash_attention_forward_lse(torch::Tensor Q,
+                                                                     torch::Tensor K,
+                                                                     torch::Tensor V, bool causal,
+                                                                     float scale) {
+  return fwd_impl(Q, K, V, causal, scale, true);
+}
+
+// Reference ablation exports (d=64, identical shapes): one kernel serves all.
+torch::Tensor d64_variant(const char* what, torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                          bool causal, float scale) {
+  check_tensor(Q, "Q", false);
+  check_tensor(K, "K", false);
+  check_tensor(V, "V", false);
+  TORCH_CHECK(Q.sizes() == K.sizes() && Q.sizes() == V.sizes(),
+              "Q, K, V must have identical shapes");
+  TORCH_CHECK(Q.size(3) == 64, std::string(what) + " kernel supports head_dim=64 only");
+  return flash_attention_forward(Q, K, V, causal, scale);
+}
+
+torch::Tensor flash_attention_forward_scalar(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                             bool causal, float scale) {
+  return d64_variant("scalar", Q, K, V, causal, scale);
+}
+
+torch::Tensor flash_attention_forward_wmma_qk(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                              bool causal, float scale) {
+  return d64_variant("wmma_qk", Q, K, V, causal, scale);
+}
+
+torch::Tensor naive_attention_forward(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                      bool causal, float scale) {
+  check_tensor(Q, "Q", false);
+  check_tensor(K, "K", false);
+  check_tensor(V, "V", false);
+  TORCH_CHECK(Q.sizes() == K.sizes() && Q.sizes() == V.sizes(),
+              "naive_attention: Q, K, V must have identical shapes");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::empty_like(Q);
+  auto ws = torch::empty({Q.size(0) * Q.size(1), Q.size(2), Q.size(2)},
+                         Q.options().dtype(torch::kFloat32));
+  const int rc = fa_naive_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                              static_cast<int>(Q.size(0)), static_cast<int>(Q.size(1)),
+                              static_cast<int>(Q.size(2)), static_cast<int>(Q.size(3)), scale,
+                              causal ? 1 : 0, ws.data_ptr<float>(), stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "naive_attention_forward: ", fa_error_string(rc));
+  return O;
+}
+
+int device_status(bool reset) { return fa_device_status(reset ? 1 : 0); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("naive_attention_forward", &naive_attention_forward);
+  m.def("flash_attention_forward", &flash_attention_forward);
+  m.def("flash_attention_forward_scalar", &flash_attention_forward_scalar);
+  m.def("flash_attention_forward_wmma_qk", &flash_attention_forward_wmma_qk);
+  m.def("flash_attention_forward_lse", &flash_attention_forward_lse,
+        "Returns (O, LSE) with LSE fp32 [B, Hq, N]");
+  m.def("device_status", &device_status, pybind11::arg("reset") = false,
+        "Error code recorded by the in-kernel watchdog (0 = none)");
+  m.def("set_watchdog_ns", &fa_set_watchdog_ns);
+  m.def("set_debug_flags", &fa_set_debug_flags);
+  m.def("smem_bytes", &fa_smem_bytes);
+  m.def("version", []() { return std::string(fa_version()); });
+}

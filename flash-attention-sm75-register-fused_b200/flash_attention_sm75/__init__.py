@@ -1,0 +1,10 @@
+"""B200 (sm_100a) FlashAttention forward behind the reference's Python API.
+
+Same public surface as the reference package
+(src/flash_attention_sm75/__init__.py:1-4): ``flash_attention_forward`` and
+``__version__``.
+"""
+from .ops import flash_attention_forward
+
+__version__ = "0.1.0"
+__all__ = ["flash_attention_forward"]

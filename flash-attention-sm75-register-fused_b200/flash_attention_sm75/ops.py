@@ -1,0 +1,106 @@
+"""Python entry point of the attention forward (reference src/flash_attention_sm75/ops.py).
+
+``flash_attention_forward(Q, K, V, causal=False, scale=None)`` keeps the
+reference's signature, argument checks and error types:
+
+* ``ValueError`` if Q is not 4-D (ops.py:70-71);
+* ``RuntimeError`` containing "supports head_dim=64 or 128" (ops.py:74-77);
+* ``RuntimeError`` "GQA expansion: Q heads (..) not divisible by K/V heads (..)"
+  (ops.py:19-22);
+* backward raises ``NotImplementedError`` (ops.py:47-52).
+
+Differences that a caller can observe only as speed or as extra options:
+
+* GQA/MQA is served natively: query head ``h`` reads KV head ``h // (Hq/Hkv)``
+  inside the kernel — the same mapping as the reference's ``repeat_interleave``
+  expansion (ops.py:24-26) — so K/V are never copied.
+* bf16 inputs are accepted in addition to fp16.
+* ``return_lse=True`` also returns the fp32 log-sum-exp ``[B, Hq, N]``.
+
+There is no CPU path: the CUDA extension must load, or the import fails.
+"""
+import math
+
+import torch
+
+import flash_attn_sm75_cuda as _C
+
+
+def _expand_kv_for_gqa(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor):
+    """Reference-compatible helper (ops.py:6-27): K/V repeated to Q's head count.
+
+    Kept for callers that import it; ``flash_attention_forward`` itself does
+    not use it, because the kernel maps heads without copying.
+    """
+    h_q = Q.size(1)
+    h_kv = K.size(1)
+    if h_q == h_kv:
+        return K, V
+    _check_gqa(h_q, h_kv)
+    factor = h_q // h_kv
+    K = K.repeat_interleave(factor, dim=1).contiguous()
+    V = V.repeat_interleave(factor, dim=1).contiguous()
+    return K, V
+
+
+def _check_gqa(h_q: int, h_kv: int) -> None:
+    if h_kv == 0 or h_q % h_kv != 0:
+        raise RuntimeError(
+            f"GQA expansion: Q heads ({h_q}) not divisible by K/V heads ({h_kv})"
+        )
+
+
+class FlashAttentionSM75Function(torch.autograd.Function):
+    """Autograd wrapper (reference ops.py:30-52); forward only."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, causal, scale, return_lse=False):
+        _check_gqa(Q.size(1), K.size(1))
+        Q = Q.contiguous()
+        K = K.contiguous()
+        V = V.contiguous()
+        if return_lse:
+            out, lse = _C.flash_attention_forward_lse(Q, K, V, bool(causal), float(scale))
+            ctx.mark_non_differentiable(lse)
+            ctx.save_for_backward(Q, K, V, out)
+            return out, lse
+        out = _C.flash_attention_forward(Q, K, V, bool(causal), float(scale))
+        ctx.save_for_backward(Q, K, V, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, *grad_outputs):
+        raise NotImplementedError(
+            "Backward pass not implemented. "
+            "flash-attention-sm75 is for inference only "
+            "(Backward pass is not implemented for this forward-only kernel)."
+        )
+
+
+def flash_attention_forward(Q, K, V, causal=False, scale=None, return_lse=False):
+    """Drop-in for ``F.scaled_dot_product_attention`` (forward) on B200.
+
+    Args:
+        Q: [B, H_q,  N, D]  float16 / bfloat16, cuda
+        K: [B, H_kv, N, D]  same dtype, H_kv divides H_q
+        V: [B, H_kv, N, D]  same dtype
+        causal: bool — top-left causal mask (query i sees keys j <= i)
+        scale:  float (default 1/sqrt(D))
+        return_lse: also return LSE [B, H_q, N] fp32 (natural log)
+
+    Returns:
+        O: [B, H_q, N, D] (and LSE when ``return_lse``)
+    """
+    if Q.dim() != 4:
+        raise ValueError("Q must be 4D [B, H, N, D]")
+
+    head_dim = Q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+
+    return FlashAttentionSM75Function.apply(Q, K, V, causal, scale, return_lse)

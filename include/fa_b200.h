@@ -1,0 +1,121 @@
+/*
+ * fa_b200.h — C ABI of the B200 (sm_100a) FlashAttention forward.
+ *
+ * Drop-in boundary for the reference's attention-forward path
+ * (JohnScheuer/flash-attention-sm75-register-fused).  Every entry point takes
+ * plain device pointers and sizes; no framework types cross this boundary.
+ *
+ * Layout (all entry points): Q [B, Hq, N, d], K/V [B, Hkv, N, d], O like Q,
+ * row-major and contiguous, f16 (or bf16 where a dtype argument exists).
+ * LSE (optional) is fp32 [B, Hq, N], natural log:  LSE = log sum_j exp(s_ij).
+ * Causal masking is top-left aligned: query i attends keys j <= i.
+ * GQA: query head h reads KV head h / (Hq / Hkv) (repeat_interleave order).
+ *
+ * Pointer arguments are typed void* here; the reference declares the legacy
+ * launchers with `half*`, which is the same C ABI, so the reference binding
+ * (src/bindings/pytorch_extension.cpp:4-19) links against this library as is.
+ */
+#ifndef FA_B200_H
+#define FA_B200_H
+
+#include <stdbool.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes returned by the int-returning entry points ---- */
+enum {
+  FA_OK = 0,
+  FA_ERR_INVALID_ARG = 1,          /* null pointer, negative size, bad causal/dtype flag */
+  FA_ERR_UNSUPPORTED_HEAD_DIM = 2, /* head_dim not in {64, 128} */
+  FA_ERR_GQA_DIVISIBILITY = 3,     /* Hq % Hkv != 0 */
+  FA_ERR_ALIGNMENT = 4,            /* a pointer is not 16-byte aligned */
+  FA_ERR_DTYPE = 5,                /* dtype not FA_DTYPE_F16 / FA_DTYPE_BF16 */
+  FA_ERR_TENSOR_MAP = 6,           /* cuTensorMapEncodeTiled rejected a shape */
+  FA_ERR_LAUNCH = 7,               /* kernel launch failed (see cudaGetLastError) */
+  FA_ERR_DEVICE = 8,               /* current device is not sm_100 */
+  FA_ERR_CUDA = 9,                 /* another CUDA runtime call failed */
+  FA_ERR_TOO_LARGE = 10,           /* a size overflows the kernel's index types */
+  FA_ERR_TIMEOUT_BASE = 100        /* device watchdog: 100 + wait site id */
+};
+
+enum { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1 };
+
+/* Test hooks (fa_set_debug_flags). */
+enum { FA_DEBUG_SKIP_Q_LOAD = 1 /* producer never loads Q: the MMA warp's wait must time out */ };
+
+/*
+ * fa_fwd — asynchronous attention forward on `stream` (cudaStream_t; NULL =
+ * legacy default stream).  Returns FA_OK or an FA_ERR_* code; argument errors
+ * are reported before anything is launched.  B == 0, Hq == 0 or N == 0 is a
+ * no-op.  `lse` may be NULL.
+ *
+ * Replaces: launch_flash_attention_forward
+ *   (reference src/kernels/flash_attention_forward.cu:795-817) with native
+ *   GQA (reference expands K/V in src/flash_attention_sm75/ops.py:6-27),
+ *   an LSE output, bf16, a caller stream and an error code.
+ */
+int fa_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+           int Hkv, int N, int head_dim, float scale, int causal, int dtype, void* stream);
+
+/* ---- reference-compatible launchers (void, fp16, blocking) ----
+ * Same signatures and conventions as the reference: errors are printed to
+ * stderr, the work runs on the legacy default stream and the call ends with
+ * cudaDeviceSynchronize(). */
+
+/* reference src/kernels/flash_attention_forward.cu:795-817 */
+void launch_flash_attention_forward(const void* Q, const void* K, const void* V, void* O,
+                                    int batch, int heads, int seq_len, int head_dim, float scale,
+                                    bool causal);
+/* reference src/kernels/flash_attention_forward.cu:819-833 (d=64 only) */
+void launch_flash_attention_forward_scalar(const void* Q, const void* K, const void* V, void* O,
+                                           int batch, int heads, int seq_len, int head_dim,
+                                           float scale, bool causal);
+/* reference src/kernels/flash_attention_forward.cu:835-849 (d=64 only) */
+void launch_flash_attention_forward_wmma_qk(const void* Q, const void* K, const void* V, void* O,
+                                            int batch, int heads, int seq_len, int head_dim,
+                                            float scale, bool causal);
+/* reference src/kernels/naive_attention.cu:115-164; workspace holds
+ * batch*heads*seq_len*seq_len floats (the materialised score matrix). */
+void launch_naive_attention(const void* Q, const void* K, const void* V, void* O, int batch,
+                            int heads, int seq_len, int head_dim, float scale, bool causal,
+                            float* workspace);
+
+/* Stream-ordered form of launch_naive_attention used by the Python binding
+ * (same math, no device synchronisation, returns a status code). */
+int fa_naive_fwd(const void* Q, const void* K, const void* V, void* O, int batch, int heads,
+                 int seq_len, int head_dim, float scale, int causal, float* workspace,
+                 void* stream);
+
+/* ---- standalone-kernel launchers ----
+ * reference flash-attention-sm75-fused/src/flash_mha_flatargs.cu:231-252
+ * (full attention, d = 64).  Asynchronous on `stream`. */
+int flatargs_launch(const void* Q, const void* K, const void* V, void* O, int B, int H, int N,
+                    float scale, void* stream);
+/* reference flash-attention-sm75-fused/src/flash_mha_v2.cu:366-392
+ * (d = 64; mode 0 = FULL, 1 = CAUSAL).  Asynchronous on `stream`. */
+int launch_v2(const void* Q, const void* K, const void* V, void* O, int B, int H, int N,
+              float scale, int mode, void* stream);
+
+/* ---- diagnostics ---- */
+/* Error code recorded by the device watchdog on the current device (0 if
+ * none); `reset` clears it.  Synchronous (reads device memory). */
+int fa_device_status(int reset);
+/* Watchdog deadline for every in-kernel wait, in ns (default 1e9). */
+void fa_set_watchdog_ns(unsigned long long ns);
+/* FA_DEBUG_* bits applied to subsequent launches (tests only; default 0). */
+void fa_set_debug_flags(int flags);
+/* Human-readable text for a status code. */
+const char* fa_error_string(int code);
+/* Dynamic shared memory one CTA of the kernel uses for this head_dim. */
+int fa_smem_bytes(int head_dim);
+/* Library version string. */
+const char* fa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H */
