@@ -151,6 +151,90 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// Fraction of exponentials evaluated by the FMA-pipe polynomial instead of
+// the MUFU unit: pair c of every group of kEmuPeriod pairs uses the
+// polynomial when c % kEmuPeriod >= kEmuPeriod - kEmuCount.
+#ifndef FA_EMU_PERIOD
+#define FA_EMU_PERIOD 4
+#endif
+#ifndef FA_EMU_COUNT
+#define FA_EMU_COUNT 1
+#endif
+constexpr int kEmuPeriod = FA_EMU_PERIOD;
+constexpr int kEmuCount = FA_EMU_COUNT;
+
+__device__ __forceinline__ float row_max(const float (&x)[kBlockN]) {
+  float a = x[0], b = x[1], c = x[2], d = x[3];
+#pragma unroll
+  for (int i = 4; i < kBlockN; i += 4) {
+    a = fmaxf(a, x[i]);
+    b = fmaxf(b, x[i + 1]);
+    c = fmaxf(c, x[i + 2]);
+    d = fmaxf(d, x[i + 3]);
+  }
+  return fmaxf(fmaxf(a, b), fmaxf(c, d));
+}
+
+__device__ __forceinline__ float row_min(const float (&x)[kBlockN]) {
+  float a = x[0], b = x[1], c = x[2], d = x[3];
+#pragma unroll
+  for (int i = 4; i < kBlockN; i += 4) {
+    a = fminf(a, x[i]);
+    b = fminf(b, x[i + 1]);
+    c = fminf(c, x[i + 2]);
+    d = fminf(d, x[i + 3]);
+  }
+  return fminf(fminf(a, b), fminf(c, d));
+}
+
+__device__ __forceinline__ float row_sum(const float (&x)[kBlockN]) {
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f, d0 = 0.f, d1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kBlockN; i += 8) {
+    ptx::fadd2(a0, a1, a0, a1, x[i], x[i + 1]);
+    ptx::fadd2(b0, b1, b0, b1, x[i + 2], x[i + 3]);
+    ptx::fadd2(c0, c1, c0, c1, x[i + 4], x[i + 5]);
+    ptx::fadd2(d0, d1, d0, d1, x[i + 6], x[i + 7]);
+  }
+  ptx::fadd2(a0, a1, a0, a1, b0, b1);
+  ptx::fadd2(c0, c1, c0, c1, d0, d1);
+  ptx::fadd2(a0, a1, a0, a1, c0, c1);
+  return a0 + a1;
+}
+
+// exp2(x * sl - m) for the 128 scores of this thread's row; the packed
+// f16/bf16 values go to TMEM (P operand of the PV MMA) in two 32-column halves;
+// returns their fp32 sum.
+template <bool BF16, bool kEmulate>
+__device__ __forceinline__ float exp_tile(float (&x)[kBlockN], float sl, float neg_m,
+                                          uint32_t tP) {
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const int i = 64 * h + 2 * c;
+      float t0, t1, e0, e1;
+      ptx::ffma2(t0, t1, x[i], x[i + 1], sl, sl, neg_m, neg_m);
+      if (kEmulate && (c % kEmuPeriod) >= kEmuPeriod - kEmuCount) {
+        ptx::exp2_poly2(e0, e1, t0, t1);
+      } else {
+        e0 = ptx::ex2_approx(t0);
+        e1 = ptx::ex2_approx(t1);
+      }
+      if (c & 1)
+        ptx::fadd2(b0, b1, b0, b1, e0, e1);
+      else
+        ptx::fadd2(a0, a1, a0, a1, e0, e1);
+      pk[c] = pack2<BF16>(e0, e1);
+    }
+    ptx::tmem_st32(tP + 32 * h, pk);
+  }
+  ptx::fadd2(a0, a1, a0, a1, b0, b1);
+  return a0 + a1;
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_constant__ FwdParams p) {
   using L = Layout<D>;
@@ -306,7 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           ptx::mma_commit(bar(L::kBarO));
           if (j + 1 < n_kv[0]) {
             if (!(ok = bar_wait(bar(L::kBarK + s1), ph1, wc, 14))) break;
-            if (L::kAliasP && !(ok = bar_wait(bar(L::kBarO), j & 1, wc, 15))) break;
             issue_s(0, s1);
             ptx::mma_commit(bar(L::kBarS));
           }
@@ -320,7 +403,6 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         ptx::mma_commit(bar(L::kBarEmpty + s));
         if (j + 1 < n_kv[1]) {
           if (!(ok = bar_wait(bar(L::kBarK + s1), ph1, wc, 17))) break;
-          if (L::kAliasP && !(ok = bar_wait(bar(L::kBarO + 1), j & 1, wc, 18))) break;
           issue_s(1, s1);
           ptx::mma_commit(bar(L::kBarS + 1));
         }
@@ -365,33 +447,37 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         pin_after_wait<32>(u3);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          x[c] = __uint_as_float(u0[c]) * sl;
-          x[32 + c] = __uint_as_float(u1[c]) * sl;
-          x[64 + c] = __uint_as_float(u2[c]) * sl;
-          x[96 + c] = __uint_as_float(u3[c]) * sl;
+          x[c] = __uint_as_float(u0[c]);
+          x[32 + c] = __uint_as_float(u1[c]);
+          x[64 + c] = __uint_as_float(u2[c]);
+          x[96 + c] = __uint_as_float(u3[c]);
         }
       }
 
       const int key0 = j * kBlockN;
-      const bool diag = p.causal && (j == tile);
-      const bool ragged = key0 + kBlockN > p.N;
-      if (diag || ragged) {
+      const bool masked = (p.causal && j == tile) || (key0 + kBlockN > p.N);
+      // Scaled tile maximum.  Unmasked tiles reduce the raw scores and scale
+      // once (the exponent then folds scale and max into one packed FMA);
+      // masked tiles are pre-scaled so that -inf marks excluded keys.
+      float m_tile;
+      float sl_eff = sl;
+      if (masked) {
         int lim = p.N - key0;
-        if (diag) lim = min(lim, r + 1);
+        if (p.causal && j == tile) lim = min(lim, r + 1);
+#pragma unroll
+        for (int c = 0; c < kBlockN; c += 2) ptx::fmul2(x[c], x[c + 1], x[c], x[c + 1], sl, sl);
 #pragma unroll
         for (int c = 0; c < kBlockN; ++c)
           if (c >= lim) x[c] = -INFINITY;
+        m_tile = row_max(x);
+        sl_eff = 1.0f;
+      } else if (sl >= 0.f) {
+        m_tile = row_max(x) * sl;
+      } else {
+        m_tile = row_min(x) * sl;
       }
 
-      float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
-#pragma unroll
-      for (int c = 4; c < kBlockN; c += 4) {
-        mx0 = fmaxf(mx0, x[c]);
-        mx1 = fmaxf(mx1, x[c + 1]);
-        mx2 = fmaxf(mx2, x[c + 2]);
-        mx3 = fmaxf(mx3, x[c + 3]);
-      }
-      const float m_new = fmaxf(m, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+      const float m_new = fmaxf(m, m_tile);
       const bool grow = m_new > m + kRescaleThreshold;
       if (j == 0) {
         m = m_new;
@@ -400,41 +486,36 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         // signalled) and is not written again until this group arrives on P.
         if (__any_sync(0xffffffffu, grow)) {
           const float alpha = grow ? ptx::ex2_approx(m - m_new) : 1.0f;
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            ptx::tmem_ld32(tO + c * 32, o);
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t o[16];
+            ptx::tmem_ld16(tO + c * 16, o);
             ptx::tmem_wait_ld();
-            pin_after_wait<32>(o);
+            pin_after_wait<16>(o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            ptx::tmem_st32(tO + c * 32, o);
+            for (int i = 0; i < 16; i += 2) {
+              float a0 = __uint_as_float(o[i]), a1 = __uint_as_float(o[i + 1]);
+              ptx::fmul2(a0, a1, a0, a1, alpha, alpha);
+              o[i] = __float_as_uint(a0);
+              o[i + 1] = __float_as_uint(a1);
+            }
+            ptx::tmem_st16(tO + c * 16, o);
           }
           ptx::tmem_wait_st();
           if (grow) l *= alpha;
         }
         if (grow) m = m_new;
       }
-      const float m_use = (m == -INFINITY) ? 0.f : m;
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
 
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float e0 = ptx::ex2_approx(x[64 * h + 2 * c] - m_use);
-          const float e1 = ptx::ex2_approx(x[64 * h + 2 * c + 1] - m_use);
-          s0 += e0;
-          s1 += e1;
-          pk[c] = pack2<BF16>(e0, e1);
-        }
-        ptx::tmem_st32(tP + 32 * h, pk);
-      }
-      l += s0 + s1;
+      // P = exp2(x * sl_eff - m): packed FMA, then exp2 split between the MUFU
+      // unit and a polynomial on the FMA pipe; written to TMEM in two halves.
+      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP)
+                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(L::kBarP + g));
+      l += tile_sum;
     }
 
     // ---- epilogue: O / l -> global, LSE

@@ -170,6 +170,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -198,6 +208,64 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32x2 arithmetic (sm_100): one instruction, two lanes of work.
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+// (d0, d1) = (a0*b0 + c0, a1*b1 + c1), round-to-nearest
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(pack_f2(a0, a1)), "l"(pack_f2(b0, b1)), "l"(pack_f2(c0, c1)));
+  unpack_f2(d, d0, d1);
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a0, a1)), "l"(pack_f2(b0, b1)));
+  unpack_f2(d, d0, d1);
+}
+__device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a0, a1)), "l"(pack_f2(b0, b1)));
+  unpack_f2(d, d0, d1);
+}
+
+// 2^t for two lanes on the FMA pipe (no MUFU), t <= 64.
+// Method: t = n + f with n = round-to-nearest(t) obtained by adding and
+// subtracting 1.5*2^23 (the addition leaves n in the low mantissa bits),
+// f in [-0.5, 0.5]; 2^f from a degree-4 polynomial fitted here by a Remez
+// exchange for minimum relative error on [-0.5, 0.5] (max rel. error
+// 2.7e-6 evaluated in fp32 Horner form); 2^n applied by adding n to the
+// exponent field.  t is clamped at -127 so the exponent never wraps; results
+// below 2^-126 come out as tiny denormals instead of exact zeros.
+__device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float t0, float t1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.9999992847442627f, c1 = 0.6931217908859253f, c2 = 0.240247443318367f,
+                  c3 = 0.05591785907745361f, c4 = 0.009570102207362652f;
+  t0 = fmaxf(t0, -127.0f);
+  t1 = fmaxf(t1, -127.0f);
+  float j0, j1, n0, n1, f0, f1;
+  fadd2(j0, j1, t0, t1, kRound, kRound);
+  fadd2(n0, n1, j0, j1, -kRound, -kRound);
+  ffma2(f0, f1, n0, n1, -1.0f, -1.0f, t0, t1);
+  float p0, p1;
+  ffma2(p0, p1, c4, c4, f0, f1, c3, c3);
+  ffma2(p0, p1, p0, p1, f0, f1, c2, c2);
+  ffma2(p0, p1, p0, p1, f0, f1, c1, c1);
+  ffma2(p0, p1, p0, p1, f0, f1, c0, c0);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(j0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(j1) << 23));
 }
 
 // ---------------------------------------------------------------- descriptors

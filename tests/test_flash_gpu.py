@@ -130,8 +130,10 @@ def test_full_size_properties(sm100):
     v = v.cuda()
     o1, l1 = run(q, k, v, False)
     o2, l2 = run(q, k[:, :, perm].contiguous(), v[:, :, perm].contiguous(), False)
-    assert (o1.float() - o2.float()).abs().max().item() <= 2e-3
-    assert (l1 - l2).abs().max().item() <= 1e-4
+    # both are kernel outputs, each within the tolerance of the exact value
+    diff = (o1.float() - o2.float()).abs()
+    assert (diff <= 2 * (2e-3 + 1e-2 * o1.float().abs())).all(), diff.max().item()
+    assert (l1 - l2).abs().max().item() <= 2e-4
 
 
 def test_causal_row0_is_v0(sm100):
