@@ -1,0 +1,426 @@
+"""Attention-forward benchmark (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c5] [--dtype f16|bf16] [--no-extras]
+
+Metric: attention-forward TFLOPS, FLOPs = 4*B*H*N^2*d (halved
+for causal, the reference's convention), whole-job aggregate over N GPUs.
+Default workload: configuration C5 full — B=4, H=32, N=8192, d=128, fp16,
+1 % of K rows scaled x8 — the shape the north-star target is quoted on; it
+fits one GPU.  Multi-GPU (torchrun, one rank per GPU): weak scaling, each
+rank owns its own B=4 slice of a global batch of 4*N; (batch, head) units are
+independent, so no collective touches the data path (NCCL only takes the max
+of the per-rank times).
+
+A step is one attention forward over the rank's batch, inputs resident in
+HBM (1.07 GB per step read+written, larger than the 126 MB L2, so no L2 flush
+is needed between steps).  `e2e` times the same forward through the public
+Python API with the step's Q/K/V copied from pinned host memory and O copied
+back inside the timed region.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "flash-attention-sm75-register-fused_b200")
+for _p in (REPO, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "attn fwd TFLOPS/GPU (causal-halved) at 1/2/4/8 B200; % of tensor peak"
+FALLBACK_PEAK_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIG_TEXT = {
+    "c1": "C1 full attention B=1 H=1 N=512 d=64",
+    "c2": "C2 full attention B=4 H=12 N=1024 d=64",
+    "c3": "C3 causal attention B=4 H=8 N=2048 d=64 (inputs x0.5)",
+    "c4": "C4 GQA causal B=2 Hq=32 Hkv=8 N=4096 d=128",
+    "c5": "C5 full attention B=4 H=32 N=8192 d=128 (1% K rows x8)",
+    "c5c": "C5 causal attention B=4 H=32 N=8192 d=128 (1% K rows x8)",
+}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIG_TEXT))
+    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip e2e, cpu_baseline and the per-config table (profiling runs)")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic(config):
+    """DRAM bytes per launch of the kernel for `config`, from the committed ncu
+    summary (profiles/fa_fwd_traffic.txt, lines `config: bytes`), or None."""
+    path = os.path.join(REPO, "profiles", "fa_fwd_traffic.txt")
+    try:
+        for line in open(path):
+            line = line.strip()
+            if line.startswith(config + ":"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU during the timed region
+    (NVML; `nvidia-smi` as fallback)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index, period=0.02):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+
+    def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._nvml = (pynvml, h)
+        except Exception:
+            self._nvml = None
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+
+    def _sample(self):
+        if self._nvml:
+            pynvml, h = self._nvml
+            mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+            try:
+                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception:
+                rs = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+            return mhz, rs
+        out = subprocess.run(
+            ["nvidia-smi", f"--id={self.index}", "--query-gpu=clocks.sm,clocks.max.sm,"
+             "clocks_event_reasons.active", "--format=csv,noheader,nounits"],
+            capture_output=True, text=True, timeout=5).stdout.strip().split(",")
+        self.max_mhz = float(out[1])
+        return float(out[0]), int(out[2].strip(), 16)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz, rs = self._sample()
+                self.samples.append(mhz)
+                self.reasons |= int(rs)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def stop(self):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=5)
+        reasons = [n for bit, n in self.REASONS.items() if self.reasons & bit and bit != 0x1]
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "samples": len(self.samples),
+            "reasons": reasons,
+        }
+
+
+# ----------------------------------------------------------------- inputs
+def make_device_inputs(cfg, b0, b1, dtype, device, seed=42):
+    """Seeded synthetic inputs for global batch entries [b0, b1): per entry a
+    CUDA generator seeded from (seed, b) draws Q, K, V ~ N(0,1) (times the
+    config's input scale), then K rows ``randperm(N)[:frac*N]`` per head x8."""
+    import torch
+    qs, ks, vs = [], [], []
+    for b in range(b0, b1):
+        g = torch.Generator(device=device).manual_seed(seed * 1_000_003 + b)
+        q = torch.randn(1, cfg.Hq, cfg.N, cfg.d, generator=g, device=device)
+        k = torch.randn(1, cfg.Hkv, cfg.N, cfg.d, generator=g, device=device)
+        v = torch.randn(1, cfg.Hkv, cfg.N, cfg.d, generator=g, device=device)
+        if cfg.input_scale != 1.0:
+            q *= cfg.input_scale
+            k *= cfg.input_scale
+            v *= cfg.input_scale
+        n_out = int(cfg.N * cfg.k_outlier_frac)
+        for h in range(cfg.Hkv if n_out else 0):
+            idx = torch.randperm(cfg.N, generator=g, device=device)[:n_out]
+            k[0, h, idx] *= cfg.k_outlier_scale
+        qs.append(q.to(dtype))
+        ks.append(k.to(dtype))
+        vs.append(v.to(dtype))
+    return torch.cat(qs).contiguous(), torch.cat(ks).contiguous(), torch.cat(vs).contiguous()
+
+
+# ----------------------------------------------------------------- CPU legs
+def cpu_sample(cfg, budget_s=8.0, seed=42):
+    """Times the CPU oracle (the reference's fp32 attention restated,
+    oracle/attention_oracle.py) with all host threads on (b, h) slices of the
+    workload: each slice is one query head with 512 of its query rows against
+    all N keys.  Returns (flops, seconds, cores, slices, rows per slice)."""
+    import torch
+    from oracle import attention_oracle as orc
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rows_n = min(512, cfg.N)
+    g = torch.Generator().manual_seed(seed)
+    flops, secs, slices = 0.0, 0.0, 0
+    while secs < budget_s:
+        q = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+        k = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+        v = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+        rows = torch.randperm(cfg.N, generator=g)[:rows_n].sort().values
+        t1 = time.perf_counter()
+        orc.attention_fp32(q, k, v, causal=cfg.causal, rows=rows)
+        secs += time.perf_counter() - t1
+        flops += (float(4.0 * cfg.d * (rows + 1).sum().item()) if cfg.causal
+                  else 4.0 * rows_n * cfg.N * cfg.d)
+        slices += 1
+    return flops, secs, cores, slices, rows_n
+
+
+def run_reference(args, cfg):
+    """--impl reference: the reference's CPU path (the oracle port) on the host
+    cores, on this arm's metric and config; each step is a bounded sample."""
+    import torch
+    from oracle import attention_oracle as orc
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rows_n = min(256, cfg.N)
+    g = torch.Generator().manual_seed(42)
+    q = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+    k = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+    v = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+    rows = torch.randperm(cfg.N, generator=g)[:rows_n].sort().values
+    step_flops = (float(4.0 * cfg.d * (rows + 1).sum().item()) if cfg.causal
+                  else 4.0 * rows_n * cfg.N * cfg.d)
+    for _ in range(args.warmup):
+        orc.attention_fp32(q, k, v, causal=cfg.causal, rows=rows)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.attention_fp32(q, k, v, causal=cfg.causal, rows=rows)
+    dt = time.perf_counter() - t0
+    tflops = step_flops * args.steps / dt / 1e12
+    sample = (f"per step: one (b,h) slice of {cfg.name}, {rows_n} query rows x {cfg.N} keys, "
+              f"d={cfg.d}, fp32 torch CPU oracle")
+    line = {
+        "metric": METRIC, "value": tflops, "unit": "TFLOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": CONFIG_TEXT[cfg.name], "B": cfg.B, "Hq": cfg.Hq, "Hkv": cfg.Hkv,
+                   "N": cfg.N, "d": cfg.d, "causal": cfg.causal},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOPS", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tflops, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU arm
+def time_steps(fn, steps, stream):
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def main():
+    args = parse_args()
+    rank, world, local_rank = dist_env()
+    from oracle import attention_oracle as orc  # config table and CPU legs only
+    cfg = orc.CONFIGS[args.config]
+
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import flash_attn_sm75_cuda as _C
+    from flash_attention_sm75 import flash_attention_forward
+    from flash_attention_sm75.sharding import batch_range
+    from flash_attention_sm75 import capi as abi
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    b0, b1 = batch_range(cfg.B, rank)
+    q, k, v = make_device_inputs(cfg, b0, b1, dtype, dev)
+    o = torch.empty_like(q)
+    lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    scale = 1.0 / math.sqrt(cfg.d)
+    dt_code = 1 if dtype == torch.bfloat16 else 0
+    lib = abi.load()
+    qp, kp, vp, op, lp, sp = (abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), abi.ptr(lse),
+                              abi.stream_ptr(stream))
+
+    def step():
+        rc = lib.fa_fwd(qp, kp, vp, op, lp, cfg.B, cfg.Hq, cfg.Hkv, cfg.N, cfg.d, scale,
+                        int(cfg.causal), dt_code, sp)
+        if rc != 0:
+            raise RuntimeError(lib.fa_error_string(rc).decode())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    ms = time_steps(step, args.steps, stream)
+    clocks = sampler.stop()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    status = lib.fa_device_status(0)
+    if status != 0:
+        raise RuntimeError(f"device watchdog fired: {lib.fa_error_string(status).decode()}")
+
+    ms_step = ms / args.steps
+    total_flops = cfg.flops * world
+    value = total_flops / (ms_step * 1e-3) / 1e12
+    peak, hbm, peak_kind = load_peaks()
+    per_gpu = value / world
+    traffic = load_traffic(cfg.name)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": args.dtype, "data": "synthetic (seeded N(0,1), 1% K rows x8 for C5)",
+        "config": {"workload": CONFIG_TEXT[cfg.name], "B_per_gpu": cfg.B, "Hq": cfg.Hq,
+                   "Hkv": cfg.Hkv, "N": cfg.N, "d": cfg.d, "causal": cfg.causal,
+                   "global_batch": cfg.B * world, "parallelism": f"dp{world} over (batch, head)",
+                   "l2": "inputs+outputs 1.07 GB/step > 126 MB L2; no flush needed"
+                   if cfg.min_bytes > 126e6 else "L2 not flushed (small config)"},
+        "tflops_per_gpu": per_gpu,
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                     "frac": per_gpu / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
+                     "frac_of_spec_2250": per_gpu / 2250.0,
+                     "traffic": traffic,
+                     "algorithmic_bytes": cfg.min_bytes},
+        "clocks": clocks,
+    }
+
+    if not args.no_extras and rank == 0:
+        line["e2e"] = e2e_leg(cfg, q, k, v, dtype, dev, flash_attention_forward)
+        flops, cpu_s, cores, slices, rows_n = cpu_sample(cfg)
+        line["cpu_baseline"] = {
+            "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
+            "sample": f"{slices} (b,h) slices of {cfg.name}, {rows_n} query rows x {cfg.N} keys each, "
+                      f"fp32 torch CPU oracle, {cpu_s:.1f} s"}
+        if world == 1:
+            line["configs"] = other_configs(lib, abi, dtype, dev)
+    elif rank == 0:
+        line["e2e"] = None
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def e2e_leg(cfg, q, k, v, dtype, dev, fwd, steps=5):
+    """Public API end to end: pinned host Q/K/V -> device, forward, O -> pinned host."""
+    import torch
+    hq = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        out = fwd(dq, dk, dv, causal=cfg.causal)
+        ho.copy_(out, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    ms = time_steps(step, steps, stream) / steps
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = ho.numel() * ho.element_size()
+    return {"value": cfg.flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+def other_configs(lib, abi, dtype, dev):
+    """Kernel-only TFLOPS of the other BASELINE configurations (reported, not the headline)."""
+    import torch
+    from oracle import attention_oracle as orc
+    out = {}
+    for name in ("c1", "c2", "c3", "c4", "c5c"):
+        c = orc.CONFIGS[name]
+        q, k, v = make_device_inputs(c, 0, c.B, dtype, dev)
+        o = torch.empty_like(q)
+        lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+        s = torch.cuda.current_stream(dev)
+        args = (abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), abi.ptr(lse), c.B, c.Hq, c.Hkv,
+                c.N, c.d, 1.0 / math.sqrt(c.d), int(c.causal), 1 if dtype == torch.bfloat16 else 0,
+                abi.stream_ptr(s))
+        fn = lambda: lib.fa_fwd(*args)
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        n = max(20, min(2000, int(2e12 / c.flops)))
+        ms = time_steps(fn, n, s) / n
+        out[name] = {"tflops": round(c.flops / ms / 1e9, 1), "us": round(ms * 1e3, 2),
+                     "gbs": round(c.min_bytes / (ms * 1e-3) / 1e9, 1)}
+    return out
+
+
+if __name__ == "__main__":
+    main()

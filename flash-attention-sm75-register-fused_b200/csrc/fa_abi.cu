@@ -21,6 +21,7 @@ namespace {
 std::atomic<unsigned> g_epoch{1};
 std::atomic<unsigned long long> g_timeout_ns{1000000000ull};
 std::atomic<int> g_debug_flags{0};
+std::atomic<long long*> g_trace{nullptr};
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -167,6 +168,7 @@ int fa_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, int
   p.causal = causal;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.debug_flags = g_debug_flags.load(std::memory_order_relaxed);
+  p.trace = g_trace.load(std::memory_order_relaxed);
   p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaError_t e = fa::launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
@@ -273,6 +275,9 @@ int fa_device_status(int reset) {
 void fa_set_watchdog_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1ull); }
 
 void fa_set_debug_flags(int flags) { g_debug_flags.store(flags); }
+
+// Development hook: device buffer for FA_TRACE builds (8*64*16 int64), or NULL.
+void fa_set_trace_buffer(void* buf) { g_trace.store(static_cast<long long*>(buf)); }
 
 const char* fa_error_string(int code) {
   switch (code) {

@@ -23,6 +23,7 @@ struct alignas(64) FwdParams {
   int causal;
   float scale_log2;  // scale * log2(e)
   int debug_flags;
+  long long* trace;  // timeline samples, used only in FA_TRACE builds
   unsigned epoch;    // launch counter, tags device status words
   unsigned long long timeout_ns;
 };

@@ -13,8 +13,9 @@
 // One CTA owns a "Q pair": two 128-row tiles of one (batch, query-head).
 //   warps 0-3  softmax group 0  (rows   0..127 of the pair, one row / thread)
 //   warps 4-7  softmax group 1  (rows 128..255)
-//   warp  8    TMA producer     (Q once, K/V through a kStages ring)
-//   warp  9    MMA issuer       (tcgen05.mma, one thread) + TMEM owner
+//   warp  8    TMA producer     (Q once, K/V tiles through a ring of slots)
+//   warp  9    MMA issuer       (tcgen05.mma from one elected lane) + TMEM owner
+//   warps 10-11 idle (complete the producer warpgroup for setmaxnreg)
 //
 // Tensor memory (512 columns x 128 lanes, lane = query row of a tile):
 //   S_g  = Q_g K_j^T        fp32, 128 columns per group
@@ -48,9 +49,18 @@ namespace {
 
 constexpr int kBlockM = 128;  // query rows per tile (one TMEM lane each)
 constexpr int kBlockN = 128;  // keys per K/V tile
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;   // 3 warpgroups
 constexpr int kWarpLoad = 8;
-constexpr int kWarpMma = 9;
+constexpr int kWarpMma = 9;    // warps 10-11 complete the third warpgroup and idle
+// Register split: launched at kLaunchRegs per thread (65536 / 384 rounded down
+// to a multiple of 8); the producer/MMA warpgroup gives registers to the two
+// softmax warpgroups.  256*kRegsSoftmax + 128*kRegsOther must not exceed
+// 384*kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegsOther = 72;
+static_assert(256 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows > 2^8
 
 template <int D>
@@ -58,17 +68,18 @@ struct Layout {
   static constexpr int kColBlocks = D / 64;       // 128-byte swizzle column blocks
   static constexpr int kBlockBytes = kBlockM * 128;  // one 64-column block of a 128-row tile
   static constexpr int kTile = kBlockM * D * 2;   // bytes of a 128-row f16 tile
-  static constexpr int kStages = (D == 128) ? 2 : 4;
+  // K and V tiles stream through one ring of tile-sized slots in load order
+  // K0 V0 K1 V1 ...; a slot is refilled once the MMAs reading it completed.
+  static constexpr int kSlots = (D == 128) ? 5 : 8;
   // shared memory (offsets from a 1024-aligned base)
   static constexpr int kOffQ = 0;                 // Q0, Q1
-  static constexpr int kOffKV = 2 * kTile;        // stage s: K at +2s*kTile, V at +(2s+1)*kTile
-  static constexpr int kOffBar = kOffKV + kStages * 2 * kTile;
+  static constexpr int kOffKV = 2 * kTile;        // ring slot s at kOffKV + s*kTile
+  static constexpr int kOffBar = kOffKV + kSlots * kTile;
   // barrier indices
   static constexpr int kBarQ = 0;                       // 2
-  static constexpr int kBarK = 2;                       // kStages
-  static constexpr int kBarV = kBarK + kStages;         // kStages
-  static constexpr int kBarEmpty = kBarV + kStages;     // kStages
-  static constexpr int kBarS = kBarEmpty + kStages;     // 2
+  static constexpr int kBarFull = 2;                    // kSlots (TMA tx-count)
+  static constexpr int kBarEmpty = kBarFull + kSlots;   // kSlots (MMA commit)
+  static constexpr int kBarS = kBarEmpty + kSlots;      // 2
   static constexpr int kBarP = kBarS + 2;               // 2
   static constexpr int kBarO = kBarP + 2;               // 2
   static constexpr int kBarDrain = kBarO + 2;           // 1
@@ -88,6 +99,8 @@ struct Layout {
   }
   static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
 };
+
+constexpr uint32_t kSuspendNs = 100000;  // upper bound of one hardware-suspended wait
 
 struct WaitCtl {
   volatile int* abort;        // CTA-wide abort flag in shared memory
@@ -110,16 +123,14 @@ __device__ void record_error(unsigned epoch, int code) {
 __device__ __forceinline__ bool bar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& c,
                                            int site, bool respect_abort) {
   const uint64_t t0 = ptx::global_timer_ns();
-  uint32_t it = 0;
   while (true) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((++it & 15u) == 0u) {
-      if (respect_abort && *c.abort) return false;
-      if (ptx::global_timer_ns() - t0 > c.timeout_ns) {
-        *c.abort = 1;
-        record_error(c.epoch, FA_ERR_TIMEOUT_BASE + site);
-        return false;
-      }
+    // sleeps in hardware until the phase completes or ~kSuspendNs elapse
+    if (ptx::mbar_try_wait_sleep(bar, parity, kSuspendNs)) return true;
+    if (respect_abort && *c.abort) return false;
+    if (ptx::global_timer_ns() - t0 > c.timeout_ns) {
+      *c.abort = 1;
+      record_error(c.epoch, FA_ERR_TIMEOUT_BASE + site);
+      return false;
     }
   }
 }
@@ -150,6 +161,22 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
   }
 }
+
+// Timeline tracing for development builds (-DFA_TRACE): the first
+// kTraceCtas CTAs record clock64() at fixed points of every K/V tile into
+// p.trace[cta][tile][event].  Compiled out otherwise.
+constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 16;
+#ifdef FA_TRACE
+#define FA_TRACE_AT(tile, ev)                                                          \
+  do {                                                                                 \
+    if (p.trace != nullptr && blockIdx.x < kTraceCtas && (tile) < kTraceTiles)         \
+      p.trace[(blockIdx.x * kTraceTiles + (tile)) * kTraceEvents + (ev)] = clock64(); \
+  } while (0)
+#else
+#define FA_TRACE_AT(tile, ev) \
+  do {                        \
+  } while (0)
+#endif
 
 // Fraction of exponentials evaluated by the FMA-pipe polynomial instead of
 // the MUFU unit: pair c of every group of kEmuPeriod pairs uses the
@@ -288,10 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
 
-  if (warp == kWarpLoad) {
+  if (warp >= 8) {
+   // ------------------------------------------------ producer warpgroup
+   ptx::setmaxnreg_dec<kRegsOther>();
+   if (warp == kWarpLoad) {
     // ===================================================== TMA producer
     if (lane == 0) {
       ptx::prefetch_tmap(&p.tm_q);
@@ -309,31 +338,27 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
                            bar(L::kBarQ + g), c * 64, q_row0 + g * kBlockM, bh, pol_q);
       }
+      // ring item i: K of tile i/2 (i even) or V of tile i/2 (i odd)
+      const int n_items = 2 * n_loop;
       int issued = 0;
-      for (int j = 0; j < n_loop; ++j) {
-        const int s = j % L::kStages;
-        if (j >= L::kStages && !bar_wait(bar(L::kBarEmpty + s), ((j / L::kStages) - 1) & 1, wc, 1))
+      for (int i = 0; i < n_items; ++i) {
+        const int slot = i % L::kSlots;
+        if (i >= L::kSlots &&
+            !bar_wait(bar(L::kBarEmpty + slot), ((i / L::kSlots) - 1) & 1, wc, 1))
           break;
-        const uint32_t k_dst = sbase + L::kOffKV + (2 * s) * L::kTile;
-        const uint32_t v_dst = k_dst + L::kTile;
-        ptx::mbar_arrive_expect_tx(bar(L::kBarK + s), L::kTile);
+        const uint32_t dst = sbase + L::kOffKV + slot * L::kTile;
+        const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
+                                  : static_cast<const void*>(&p.tm_k);
+        ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
-          ptx::tma_load_3d(k_dst + c * L::kBlockBytes, &p.tm_k, bar(L::kBarK + s), c * 64,
-                           j * kBlockN, bh_kv, pol_kv);
-        ptx::mbar_arrive_expect_tx(bar(L::kBarV + s), L::kTile);
-#pragma unroll
-        for (int c = 0; c < L::kColBlocks; ++c)
-          ptx::tma_load_3d(v_dst + c * L::kBlockBytes, &p.tm_v, bar(L::kBarV + s), c * 64,
-                           j * kBlockN, bh_kv, pol_kv);
-        issued = j + 1;
+          ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
+                           (i >> 1) * kBlockN, bh_kv, pol_kv);
+        issued = i + 1;
       }
       // Drain: every copy this thread started must land before the CTA exits.
-      for (int j = max(0, issued - L::kStages); j < issued; ++j) {
-        const int s = j % L::kStages;
-        bar_wait(bar(L::kBarK + s), (j / L::kStages) & 1, wc, 2, false);
-        bar_wait(bar(L::kBarV + s), (j / L::kStages) & 1, wc, 2, false);
-      }
+      for (int i = max(0, issued - L::kSlots); i < issued; ++i)
+        bar_wait(bar(L::kBarFull + i % L::kSlots), (i / L::kSlots) & 1, wc, 2, false);
       if (!skip_q) {
         bar_wait(bar(L::kBarQ), 0, wc, 2, false);
         if (has_q1) bar_wait(bar(L::kBarQ + 1), 0, wc, 2, false);
@@ -341,78 +366,121 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     }
   } else if (warp == kWarpMma) {
     // ===================================================== MMA issuer
-    if (lane == 0) {
+    // The whole warp runs this loop so that addresses and descriptors stay
+    // warp-uniform; one elected lane issues each batch of tcgen05 ops.
+    {
       constexpr uint32_t fmt = BF16 ? 1u : 0u;
       constexpr uint32_t idesc_qk = ptx::make_idesc_f16(kBlockM, kBlockN, fmt, 0, 0);
       constexpr uint32_t idesc_pv = ptx::make_idesc_f16(kBlockM, D, fmt, 0, 1);
 
-      auto issue_s = [&](int g, int s) {
-        const uint32_t qa = sbase + L::kOffQ + g * L::kTile;
-        const uint32_t ka = sbase + L::kOffKV + (2 * s) * L::kTile;
+      auto slot_of = [](int item) { return item % L::kSlots; };
+      auto phase_of = [](int item) { return static_cast<uint32_t>((item / L::kSlots) & 1); };
+      // descriptor of the slot-0 K tile (K-major) and V tile (MN-major); a slot
+      // offset is added to the start-address field (16-byte units)
+      const uint64_t k_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16, 1024);
+      const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
+      const uint64_t q_desc[2] = {ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024),
+                                  ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024)};
+      auto issue_s = [&](int g, int j) {
+        const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(2 * j) * L::kTile) >> 4);
+        const uint64_t qd = q_desc[g];
+        if (ptx::elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / 4) * L::kBlockBytes + (kk % 4) * 32;
-          ptx::mma_ss(tmem + L::tS(g), ptx::smem_desc_sw128(qa + off, 16, 1024),
-                      ptx::smem_desc_sw128(ka + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
+            ptx::mma_ss(tmem + L::tS(g), qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          ptx::mma_commit(bar(L::kBarS + g));
         }
+        __syncwarp();
       };
-      auto issue_pv = [&](int g, int s, bool accumulate) {
-        const uint32_t va = sbase + L::kOffKV + (2 * s + 1) * L::kTile;
+      auto issue_pv = [&](int g, int j) {
+        const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(2 * j + 1) * L::kTile) >> 4);
+        if (ptx::elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
-                      ptx::smem_desc_sw128(va + kk * 2048, L::kBlockBytes, 1024), idesc_pv,
-                      (accumulate || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBlockN / 16; ++kk)
+            ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
+                        vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_commit(bar(L::kBarO + g));
         }
+        __syncwarp();
+      };
+      auto commit = [&](uint32_t b) {
+        if (ptx::elect_one()) ptx::mma_commit(b);
+        __syncwarp();
+      };
+      auto wait = [&](uint32_t b, uint32_t ph, int site) {
+        return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
       };
 
-      bool ok = bar_wait(bar(L::kBarQ), 0, wc, 10);
-      if (ok && has_q1) ok = bar_wait(bar(L::kBarQ + 1), 0, wc, 10);
-      if (ok) ok = bar_wait(bar(L::kBarK), 0, wc, 11);
+      // Issue order per tile j (two groups g0, g1 ping-pong on the tensor pipe):
+      //   PV0(j)  S0(j+1)  PV1(j)  S1(j+1)
+      // so each group's softmax overlaps the other group's two MMAs.  S_g(j+1)
+      // may overwrite P_g(j) (d=128): tcgen05.mma ops of one thread execute in
+      // issue order, so PV_g(j) has read P_g(j) before S_g(j+1) writes it.
+      const bool g1 = n_kv[1] > 0;
+      bool ok = wait(bar(L::kBarQ), 0, 10);
+      if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
+      if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
       if (ok) {
         issue_s(0, 0);
-        ptx::mma_commit(bar(L::kBarS));
-        if (n_kv[1] > 0) {
-          issue_s(1, 0);
-          ptx::mma_commit(bar(L::kBarS + 1));
-        }
+        if (g1) issue_s(1, 0);
+        commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
       }
       for (int j = 0; ok && j < n_loop; ++j) {
-        const int s = j % L::kStages;
-        const uint32_t ph = (j / L::kStages) & 1;
-        const int s1 = (j + 1) % L::kStages;
-        const uint32_t ph1 = ((j + 1) / L::kStages) & 1;
-        if (!(ok = bar_wait(bar(L::kBarV + s), ph, wc, 12))) break;
+        const int item_v = 2 * j + 1;
+        const int item_k = 2 * j + 2;  // K of tile j+1
+        if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
+        const bool next0 = j + 1 < n_kv[0];
+        const bool next1 = j + 1 < n_kv[1];
         if (j < n_kv[0]) {
-          if (!(ok = bar_wait(bar(L::kBarP), j & 1, wc, 13))) break;
+          if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
           ptx::tc_fence_after();
-          issue_pv(0, s, j > 0);
-          ptx::mma_commit(bar(L::kBarO));
-          if (j + 1 < n_kv[0]) {
-            if (!(ok = bar_wait(bar(L::kBarK + s1), ph1, wc, 14))) break;
-            issue_s(0, s1);
-            ptx::mma_commit(bar(L::kBarS));
+          if (lane == 0) FA_TRACE_AT(j, 0);
+          issue_pv(0, j);
+          if (next0) {
+            if (!(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14))) break;
+            if (lane == 0) FA_TRACE_AT(j, 1);
+            issue_s(0, j + 1);
+            if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
           }
         }
         if (j < n_kv[1]) {
-          if (!(ok = bar_wait(bar(L::kBarP + 1), j & 1, wc, 16))) break;
+          if (!(ok = wait(bar(L::kBarP + 1), j & 1, 16))) break;
           ptx::tc_fence_after();
-          issue_pv(1, s, j > 0);
-          ptx::mma_commit(bar(L::kBarO + 1));
+          if (lane == 0) FA_TRACE_AT(j, 2);
+          issue_pv(1, j);
         }
-        ptx::mma_commit(bar(L::kBarEmpty + s));
-        if (j + 1 < n_kv[1]) {
-          if (!(ok = bar_wait(bar(L::kBarK + s1), ph1, wc, 17))) break;
-          issue_s(1, s1);
-          ptx::mma_commit(bar(L::kBarS + 1));
+        commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
+        if (next1) {
+          if (!(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 17))) break;
+          if (lane == 0) FA_TRACE_AT(j, 3);
+          issue_s(1, j + 1);
+          commit(bar(L::kBarEmpty + slot_of(item_k)));
         }
       }
       // Drain: all MMAs issued above complete before TMEM is released.
-      ptx::mma_commit(bar(L::kBarDrain));
+      commit(bar(L::kBarDrain));
       bar_wait(bar(L::kBarDrain), 0, wc, 19, false);
+      __syncwarp();
     }
+#ifdef FA_TRACE
+   } else if (lane == 0) {
+    // trace observers: warp 10 (group 0) / 11 (group 1) timestamp the
+    // completion of every S and PV MMA of their group
+    const int og = warp - 10;
+    for (int j = 0; j < n_kv[og]; ++j) {
+      if (!bar_wait(bar(L::kBarS + og), j & 1, wc, 30)) break;
+      FA_TRACE_AT(j, 12 + 2 * og);
+      if (!bar_wait(bar(L::kBarO + og), j & 1, wc, 31)) break;
+      FA_TRACE_AT(j, 13 + 2 * og);
+    }
+#endif
+   }
   } else {
     // ===================================================== softmax groups
+    ptx::setmaxnreg_inc<kRegsSoftmax>();
     const int g = warp >> 2;
     const int n_tiles = n_kv[g];
     const int wq = warp & 3;
@@ -431,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), j & 1, wc, 20 + g));
       if (!ok) break;
+      if (r == 0) FA_TRACE_AT(j, 4 + 4 * g);
       ptx::tc_fence_after();
 
       float x[kBlockN];
@@ -477,6 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         m_tile = row_min(x) * sl;
       }
 
+      if (r == 0) FA_TRACE_AT(j, 5 + 4 * g);
       const float m_new = fmaxf(m, m_tile);
       const bool grow = m_new > m + kRescaleThreshold;
       if (j == 0) {
@@ -514,6 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
                                     : exp_tile<BF16, true>(x, sl_eff, neg_m, tP);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
+      if (r == 0) FA_TRACE_AT(j, 6 + 4 * g);
       ptx::mbar_arrive(bar(L::kBarP + g));
       l += tile_sum;
     }
@@ -570,8 +641,15 @@ static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Layout<D>::kDynBytes);
+    // The setmaxnreg split is only safe if the kernel is launched with exactly
+    // kLaunchRegs registers per thread; anything else is refused.
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads)
+      return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Layout<D>::kDynBytes);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_done[dev] = 1;
   }

@@ -1,0 +1,75 @@
+"""ctypes binding of the C ABI in include/fa_b200.h.
+
+Loads the in-tree ``lib/libfa_b200.so`` and declares every entry point with
+its C signature, so Python callers (tests, bench.py, hosts without the pybind
+module) call the same boundary a C or cgo host would.  Torch is used only to
+obtain device pointers and the current stream in the tensor helpers.
+"""
+import ctypes
+import os
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libfa_b200.so")
+
+c_vp, c_int, c_float, c_bool = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_bool
+
+SIGNATURES = {
+    "fa_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
+                       c_int, c_int, c_vp]),
+    "launch_flash_attention_forward": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
+                                              c_float, c_bool]),
+    "launch_flash_attention_forward_scalar": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
+                                                     c_int, c_float, c_bool]),
+    "launch_flash_attention_forward_wmma_qk": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
+                                                      c_int, c_float, c_bool]),
+    "launch_naive_attention": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float,
+                                      c_bool, c_vp]),
+    "fa_naive_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_int,
+                             c_vp, c_vp]),
+    "flatargs_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_vp]),
+    "launch_v2": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_int, c_vp]),
+    "fa_device_status": (c_int, [c_int]),
+    "fa_set_watchdog_ns": (None, [ctypes.c_ulonglong]),
+    "fa_set_debug_flags": (None, [c_int]),
+    "fa_set_trace_buffer": (None, [c_vp]),
+    "fa_error_string": (ctypes.c_char_p, [c_int]),
+    "fa_smem_bytes": (c_int, [c_int]),
+    "fa_version": (ctypes.c_char_p, []),
+}
+
+_lib = None
+
+
+def load():
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def stream_ptr(torch_stream=None):
+    import torch
+    s = torch_stream or torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def fa_fwd(q, k, v, o, lse=None, causal=False, scale=None, stream=None):
+    """Call fa_fwd on torch CUDA tensors laid out [B, H, N, d]; returns the status."""
+    import math
+    import torch
+    B, Hq, N, d = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    return load().fa_fwd(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), B, Hq, Hkv, N, d,
+                         float(scale), int(bool(causal)), dtype, stream_ptr(stream))

@@ -1,55 +1,13 @@
-"""ctypes view of the C ABI in include/fa_b200.h (test helper).
-
-Loads the in-tree ``lib/libfa_b200.so`` and declares every entry point, so
-that tests call the same boundary a C, cgo or ctypes host would.
-"""
-import ctypes
+"""Test-side view of the C ABI: the package's ctypes binding plus a parser
+for the declarations in include/fa_b200.h."""
 import os
 import re
 
+from flash_attention_sm75.capi import *  # noqa: F401,F403
+from flash_attention_sm75.capi import LIB_PATH, SIGNATURES, fa_fwd, load, ptr, stream_ptr  # noqa: F401
+
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-PKG_DIR = os.path.join(REPO, "flash-attention-sm75-register-fused_b200")
-LIB_PATH = os.path.join(PKG_DIR, "lib", "libfa_b200.so")
 HEADER = os.path.join(REPO, "include", "fa_b200.h")
-
-c_vp, c_int, c_float, c_bool = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_bool
-
-SIGNATURES = {
-    "fa_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
-                       c_int, c_int, c_vp]),
-    "launch_flash_attention_forward": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
-                                              c_float, c_bool]),
-    "launch_flash_attention_forward_scalar": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
-                                                     c_int, c_float, c_bool]),
-    "launch_flash_attention_forward_wmma_qk": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
-                                                      c_int, c_float, c_bool]),
-    "launch_naive_attention": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float,
-                                      c_bool, c_vp]),
-    "fa_naive_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_int,
-                             c_vp, c_vp]),
-    "flatargs_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_vp]),
-    "launch_v2": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_int, c_vp]),
-    "fa_device_status": (c_int, [c_int]),
-    "fa_set_watchdog_ns": (None, [ctypes.c_ulonglong]),
-    "fa_set_debug_flags": (None, [c_int]),
-    "fa_error_string": (ctypes.c_char_p, [c_int]),
-    "fa_smem_bytes": (c_int, [c_int]),
-    "fa_version": (ctypes.c_char_p, []),
-}
-
-_lib = None
-
-
-def load():
-    global _lib
-    if _lib is None:
-        lib = ctypes.CDLL(LIB_PATH)
-        for name, (res, args) in SIGNATURES.items():
-            fn = getattr(lib, name)
-            fn.restype = res
-            fn.argtypes = args
-        _lib = lib
-    return _lib
 
 
 def header_functions():
@@ -59,26 +17,3 @@ def header_functions():
     names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*([a-z_][a-z0-9_]*)\s*\(",
                        text, flags=re.M)
     return sorted(set(names))
-
-
-def ptr(t):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
-
-
-def stream_ptr(torch_stream=None):
-    import torch
-    s = torch_stream or torch.cuda.current_stream()
-    return ctypes.c_void_p(s.cuda_stream)
-
-
-def fa_fwd(q, k, v, o, lse=None, causal=False, scale=None, stream=None):
-    """Call fa_fwd on torch CUDA tensors laid out [B, H, N, d]; returns the status."""
-    import math
-    import torch
-    B, Hq, N, d = q.shape
-    Hkv = k.shape[1]
-    if scale is None:
-        scale = 1.0 / math.sqrt(d)
-    dtype = 1 if q.dtype == torch.bfloat16 else 0
-    return load().fa_fwd(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), B, Hq, Hkv, N, d,
-                         float(scale), int(bool(causal)), dtype, stream_ptr(stream))
