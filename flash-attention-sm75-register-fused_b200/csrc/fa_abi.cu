@@ -276,7 +276,7 @@ void fa_set_watchdog_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1u
 
 void fa_set_debug_flags(int flags) { g_debug_flags.store(flags); }
 
-// Development hook: device buffer for FA_TRACE builds (8*64*16 int64), or NULL.
+// Development hook: device buffer for FA_TRACE builds (8*64*32 int64), or NULL.
 void fa_set_trace_buffer(void* buf) { g_trace.store(static_cast<long long*>(buf)); }
 
 const char* fa_error_string(int code) {

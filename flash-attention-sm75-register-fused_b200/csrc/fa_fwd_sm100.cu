@@ -57,11 +57,14 @@ constexpr int kWarpMma = 9;    // warps 10-11 complete the third warpgroup and i
 // softmax warpgroups.  256*kRegsSoftmax + 128*kRegsOther must not exceed
 // 384*kLaunchRegs.
 constexpr int kLaunchRegs = 168;
-constexpr int kRegsSoftmax = 216;
-constexpr int kRegsOther = 72;
+constexpr int kRegsSoftmax = 208;
+constexpr int kRegsOther = 88;
 static_assert(256 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kLaunchRegs,
               "register split exceeds the launch allocation");
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows > 2^8
+// Lazy rescaling: O and l keep a stale row max until the true max exceeds it
+// by more than 2^15 (log2 units), so P = exp2(s - m_stale) <= 2^15 still fits
+// f16 (max 65504) and bf16; results are identical up to rounding.
+constexpr float kRescaleThreshold = 15.0f;
 
 template <int D>
 struct Layout {
@@ -165,7 +168,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // Timeline tracing for development builds (-DFA_TRACE): the first
 // kTraceCtas CTAs record clock64() at fixed points of every K/V tile into
 // p.trace[cta][tile][event].  Compiled out otherwise.
-constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 16;
+constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
 #ifdef FA_TRACE
 #define FA_TRACE_AT(tile, ev)                                                          \
   do {                                                                                 \
@@ -185,7 +188,7 @@ constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 16;
 #define FA_EMU_PERIOD 4
 #endif
 #ifndef FA_EMU_COUNT
-#define FA_EMU_COUNT 1
+#define FA_EMU_COUNT 0
 #endif
 constexpr int kEmuPeriod = FA_EMU_PERIOD;
 constexpr int kEmuCount = FA_EMU_COUNT;
@@ -229,13 +232,14 @@ __device__ __forceinline__ float row_sum(const float (&x)[kBlockN]) {
   return a0 + a1;
 }
 
-// exp2(x * sl - m) for the 128 scores of this thread's row; the packed
+// exp2(x * sl - m) for the 128 scores (and, if kTrackMax, the raw max of x) of this thread's row; the packed
 // f16/bf16 values go to TMEM (P operand of the PV MMA) in two 32-column halves;
 // returns their fp32 sum.
-template <bool BF16, bool kEmulate>
-__device__ __forceinline__ float exp_tile(float (&x)[kBlockN], float sl, float neg_m,
-                                          uint32_t tP) {
+template <bool BF16, bool kEmulate, bool kTrackMax>
+__device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, float neg_m,
+                                          uint32_t tP, float* max_out) {
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     uint32_t pk[32];
@@ -254,10 +258,17 @@ __device__ __forceinline__ float exp_tile(float (&x)[kBlockN], float sl, float n
         ptx::fadd2(b0, b1, b0, b1, e0, e1);
       else
         ptx::fadd2(a0, a1, a0, a1, e0, e1);
+      if (kTrackMax) {
+        if (c & 1)
+          mx1 = fmaxf(mx1, fmaxf(x[i], x[i + 1]));
+        else
+          mx0 = fmaxf(mx0, fmaxf(x[i], x[i + 1]));
+      }
       pk[c] = pack2<BF16>(e0, e1);
     }
     ptx::tmem_st32(tP + 32 * h, pk);
   }
+  if (kTrackMax) *max_out = fmaxf(mx0, mx1);
   ptx::fadd2(a0, a1, a0, a1, b0, b1);
   return a0 + a1;
 }
@@ -379,11 +390,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // offset is added to the start-address field (16-byte units)
       const uint64_t k_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16, 1024);
       const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
-      const uint64_t q_desc[2] = {ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024),
-                                  ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024)};
+      const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
+      const uint64_t q_desc1 = ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024);
       auto issue_s = [&](int g, int j) {
         const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(2 * j) * L::kTile) >> 4);
-        const uint64_t qd = q_desc[g];
+        const uint64_t qd = g ? q_desc1 : q_desc0;
         if (ptx::elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -472,9 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const int og = warp - 10;
     for (int j = 0; j < n_kv[og]; ++j) {
       if (!bar_wait(bar(L::kBarS + og), j & 1, wc, 30)) break;
-      FA_TRACE_AT(j, 12 + 2 * og);
+      FA_TRACE_AT(j, 24 + 2 * og);
       if (!bar_wait(bar(L::kBarO + og), j & 1, wc, 31)) break;
-      FA_TRACE_AT(j, 13 + 2 * og);
+      FA_TRACE_AT(j, 25 + 2 * og);
     }
 #endif
    }
@@ -499,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), j & 1, wc, 20 + g));
       if (!ok) break;
-      if (r == 0) FA_TRACE_AT(j, 4 + 4 * g);
+      if (lane == 0) FA_TRACE_AT(j, 16 + warp);
       ptx::tc_fence_after();
 
       float x[kBlockN];
@@ -546,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         m_tile = row_min(x) * sl;
       }
 
-      if (r == 0) FA_TRACE_AT(j, 5 + 4 * g);
+      if (r == 0) FA_TRACE_AT(j, 28 + g);
       const float m_new = fmaxf(m, m_tile);
       const bool grow = m_new > m + kRescaleThreshold;
       if (j == 0) {
@@ -557,19 +568,19 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         if (__any_sync(0xffffffffu, grow)) {
           const float alpha = grow ? ptx::ex2_approx(m - m_new) : 1.0f;
 #pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t o[16];
-            ptx::tmem_ld16(tO + c * 16, o);
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld32(tO + c * 32, o);
             ptx::tmem_wait_ld();
-            pin_after_wait<16>(o);
+            pin_after_wait<32>(o);
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
+            for (int i = 0; i < 32; i += 2) {
               float a0 = __uint_as_float(o[i]), a1 = __uint_as_float(o[i + 1]);
               ptx::fmul2(a0, a1, a0, a1, alpha, alpha);
               o[i] = __float_as_uint(a0);
               o[i + 1] = __float_as_uint(a1);
             }
-            ptx::tmem_st16(tO + c * 16, o);
+            ptx::tmem_st32(tO + c * 32, o);
           }
           ptx::tmem_wait_st();
           if (grow) l *= alpha;
@@ -580,11 +591,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 
       // P = exp2(x * sl_eff - m): packed FMA, then exp2 split between the MUFU
       // unit and a polynomial on the FMA pipe; written to TMEM in two halves.
-      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP)
-                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP);
+      const float tile_sum = masked ? exp_tile<BF16, false, false>(x, sl_eff, neg_m, tP, nullptr)
+                                    : exp_tile<BF16, true, false>(x, sl_eff, neg_m, tP, nullptr);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      if (r == 0) FA_TRACE_AT(j, 6 + 4 * g);
+      if (lane == 0) FA_TRACE_AT(j, 8 + warp);
       ptx::mbar_arrive(bar(L::kBarP + g));
       l += tile_sum;
     }

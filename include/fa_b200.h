@@ -107,7 +107,7 @@ int fa_device_status(int reset);
 void fa_set_watchdog_ns(unsigned long long ns);
 /* FA_DEBUG_* bits applied to subsequent launches (tests only; default 0). */
 void fa_set_debug_flags(int flags);
-/* Development hook: device buffer (8*64*16 int64) that builds compiled with
+/* Development hook: device buffer (8*64*32 int64) that builds compiled with
  * FA_TRACE fill with per-tile clock64() samples; NULL disables.  No effect in
  * regular builds. */
 void fa_set_trace_buffer(void* buf);
