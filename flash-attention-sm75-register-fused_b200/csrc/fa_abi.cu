@@ -292,6 +292,8 @@ const char* fa_error_string(int code) {
     case FA_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case FA_ERR_CUDA: return "CUDA runtime call failed";
     case FA_ERR_TOO_LARGE: return "problem size exceeds the kernel's index range";
+    case FA_ERR_SCRATCH_LIMIT:
+      return "batch*heads*seq_len^2 exceeds the 4Mi-float scratch of fa_naive_fwd_noalloc";
     default: break;
   }
   if (code >= FA_ERR_TIMEOUT_BASE) return "device watchdog: an in-kernel wait timed out";
@@ -306,3 +308,55 @@ int fa_smem_bytes(int head_dim) {
 const char* fa_version(void) { return "fa_b200 0.1.0 (sm_100a tcgen05)"; }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-alloc
+// Materialised attention for callers that must not allocate device memory
+// while they run (hosts whose allocator is closed after start-up, real-time
+// or embedded loops, runtimes that own all device memory): the score matrix
+// lives in a fixed file-scope device array instead of a caller-provided or
+// freshly allocated workspace.  The array is part of this library's device
+// image, so every GPU that loads the library keeps these 16 MiB until the
+// process exits.
+namespace {
+
+constexpr unsigned long long kNoAllocScratchFloats = 4ull << 20;  // 16 MiB of fp32 scores
+__device__ __align__(256) float g_naive_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array for the current device.  Host code may
+// not pass the symbol itself to a kernel (on the host it names a host-side
+// stand-in); the address is looked up once per device, with that device
+// current, and cached.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return FA_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_naive_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return FA_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" int fa_naive_fwd_noalloc(const void* Q, const void* K, const void* V, void* O,
+                                    int batch, int heads, int seq_len, int head_dim, float scale,
+                                    int causal, void* stream) {
+  if (batch < 0 || heads < 0 || seq_len < 0 || head_dim <= 0) return FA_ERR_INVALID_ARG;
+  if (batch == 0 || heads == 0 || seq_len == 0) return FA_OK;
+  const unsigned long long need = static_cast<unsigned long long>(batch) * heads *
+                                  static_cast<unsigned long long>(seq_len) * seq_len;
+  if (need > kNoAllocScratchFloats) return FA_ERR_SCRATCH_LIMIT;
+  float* ws = nullptr;
+  if (int rc = noalloc_scratch(&ws)) return rc;
+  // Every score the softmax and PV kernels read is written by the QK^T kernel
+  // of the same call first, so the shared array needs no clearing.
+  return fa_naive_fwd(Q, K, V, O, batch, heads, seq_len, head_dim, scale, causal, ws, stream);
+}

@@ -26,6 +26,8 @@ SIGNATURES = {
                                       c_bool, c_vp]),
     "fa_naive_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float, c_int,
                              c_vp, c_vp]),
+    "fa_naive_fwd_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_float,
+                                     c_int, c_vp]),
     "flatargs_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_vp]),
     "launch_v2": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_float, c_int, c_vp]),
     "fa_device_status": (c_int, [c_int]),

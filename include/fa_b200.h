@@ -38,6 +38,7 @@ enum {
   FA_ERR_DEVICE = 8,               /* current device is not sm_100 */
   FA_ERR_CUDA = 9,                 /* another CUDA runtime call failed */
   FA_ERR_TOO_LARGE = 10,           /* a size overflows the kernel's index types */
+  FA_ERR_SCRATCH_LIMIT = 11,       /* fa_naive_fwd_noalloc: problem larger than its static scratch */
   FA_ERR_TIMEOUT_BASE = 100        /* device watchdog: 100 + wait site id */
 };
 
@@ -88,6 +89,29 @@ void launch_naive_attention(const void* Q, const void* K, const void* V, void* O
 int fa_naive_fwd(const void* Q, const void* K, const void* V, void* O, int batch, int heads,
                  int seq_len, int head_dim, float scale, int causal, float* workspace,
                  void* stream);
+
+/* fa_naive_fwd_noalloc — the materialised attention of fa_naive_fwd for
+ * callers that cannot allocate device memory while they run: hosts whose
+ * allocator is closed after start-up, real-time or embedded loops, runtimes
+ * that own all device memory and forbid cudaMalloc from libraries.  It has no
+ * counterpart in the reference (the reference's binding allocates the
+ * workspace with torch::empty per call, pytorch_extension.cpp:37-40).
+ *   - The score workspace is a file-scope device array of 4Mi floats
+ *     (16 MiB), so batch*heads*seq_len*seq_len must be <= 4194304; larger
+ *     problems return FA_ERR_SCRATCH_LIMIT and launch nothing.  Every GPU that
+ *     loads this library holds those 16 MiB until the process exits.
+ *   - Nothing is allocated or freed: no cudaMalloc/cudaFree, no allocating
+ *     library call.  The first call on a device looks up the array's device
+ *     address (cudaGetSymbolAddress) with that device current; make that first
+ *     call before any stream capture on the device.
+ *   - All calls on a device share the one array and it keeps the last call's
+ *     contents (every score is rewritten before it is read, so nothing needs
+ *     clearing).  Calls whose work overlaps on the GPU race on the array:
+ *     order them on one stream or synchronise between them.
+ * Arguments, layout (fp16), stream semantics and results as fa_naive_fwd. */
+int fa_naive_fwd_noalloc(const void* Q, const void* K, const void* V, void* O, int batch,
+                         int heads, int seq_len, int head_dim, float scale, int causal,
+                         void* stream);
 
 /* ---- standalone-kernel launchers ----
  * reference flash-attention-sm75-fused/src/flash_mha_flatargs.cu:231-252
