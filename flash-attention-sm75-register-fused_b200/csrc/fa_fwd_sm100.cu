@@ -188,7 +188,7 @@ constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
 #define FA_EMU_PERIOD 4
 #endif
 #ifndef FA_EMU_COUNT
-#define FA_EMU_COUNT 0
+#define FA_EMU_COUNT 1
 #endif
 constexpr int kEmuPeriod = FA_EMU_PERIOD;
 constexpr int kEmuCount = FA_EMU_COUNT;

@@ -284,24 +284,26 @@ __device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, 
 // 2^t for two lanes on the FMA pipe (no MUFU), t <= 64.
 // Method: t = n + f with n = round-to-nearest(t) obtained by adding and
 // subtracting 1.5*2^23 (the addition leaves n in the low mantissa bits),
-// f in [-0.5, 0.5]; 2^f from a degree-4 polynomial fitted here by a Remez
+// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted here by a Remez
 // exchange for minimum relative error on [-0.5, 0.5] (max rel. error
-// 2.7e-6 evaluated in fp32 Horner form); 2^n applied by adding n to the
-// exponent field.  t is clamped at -127 so the exponent never wraps; results
-// below 2^-126 come out as tiny denormals instead of exact zeros.
+// 7.5e-5 evaluated in fp32 Horner form, below the 4.9e-4 rounding of the
+// f16 P it feeds); 2^n applied by adding n to the exponent field.  t is
+// clamped at -126: with n >= -126 and 2^f >= 2^-0.5 the exponent sum stays
+// >= 0, so it never borrows into the sign bit (at -127 a polynomial value
+// just below 1.0 would wrap to a NaN); results below 2^-126 come out as
+// denormals of magnitude <= 1.2e-38 instead of exact zeros.
 __device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float t0, float t1) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.9999992847442627f, c1 = 0.6931217908859253f, c2 = 0.240247443318367f,
-                  c3 = 0.05591785907745361f, c4 = 0.009570102207362652f;
-  t0 = fmaxf(t0, -127.0f);
-  t1 = fmaxf(t1, -127.0f);
+  constexpr float c0 = 0.9999280571937561f, c1 = 0.6932609677314758f, c2 = 0.2426111251115799f,
+                  c3 = 0.0551716685295105f;
+  t0 = fmaxf(t0, -126.0f);
+  t1 = fmaxf(t1, -126.0f);
   float j0, j1, n0, n1, f0, f1;
   fadd2(j0, j1, t0, t1, kRound, kRound);
   fadd2(n0, n1, j0, j1, -kRound, -kRound);
   ffma2(f0, f1, n0, n1, -1.0f, -1.0f, t0, t1);
   float p0, p1;
-  ffma2(p0, p1, c4, c4, f0, f1, c3, c3);
-  ffma2(p0, p1, p0, p1, f0, f1, c2, c2);
+  ffma2(p0, p1, c3, c3, f0, f1, c2, c2);
   ffma2(p0, p1, p0, p1, f0, f1, c1, c1);
   ffma2(p0, p1, p0, p1, f0, f1, c0, c0);
   y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(j0) << 23));
