@@ -50,8 +50,11 @@ namespace {
 constexpr int kBlockM = 128;  // query rows per tile (one TMEM lane each)
 constexpr int kBlockN = 128;  // keys per K/V tile
 constexpr int kThreads = 384;   // 3 warpgroups
+// Warpgroup of the producer, the MMA issuer and two spare warps (8-11); the
+// two softmax warpgroups are warps 0-7.
 constexpr int kWarpLoad = 8;
-constexpr int kWarpMma = 9;    // warps 10-11 complete the third warpgroup and idle
+constexpr int kWarpMma = 9;
+constexpr int kWarpSoftmax0 = 0;
 // Register split: launched at kLaunchRegs per thread (65536 / 384 rounded down
 // to a multiple of 8); the producer/MMA warpgroup gives registers to the two
 // softmax warpgroups.  256*kRegsSoftmax + 128*kRegsOther must not exceed
@@ -193,53 +196,43 @@ constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
 constexpr int kEmuPeriod = FA_EMU_PERIOD;
 constexpr int kEmuCount = FA_EMU_COUNT;
 
-__device__ __forceinline__ float row_max(const float (&x)[kBlockN]) {
+// Three-input max / min (sm_100 forms of max.f32 / min.f32).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Max (kMin: min) of N scores in four independent three-input chains.
+template <int N, bool kMin>
+__device__ __forceinline__ float row_extreme(const float (&x)[N]) {
+  static_assert(N % 8 == 0 && N >= 16, "row length");
+  auto op3 = [](float a, float b, float c) { return kMin ? fmin3(a, b, c) : fmax3(a, b, c); };
   float a = x[0], b = x[1], c = x[2], d = x[3];
 #pragma unroll
-  for (int i = 4; i < kBlockN; i += 4) {
-    a = fmaxf(a, x[i]);
-    b = fmaxf(b, x[i + 1]);
-    c = fmaxf(c, x[i + 2]);
-    d = fmaxf(d, x[i + 3]);
+  for (int i = 4; i + 8 <= N; i += 8) {
+    a = op3(a, x[i], x[i + 1]);
+    b = op3(b, x[i + 2], x[i + 3]);
+    c = op3(c, x[i + 4], x[i + 5]);
+    d = op3(d, x[i + 6], x[i + 7]);
   }
-  return fmaxf(fmaxf(a, b), fmaxf(c, d));
+  a = op3(a, x[N - 4], x[N - 3]);
+  b = op3(b, x[N - 2], x[N - 1]);
+  return op3(a, b, kMin ? fminf(c, d) : fmaxf(c, d));
 }
 
-__device__ __forceinline__ float row_min(const float (&x)[kBlockN]) {
-  float a = x[0], b = x[1], c = x[2], d = x[3];
-#pragma unroll
-  for (int i = 4; i < kBlockN; i += 4) {
-    a = fminf(a, x[i]);
-    b = fminf(b, x[i + 1]);
-    c = fminf(c, x[i + 2]);
-    d = fminf(d, x[i + 3]);
-  }
-  return fminf(fminf(a, b), fminf(c, d));
-}
-
-__device__ __forceinline__ float row_sum(const float (&x)[kBlockN]) {
-  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f, d0 = 0.f, d1 = 0.f;
-#pragma unroll
-  for (int i = 0; i < kBlockN; i += 8) {
-    ptx::fadd2(a0, a1, a0, a1, x[i], x[i + 1]);
-    ptx::fadd2(b0, b1, b0, b1, x[i + 2], x[i + 3]);
-    ptx::fadd2(c0, c1, c0, c1, x[i + 4], x[i + 5]);
-    ptx::fadd2(d0, d1, d0, d1, x[i + 6], x[i + 7]);
-  }
-  ptx::fadd2(a0, a1, a0, a1, b0, b1);
-  ptx::fadd2(c0, c1, c0, c1, d0, d1);
-  ptx::fadd2(a0, a1, a0, a1, c0, c1);
-  return a0 + a1;
-}
-
-// exp2(x * sl - m) for the 128 scores (and, if kTrackMax, the raw max of x) of this thread's row; the packed
+// exp2(x * sl - m) for the 128 scores of this thread's row; the packed
 // f16/bf16 values go to TMEM (P operand of the PV MMA) in two 32-column halves;
 // returns their fp32 sum.
-template <bool BF16, bool kEmulate, bool kTrackMax>
+template <bool BF16, bool kEmulate>
 __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, float neg_m,
-                                          uint32_t tP, float* max_out) {
+                                          uint32_t tP) {
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-  float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     uint32_t pk[32];
@@ -258,17 +251,10 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
         ptx::fadd2(b0, b1, b0, b1, e0, e1);
       else
         ptx::fadd2(a0, a1, a0, a1, e0, e1);
-      if (kTrackMax) {
-        if (c & 1)
-          mx1 = fmaxf(mx1, fmaxf(x[i], x[i + 1]));
-        else
-          mx0 = fmaxf(mx0, fmaxf(x[i], x[i + 1]));
-      }
       pk[c] = pack2<BF16>(e0, e1);
     }
     ptx::tmem_st32(tP + 32 * h, pk);
   }
-  if (kTrackMax) *max_out = fmaxf(mx0, mx1);
   ptx::fadd2(a0, a1, a0, a1, b0, b1);
   return a0 + a1;
 }
@@ -328,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
 
-  if (warp >= 8) {
+  if (warp < kWarpSoftmax0 || warp >= kWarpSoftmax0 + 8) {
    // ------------------------------------------------ producer warpgroup
    ptx::setmaxnreg_dec<kRegsOther>();
    if (warp == kWarpLoad) {
@@ -425,6 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
       };
 
+
       // Issue order per tile j (two groups g0, g1 ping-pong on the tensor pipe):
       //   PV0(j)  S0(j+1)  PV1(j)  S1(j+1)
       // so each group's softmax overlaps the other group's two MMAs.  S_g(j+1)
@@ -442,18 +429,26 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       for (int j = 0; ok && j < n_loop; ++j) {
         const int item_v = 2 * j + 1;
         const int item_k = 2 * j + 2;  // K of tile j+1
-        if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
         const bool next0 = j + 1 < n_kv[0];
         const bool next1 = j + 1 < n_kv[1];
+        // V_j and K_{j+1} are waited for before the P waits, so that a
+        // group's PV and next S go out back to back once its P is ready.
+        // Every release the producer needs before loading them was committed
+        // in an earlier iteration, so these waits cannot depend on this one.
+        if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
+        if ((next0 || next1) &&
+            !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
+          break;
         if (j < n_kv[0]) {
           if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
           ptx::tc_fence_after();
           if (lane == 0) FA_TRACE_AT(j, 0);
           issue_pv(0, j);
+          if (lane == 0) FA_TRACE_AT(j, 4);
           if (next0) {
-            if (!(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14))) break;
             if (lane == 0) FA_TRACE_AT(j, 1);
             issue_s(0, j + 1);
+            if (lane == 0) FA_TRACE_AT(j, 5);
             if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
           }
         }
@@ -465,7 +460,6 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
         commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
         if (next1) {
-          if (!(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 17))) break;
           if (lane == 0) FA_TRACE_AT(j, 3);
           issue_s(1, j + 1);
           commit(bar(L::kBarEmpty + slot_of(item_k)));
@@ -480,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
    } else if (lane == 0) {
     // trace observers: warp 10 (group 0) / 11 (group 1) timestamp the
     // completion of every S and PV MMA of their group
-    const int og = warp - 10;
+    const int og = warp - kWarpMma - 1;
     for (int j = 0; j < n_kv[og]; ++j) {
       if (!bar_wait(bar(L::kBarS + og), j & 1, wc, 30)) break;
       FA_TRACE_AT(j, 24 + 2 * og);
@@ -492,7 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   } else {
     // ===================================================== softmax groups
     ptx::setmaxnreg_inc<kRegsSoftmax>();
-    const int g = warp >> 2;
+    const int sw = warp - kWarpSoftmax0;        // softmax warp 0..7
+    const int g = sw >> 2;
     const int n_tiles = n_kv[g];
     const int wq = warp & 3;
     const int r = wq * 32 + lane;               // row within the tile == TMEM lane
@@ -510,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), j & 1, wc, 20 + g));
       if (!ok) break;
-      if (lane == 0) FA_TRACE_AT(j, 16 + warp);
+      if (lane == 0) FA_TRACE_AT(j, 16 + sw);
       ptx::tc_fence_after();
 
       float x[kBlockN];
@@ -549,12 +544,12 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 #pragma unroll
         for (int c = 0; c < kBlockN; ++c)
           if (c >= lim) x[c] = -INFINITY;
-        m_tile = row_max(x);
+        m_tile = row_extreme<kBlockN, false>(x);
         sl_eff = 1.0f;
       } else if (sl >= 0.f) {
-        m_tile = row_max(x) * sl;
+        m_tile = row_extreme<kBlockN, false>(x) * sl;
       } else {
-        m_tile = row_min(x) * sl;
+        m_tile = row_extreme<kBlockN, true>(x) * sl;
       }
 
       if (r == 0) FA_TRACE_AT(j, 28 + g);
@@ -591,11 +586,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 
       // P = exp2(x * sl_eff - m): packed FMA, then exp2 split between the MUFU
       // unit and a polynomial on the FMA pipe; written to TMEM in two halves.
-      const float tile_sum = masked ? exp_tile<BF16, false, false>(x, sl_eff, neg_m, tP, nullptr)
-                                    : exp_tile<BF16, true, false>(x, sl_eff, neg_m, tP, nullptr);
+      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP)
+                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      if (lane == 0) FA_TRACE_AT(j, 8 + warp);
+      if (lane == 0) FA_TRACE_AT(j, 8 + sw);
       ptx::mbar_arrive(bar(L::kBarP + g));
       l += tile_sum;
     }
