@@ -170,7 +170,15 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 // Timeline tracing for development builds (-DFA_TRACE): the first
 // kTraceCtas CTAs record clock64() at fixed points of every K/V tile into
-// p.trace[cta][tile][event].  Compiled out otherwise.
+// p.trace[cta][tile][event].  Compiled out otherwise.  Events of tile j:
+//   0-3   MMA warp starts issuing PV0(j), S0(j+1), PV1(j), S1(j+1)
+//   4, 5  MMA warp has issued PV0(j), S0(j+1)
+//   6, 7  MMA warp before / after the V_j and K_{j+1} waits
+//   8-15  softmax warp w arrived on P (w = 0..7)
+//   16-23 softmax warp w saw S complete
+//   24-27 observer warps (d=128): S0(j), PV0(j), S1(j), PV1(j) complete
+//   28-29 group 0 / 1 tile max computed (row 0)
+//   30-31 producer issued the loads of V_j / K_{j+1}
 constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
 #ifdef FA_TRACE
 #define FA_TRACE_AT(tile, ev)                                                          \
@@ -346,6 +354,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         const uint32_t dst = sbase + L::kOffKV + slot * L::kTile;
         const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
                                   : static_cast<const void*>(&p.tm_k);
+        if ((i & 1) && (i >> 1) < kTraceTiles) FA_TRACE_AT(i >> 1, 30);        // V_j issued
+        if (!(i & 1) && i > 0) FA_TRACE_AT((i >> 1) - 1, 31);                   // K_{j+1} issued
         ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
@@ -412,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       };
 
 
+
       // Issue order per tile j (two groups g0, g1 ping-pong on the tensor pipe):
       //   PV0(j)  S0(j+1)  PV1(j)  S1(j+1)
       // so each group's softmax overlaps the other group's two MMAs.  S_g(j+1)
@@ -435,10 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         // group's PV and next S go out back to back once its P is ready.
         // Every release the producer needs before loading them was committed
         // in an earlier iteration, so these waits cannot depend on this one.
+        if (lane == 0) FA_TRACE_AT(j, 6);
         if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
         if ((next0 || next1) &&
             !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
           break;
+        if (lane == 0) FA_TRACE_AT(j, 7);
         if (j < n_kv[0]) {
           if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
           ptx::tc_fence_after();
@@ -474,11 +487,20 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
    } else if (lane == 0) {
     // trace observers: warp 10 (group 0) / 11 (group 1) timestamp the
     // completion of every S and PV MMA of their group
+    // (polling without suspension, so the timestamps are not delayed by a
+    // wake-up; each poll loop gives up after 2^26 polls or on abort)
     const int og = warp - kWarpMma - 1;
+    auto poll = [&](uint32_t b, uint32_t ph) {
+      for (uint32_t n = 0; n < (1u << 26); ++n) {
+        if (ptx::mbar_test_wait(b, ph)) return true;
+        if ((n & 1023u) == 1023u && *abort_flag) return false;
+      }
+      return false;
+    };
     for (int j = 0; j < n_kv[og]; ++j) {
-      if (!bar_wait(bar(L::kBarS + og), j & 1, wc, 30)) break;
+      if (!poll(bar(L::kBarS + og), j & 1)) break;
       FA_TRACE_AT(j, 24 + 2 * og);
-      if (!bar_wait(bar(L::kBarO + og), j & 1, wc, 31)) break;
+      if (!poll(bar(L::kBarO + og), j & 1)) break;
       FA_TRACE_AT(j, 25 + 2 * og);
     }
 #endif
