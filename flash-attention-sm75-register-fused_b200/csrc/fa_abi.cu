@@ -126,53 +126,168 @@ __global__ void naive_pv_kernel(const float* __restrict__ P, const __half* __res
   O[(bh * n + i) * d + c] = __float2half_rn(acc);
 }
 
-}  // namespace
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  static std::atomic<int> cache[64];
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
 
-extern "C" {
+// How one call is laid out on the GPU.  Short GQA queries (Nq <= 128) are
+// "packed": the group's query heads are consecutive in [B, Hq, Nq, d], so the
+// G*Nq rows of one KV head form one row sequence (pos = row % Nq) and share
+// every K/V tile.  When (batch*head, Q pair) units alone fill less than one
+// wave and a workspace is available, the key range is split so that about two
+// CTAs per SM run; a combine kernel merges the splits.
+struct Plan {
+  bool pack = false;
+  int heads = 0, rows = 0, group = 1, pos_mod = 1, n_qpairs = 0, n_kv_tiles = 0;
+  int n_splits = 1, tiles_per_split = 0;
+  size_t ws_o_bytes = 0, ws_bytes = 0;
+};
 
-int fa_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
-           int Hkv, int N, int head_dim, float scale, int causal, int dtype, void* stream) {
-  if (B < 0 || Hq < 0 || Hkv < 0 || N < 0) return FA_ERR_INVALID_ARG;
+Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) {
+  Plan k;
+  const int G = Hq / Hkv;
+  k.pack = G > 1 && Nq <= 128;
+  k.heads = k.pack ? Hkv : Hq;
+  k.rows = k.pack ? G * Nq : Nq;
+  k.group = k.pack ? 1 : G;
+  k.pos_mod = k.pack ? Nq : k.rows;
+  k.n_qpairs = (k.rows + 255) / 256;
+  k.n_kv_tiles = (Nk + 127) / 128;
+  k.tiles_per_split = k.n_kv_tiles;
+  const long long units = static_cast<long long>(k.n_qpairs) * B * k.heads;
+  const int sms = sm_count();
+  if (allow_split && units < sms && k.n_kv_tiles > 1) {
+    long long want = (2LL * sms + units - 1) / units;
+    if (want > k.n_kv_tiles) want = k.n_kv_tiles;
+    if (want > 64) want = 64;
+    k.tiles_per_split = static_cast<int>((k.n_kv_tiles + want - 1) / want);
+    k.n_splits = (k.n_kv_tiles + k.tiles_per_split - 1) / k.tiles_per_split;
+  }
+  if (k.n_splits > 1) {
+    const size_t rows_total = static_cast<size_t>(B) * k.heads * k.rows;
+    k.ws_o_bytes = static_cast<size_t>(k.n_splits) * rows_total * d * sizeof(float);
+    k.ws_bytes = k.ws_o_bytes + static_cast<size_t>(k.n_splits) * rows_total * sizeof(float);
+  }
+  return k;
+}
+
+// Shared argument checks of fa_fwd / fa_fwd_kvcache; FA_OK means "launch".
+// *empty is set when there is nothing to compute.
+int check_args(const void* Q, const void* K, const void* V, const void* O, const float* lse,
+               int B, int Hq, int Hkv, int Nq, int Nk, int head_dim, float scale, int causal,
+               int dtype, bool* empty) {
+  *empty = false;
+  if (B < 0 || Hq < 0 || Hkv < 0 || Nq < 0 || Nk < 0) return FA_ERR_INVALID_ARG;
   if (head_dim != 64 && head_dim != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_DTYPE;
-  if (causal != 0 && causal != 1) return FA_ERR_INVALID_ARG;
-  if (B == 0 || Hq == 0 || N == 0) return FA_OK;
-  if (Hkv == 0) return FA_ERR_INVALID_ARG;
+  if (causal < FA_CAUSAL_NONE || causal > FA_CAUSAL_TOP_LEFT) return FA_ERR_INVALID_ARG;
+  if (B == 0 || Hq == 0 || Nq == 0) {
+    *empty = true;
+    return FA_OK;
+  }
+  if (Hkv == 0 || Nk == 0) return FA_ERR_INVALID_ARG;
   if (Hq % Hkv != 0) return FA_ERR_GQA_DIVISIBILITY;
   if (!Q || !K || !V || !O) return FA_ERR_INVALID_ARG;
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) ||
       (reinterpret_cast<uintptr_t>(lse) & 3u))
     return FA_ERR_ALIGNMENT;
   if (!std::isfinite(scale)) return FA_ERR_INVALID_ARG;
-  const long long bhq = static_cast<long long>(B) * Hq;
-  const long long n_qpairs = (static_cast<long long>(N) + 255) / 256;
-  if (bhq * n_qpairs > 0x7fffffffLL || static_cast<long long>(N) + 256 > 0x7fffffffLL)
+  const long long rows = static_cast<long long>(B) * Hq * Nq;
+  if (Nq > (1 << 30) || Nk > (1 << 30) || rows > (1LL << 40) ||
+      static_cast<long long>(B) * Hq * ((static_cast<long long>(Nq) + 255) / 256) > 0x7fffffffLL)
     return FA_ERR_TOO_LARGE;
-  if (int rc = check_device()) return rc;
+  return check_device();
+}
+
+int launch_attention(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
+                     int Hq, int Hkv, int Nq, int Nk, int head_dim, float scale, int causal,
+                     int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  const bool bf16 = dtype == FA_DTYPE_BF16;
+  Plan k = make_plan(B, Hq, Hkv, Nq, Nk, head_dim, workspace != nullptr);
+  if (k.n_splits > 1 && (workspace_bytes < k.ws_bytes || !aligned16(workspace)))
+    k = make_plan(B, Hq, Hkv, Nq, Nk, head_dim, false);  // too small: no split
+  if (static_cast<long long>(k.n_qpairs) * B * k.heads * k.n_splits > 0x7fffffffLL)
+    return FA_ERR_TOO_LARGE;
 
   fa::FwdParams p;
-  const bool bf16 = dtype == FA_DTYPE_BF16;
-  if (!make_map(&p.tm_q, Q, head_dim, N, bhq, bf16) ||
-      !make_map(&p.tm_k, K, head_dim, N, static_cast<long long>(B) * Hkv, bf16) ||
-      !make_map(&p.tm_v, V, head_dim, N, static_cast<long long>(B) * Hkv, bf16))
+  const long long bh = static_cast<long long>(B) * k.heads;
+  if (!make_map(&p.tm_q, Q, head_dim, k.rows, bh, bf16) ||
+      !make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16) ||
+      !make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16))
     return FA_ERR_TENSOR_MAP;
   p.o = O;
   p.lse = lse;
   p.B = B;
-  p.Hq = Hq;
+  p.heads = k.heads;
   p.Hkv = Hkv;
-  p.N = N;
-  p.group = Hq / Hkv;
-  p.n_qpairs = static_cast<int>(n_qpairs);
-  p.n_kv_tiles = (N + 127) / 128;
-  p.causal = causal;
+  p.Nq = k.rows;
+  p.Nk = Nk;
+  p.group = k.group;
+  p.n_qpairs = k.n_qpairs;
+  p.n_kv_tiles = k.n_kv_tiles;
+  p.causal = causal != FA_CAUSAL_NONE ? 1 : 0;
+  p.causal_off = causal == FA_CAUSAL_BOTTOM_RIGHT ? Nk - Nq : 0;
+  p.pos_mod = k.pos_mod;
+  p.n_splits = k.n_splits;
+  p.tiles_per_split = k.tiles_per_split;
+  p.ws_o = k.n_splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  p.ws_lse = k.n_splits > 1
+                 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + k.ws_o_bytes)
+                 : nullptr;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.debug_flags = g_debug_flags.load(std::memory_order_relaxed);
   p.trace = g_trace.load(std::memory_order_relaxed);
   p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
-  const cudaError_t e = fa::launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fa::launch_fwd(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
+  if (k.n_splits > 1 && fa::launch_combine(p, head_dim, bf16, s) != cudaSuccess)
+    return FA_ERR_LAUNCH;
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+           int Hkv, int N, int head_dim, float scale, int causal, int dtype, void* stream) {
+  if (causal != 0 && causal != 1) return FA_ERR_INVALID_ARG;
+  bool empty = false;
+  if (int rc = check_args(Q, K, V, O, lse, B, Hq, Hkv, N, N, head_dim, scale, causal, dtype,
+                          &empty))
+    return rc;
+  if (empty) return FA_OK;
+  return launch_attention(Q, K, V, O, lse, B, Hq, Hkv, N, N, head_dim, scale, causal, dtype,
+                          nullptr, 0, stream);
+}
+
+int fa_fwd_kvcache(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
+                   int Hq, int Hkv, int Nq, int Nk, int head_dim, float scale, int causal,
+                   int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  bool empty = false;
+  if (int rc = check_args(Q, K, V, O, lse, B, Hq, Hkv, Nq, Nk, head_dim, scale, causal, dtype,
+                          &empty))
+    return rc;
+  if (empty) return FA_OK;
+  return launch_attention(Q, K, V, O, lse, B, Hq, Hkv, Nq, Nk, head_dim, scale, causal, dtype,
+                          workspace, workspace_bytes, stream);
+}
+
+size_t fa_fwd_kvcache_workspace_bytes(int B, int Hq, int Hkv, int Nq, int Nk, int head_dim) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Nq <= 0 || Nk <= 0 || Hq % Hkv != 0 ||
+      (head_dim != 64 && head_dim != 128))
+    return 0;
+  return make_plan(B, Hq, Hkv, Nq, Nk, head_dim, true).ws_bytes;
 }
 
 static void legacy_fwd(const char* tag, const void* Q, const void* K, const void* V, void* O,

@@ -11,16 +11,26 @@ namespace fa {
 // Kernel parameters; passed by value as a __grid_constant__ so the TMA
 // descriptors live in parameter space.
 struct alignas(64) FwdParams {
-  CUtensorMap tm_q;  // 3-D (d, N, B*Hq),  box (64, 128, 1), 128-byte swizzle
-  CUtensorMap tm_k;  // 3-D (d, N, B*Hkv)
-  CUtensorMap tm_v;  // 3-D (d, N, B*Hkv)
-  void* o;           // [B, Hq, N, d] f16/bf16
-  float* lse;        // [B, Hq, N] fp32 or nullptr
-  int B, Hq, Hkv, N;
-  int group;         // Hq / Hkv
-  int n_qpairs;      // ceil(N / 256): CTAs per (batch, head)
-  int n_kv_tiles;    // ceil(N / 128)
-  int causal;
+  CUtensorMap tm_q;  // 3-D (d, Nq, B*heads), box (64, 128, 1), 128-byte swizzle
+  CUtensorMap tm_k;  // 3-D (d, Nk, B*Hkv)
+  CUtensorMap tm_v;  // 3-D (d, Nk, B*Hkv)
+  void* o;           // [B*heads, Nq, d] f16/bf16
+  float* lse;        // [B*heads, Nq] fp32 or nullptr
+  // Query rows are grouped as (batch*heads, Nq).  Unpacked: heads = Hq,
+  // Nq = the query length.  GQA-packed (short queries): heads = Hkv and the
+  // Nq = group*len rows of a KV head are the group's query heads one after
+  // another (the same memory as [B, Hq, len, d]).
+  int B, heads, Hkv, Nq, Nk;
+  int group;         // query "heads" per KV head (1 when packed)
+  int n_qpairs;      // ceil(Nq / 256): Q pairs per (batch, head)
+  int n_kv_tiles;    // ceil(Nk / 128)
+  int causal;        // key j visible to row r iff j <= pos(r) + causal_off
+  int causal_off;
+  int pos_mod;       // pos(r) = r % pos_mod (packed: the query length; else Nq)
+  int n_splits;      // key-range splits per (batch*head, Q pair); 1 = no split
+  int tiles_per_split;
+  float* ws_o;       // n_splits > 1: normalised partial O [n_splits][B*heads][Nq][d] fp32
+  float* ws_lse;     // partial LSE [n_splits][B*heads][Nq] (natural log)
   float scale_log2;  // scale * log2(e)
   int debug_flags;
   long long* trace;  // timeline samples, used only in FA_TRACE builds
@@ -28,7 +38,28 @@ struct alignas(64) FwdParams {
   unsigned long long timeout_ns;
 };
 
+// Number of K/V tiles a 128-row query tile t needs (all tiles when not causal).
+// Shared by the attention kernel and the split combine so that both agree on
+// which splits hold data for a row.
+__host__ __device__ inline int kv_tiles_for_tile(const FwdParams& p, int t) {
+  if (!p.causal) return p.n_kv_tiles;
+  const int lo = t * 128;
+  const int hi = (lo + 127 < p.Nq - 1) ? lo + 127 : p.Nq - 1;
+  int max_pos;
+  if (p.pos_mod >= p.Nq) {
+    max_pos = hi;
+  } else {
+    max_pos = (hi / p.pos_mod != lo / p.pos_mod) ? p.pos_mod - 1 : hi % p.pos_mod;
+  }
+  const long long kmax = static_cast<long long>(max_pos) + p.causal_off;  // last visible key
+  if (kmax < 0) return 0;
+  const long long n = kmax / 128 + 1;
+  return n < p.n_kv_tiles ? static_cast<int>(n) : p.n_kv_tiles;
+}
+
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream);
+// Merges the n_splits partial results of p.ws_o / p.ws_lse into p.o / p.lse.
+cudaError_t launch_combine(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream);
 int smem_bytes_for(int head_dim);
 cudaError_t read_status(unsigned long long* out, bool reset);
 

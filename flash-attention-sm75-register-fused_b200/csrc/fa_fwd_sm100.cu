@@ -281,22 +281,27 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
 
-  // ---- work item: (batch*head, Q pair); causal pairs of one head run heaviest first
-  const int bh = blockIdx.x / p.n_qpairs;
-  int qp = blockIdx.x % p.n_qpairs;
+  // ---- work item: (batch*head, Q pair, key split); causal pairs of one head
+  // run heaviest first
+  const int sp = blockIdx.x % p.n_splits;
+  const int rest = blockIdx.x / p.n_splits;
+  const int bh = rest / p.n_qpairs;
+  int qp = rest % p.n_qpairs;
   if (p.causal) qp = p.n_qpairs - 1 - qp;
-  const int b = bh / p.Hq;
-  const int hq = bh % p.Hq;
+  const int b = bh / p.heads;
+  const int hq = bh % p.heads;
   const int bh_kv = b * p.Hkv + hq / p.group;
   const int q_row0 = qp * 2 * kBlockM;
-  const bool has_q1 = q_row0 + kBlockM < p.N;
+  const bool has_q1 = q_row0 + kBlockM < p.Nq;
+  // This CTA covers K/V tiles j_begin + it (it = 0, 1, ...); n_kv[g] is the
+  // number of those tiles that group g sees (0 when its causal range or the
+  // split ends earlier).
+  const int j_begin = sp * p.tiles_per_split;
   int n_kv[2];
-  if (p.causal) {
-    n_kv[0] = min(2 * qp + 1, p.n_kv_tiles);
-    n_kv[1] = has_q1 ? min(2 * qp + 2, p.n_kv_tiles) : 0;
-  } else {
-    n_kv[0] = p.n_kv_tiles;
-    n_kv[1] = has_q1 ? p.n_kv_tiles : 0;
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int total = (g == 0 || has_q1) ? kv_tiles_for_tile(p, 2 * qp + g) : 0;
+    n_kv[g] = max(0, min(total, j_begin + p.tiles_per_split) - j_begin);
   }
   const int n_loop = max(n_kv[0], n_kv[1]);
 
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
           ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
-                           (i >> 1) * kBlockN, bh_kv, pol_kv);
+                           (j_begin + (i >> 1)) * kBlockN, bh_kv, pol_kv);
         issued = i + 1;
       }
       // Drain: every copy this thread started must land before the CTA exits.
@@ -428,14 +433,20 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // so each group's softmax overlaps the other group's two MMAs.  S_g(j+1)
       // may overwrite P_g(j) (d=128): tcgen05.mma ops of one thread execute in
       // issue order, so PV_g(j) has read P_g(j) before S_g(j+1) writes it.
+      // A group without tiles in this split issues nothing; with no tiles at
+      // all the producer loads no K/V and this warp waits for nothing.
+      const bool g0 = n_kv[0] > 0;
       const bool g1 = n_kv[1] > 0;
-      bool ok = wait(bar(L::kBarQ), 0, 10);
-      if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
-      if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
-      if (ok) {
-        issue_s(0, 0);
-        if (g1) issue_s(1, 0);
-        commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
+      bool ok = true;
+      if (n_loop > 0) {
+        if (g0) ok = wait(bar(L::kBarQ), 0, 10);
+        if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
+        if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
+        if (ok) {
+          if (g0) issue_s(0, 0);
+          if (g1) issue_s(1, 0);
+          commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
+        }
       }
       for (int j = 0; ok && j < n_loop; ++j) {
         const int item_v = 2 * j + 1;
@@ -515,6 +526,19 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const int r = wq * 32 + lane;               // row within the tile == TMEM lane
     const int tile = 2 * qp + g;                // global 128-row tile index
     const int q_row = tile * kBlockM + r;
+    // causal limit of this row: key k is visible iff k < pos + causal_off + 1
+    const int vis_end = q_row % p.pos_mod + p.causal_off + 1;
+    // smallest limit over the tile's rows: a K/V tile needs masking when any
+    // of its keys lies at or beyond it (or beyond Nk)
+    int tile_vis_end;
+    {
+      const int lo = tile * kBlockM;
+      const int hi = min(lo + kBlockM - 1, p.Nq - 1);
+      const int min_pos = (p.pos_mod >= p.Nq)                   ? lo
+                          : (hi / p.pos_mod != lo / p.pos_mod) ? 0
+                                                                : lo % p.pos_mod;
+      tile_vis_end = min_pos + p.causal_off + 1;
+    }
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + L::tS(g);
     const uint32_t tP = tmem + lane_off + L::tP(g);
@@ -551,16 +575,17 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
       }
 
-      const int key0 = j * kBlockN;
-      const bool masked = (p.causal && j == tile) || (key0 + kBlockN > p.N);
+      const int key0 = (j_begin + j) * kBlockN;
+      const bool masked =
+          (p.causal && key0 + kBlockN > tile_vis_end) || (key0 + kBlockN > p.Nk);
       // Scaled tile maximum.  Unmasked tiles reduce the raw scores and scale
       // once (the exponent then folds scale and max into one packed FMA);
       // masked tiles are pre-scaled so that -inf marks excluded keys.
       float m_tile;
       float sl_eff = sl;
       if (masked) {
-        int lim = p.N - key0;
-        if (p.causal && j == tile) lim = min(lim, r + 1);
+        int lim = p.Nk - key0;
+        if (p.causal) lim = min(lim, vis_end - key0);
 #pragma unroll
         for (int c = 0; c < kBlockN; c += 2) ptx::fmul2(x[c], x[c + 1], x[c], x[c + 1], sl, sl);
 #pragma unroll
@@ -617,35 +642,66 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       l += tile_sum;
     }
 
-    // ---- epilogue: O / l -> global, LSE
-    if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarO + g), (n_tiles - 1) & 1, wc, 22 + g));
-    if (ok) {
-      ptx::tc_fence_after();
-      const bool row_ok = q_row < p.N;
-      const float inv_l = (l > 0.f) ? 1.0f / l : 0.f;
-      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      T* orow = reinterpret_cast<T*>(p.o) + (static_cast<size_t>(bh) * p.N + q_row) * D;
+    // ---- epilogue: O / l -> global (or the split workspace), LSE
+    const bool row_ok = q_row < p.Nq;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    const size_t row_index = static_cast<size_t>(bh) * p.Nq + q_row;
+    if (n_tiles == 0) {
+      // No visible key for these rows (causal offset below zero): O = 0 and
+      // LSE = -inf.  A split without tiles leaves the rows to other splits.
+      if (p.n_splits == 1 && row_ok) {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.o) + row_index * D);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        ptx::tmem_ld32(tO + c * 32, o);
-        ptx::tmem_wait_ld();
-        pin_after_wait<32>(o);
-        uint32_t h[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          h[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-        }
+        for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (p.lse != nullptr) p.lse[row_index] = -INFINITY;
       }
-      if (row_ok && p.lse != nullptr) {
+    } else {
+      if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarO + g), (n_tiles - 1) & 1, wc, 22 + g));
+      if (ok) {
+        ptx::tc_fence_after();
+        const float inv_l = (l > 0.f) ? 1.0f / l : 0.f;
         const float m_use = (m == -INFINITY) ? 0.f : m;
-        p.lse[static_cast<size_t>(bh) * p.N + q_row] =
-            (l > 0.f) ? (m_use + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+        const float lse_row = (l > 0.f) ? (m_use + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+        if (p.n_splits == 1) {
+          T* orow = reinterpret_cast<T*>(p.o) + row_index * D;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld32(tO + c * 32, o);
+            ptx::tmem_wait_ld();
+            pin_after_wait<32>(o);
+            uint32_t h[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              h[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+            if (row_ok) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+            }
+          }
+          if (row_ok && p.lse != nullptr) p.lse[row_index] = lse_row;
+        } else {
+          // partial result of this key split, normalised by its own row sum
+          const size_t ws_row = static_cast<size_t>(sp) * p.B * p.heads * p.Nq + row_index;
+          float* wrow = p.ws_o + ws_row * D;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld32(tO + c * 32, o);
+            ptx::tmem_wait_ld();
+            pin_after_wait<32>(o);
+            if (row_ok) {
+              float4* dst = reinterpret_cast<float4*>(wrow + c * 32);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                                     __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
+            }
+          }
+          if (row_ok) p.ws_lse[ws_row] = lse_row;
+        }
       }
     }
   }
@@ -658,6 +714,61 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, L::kTmemCols);
   }
+}
+
+// Merge of key-split partial results: for each query row (one warp),
+//   LSE = log sum_s exp(LSE_s),  O = sum_s exp(LSE_s - LSE) * O_s
+// over the splits that hold data for the row's tile (the same count the
+// attention kernel derives from kv_tiles_for_tile).  Rows without any
+// visible key get O = 0 and LSE = -inf.
+template <int D, bool BF16>
+__global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__ FwdParams p) {
+  constexpr int E = D / 32;  // elements per lane
+  const long long n_rows = static_cast<long long>(p.B) * p.heads * p.Nq;
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const int lane = threadIdx.x & 31;
+  const int q_row = static_cast<int>(row % p.Nq);
+  const int total = kv_tiles_for_tile(p, q_row / kBlockM);
+  const int ns = min(p.n_splits, (total + p.tiles_per_split - 1) / p.tiles_per_split);
+  float mx = -INFINITY;
+  for (int s = 0; s < ns; ++s) mx = fmaxf(mx, p.ws_lse[static_cast<size_t>(s) * n_rows + row]);
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  float wsum = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < ns; ++s) {
+      const float ls = p.ws_lse[static_cast<size_t>(s) * n_rows + row];
+      if (ls == -INFINITY) continue;
+      const float w = expf(ls - mx);
+      wsum += w;
+      const float* src = p.ws_o + (static_cast<size_t>(s) * n_rows + row) * D + lane * E;
+      if constexpr (E == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        acc[0] = fmaf(w, v.x, acc[0]);
+        acc[1] = fmaf(w, v.y, acc[1]);
+        acc[2] = fmaf(w, v.z, acc[2]);
+        acc[3] = fmaf(w, v.w, acc[3]);
+      } else {
+        const float2 v = *reinterpret_cast<const float2*>(src);
+        acc[0] = fmaf(w, v.x, acc[0]);
+        acc[1] = fmaf(w, v.y, acc[1]);
+      }
+    }
+  }
+  const float inv = wsum > 0.f ? 1.0f / wsum : 0.f;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  T* dst = reinterpret_cast<T*>(p.o) + row * D + lane * E;
+  uint32_t h[E / 2];
+#pragma unroll
+  for (int e = 0; e < E / 2; ++e) h[e] = pack2<BF16>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+  if constexpr (E == 4) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(h[0], h[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = h[0];
+  }
+  if (lane == 0 && p.lse != nullptr) p.lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
 }
 
 }  // namespace
@@ -686,9 +797,22 @@ static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream
 }
 
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
-  const int grid = p.n_qpairs * p.B * p.Hq;
+  const int grid = p.n_qpairs * p.B * p.heads * p.n_splits;
   if (head_dim == 64) return bf16 ? launch_impl<64, true>(p, grid, stream) : launch_impl<64, false>(p, grid, stream);
   return bf16 ? launch_impl<128, true>(p, grid, stream) : launch_impl<128, false>(p, grid, stream);
+}
+
+cudaError_t launch_combine(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
+  const long long n_rows = static_cast<long long>(p.B) * p.heads * p.Nq;
+  const unsigned grid = static_cast<unsigned>((n_rows + 7) / 8);
+  if (head_dim == 64) {
+    if (bf16) fa_combine_kernel<64, true><<<grid, 256, 0, stream>>>(p);
+    else fa_combine_kernel<64, false><<<grid, 256, 0, stream>>>(p);
+  } else {
+    if (bf16) fa_combine_kernel<128, true><<<grid, 256, 0, stream>>>(p);
+    else fa_combine_kernel<128, false><<<grid, 256, 0, stream>>>(p);
+  }
+  return cudaGetLastError();
 }
 
 int smem_bytes_for(int head_dim) {

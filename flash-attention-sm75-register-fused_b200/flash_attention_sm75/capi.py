@@ -16,6 +16,9 @@ c_vp, c_int, c_float, c_bool = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ct
 SIGNATURES = {
     "fa_fwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float,
                        c_int, c_int, c_vp]),
+    "fa_fwd_kvcache": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
+                               c_int, c_float, c_int, c_int, c_vp, ctypes.c_size_t, c_vp]),
+    "fa_fwd_kvcache_workspace_bytes": (ctypes.c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "launch_flash_attention_forward": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
                                               c_float, c_bool]),
     "launch_flash_attention_forward_scalar": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
@@ -75,3 +78,31 @@ def fa_fwd(q, k, v, o, lse=None, causal=False, scale=None, stream=None):
     dtype = 1 if q.dtype == torch.bfloat16 else 0
     return load().fa_fwd(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), B, Hq, Hkv, N, d,
                          float(scale), int(bool(causal)), dtype, stream_ptr(stream))
+
+
+CAUSAL_NONE, CAUSAL_BOTTOM_RIGHT, CAUSAL_TOP_LEFT = 0, 1, 2
+
+
+def fa_fwd_kvcache(q, k, v, o, lse=None, causal=CAUSAL_NONE, scale=None, stream=None,
+                   workspace=True):
+    """Call fa_fwd_kvcache on torch CUDA tensors (Q/O [B, Hq, Nq, d], K/V
+    [B, Hkv, Nk, d]); ``workspace=True`` allocates the split workspace the
+    library asks for, ``None`` runs unsplit.  Returns the status."""
+    import math
+    import torch
+    B, Hq, Nq, d = q.shape
+    Hkv, Nk = k.shape[1], k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    lib = load()
+    ws, nbytes = None, 0
+    if workspace is True:
+        nbytes = lib.fa_fwd_kvcache_workspace_bytes(B, Hq, Hkv, Nq, Nk, d)
+        if nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    elif workspace is not None:
+        ws, nbytes = workspace, workspace.numel() * workspace.element_size()
+    return lib.fa_fwd_kvcache(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), B, Hq, Hkv, Nq, Nk, d,
+                              float(scale), int(causal), dtype, ptr(ws), nbytes,
+                              stream_ptr(stream))

@@ -19,6 +19,7 @@
 #define FA_B200_H
 
 #include <stdbool.h>
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -44,6 +45,14 @@ enum {
 
 enum { FA_DTYPE_F16 = 0, FA_DTYPE_BF16 = 1 };
 
+/* Causal alignment for fa_fwd_kvcache (fa_fwd takes 0/1; for Nq == Nk both
+ * alignments are the reference's top-left mask, attention_ref.py:33-40). */
+enum {
+  FA_CAUSAL_NONE = 0,
+  FA_CAUSAL_BOTTOM_RIGHT = 1, /* key j visible to query i iff j <= i + Nk - Nq (KV cache) */
+  FA_CAUSAL_TOP_LEFT = 2      /* key j visible to query i iff j <= i (SDPA is_causal) */
+};
+
 /* Test hooks (fa_set_debug_flags). */
 enum { FA_DEBUG_SKIP_Q_LOAD = 1 /* producer never loads Q: the MMA warp's wait must time out */ };
 
@@ -60,6 +69,27 @@ enum { FA_DEBUG_SKIP_Q_LOAD = 1 /* producer never loads Q: the MMA warp's wait m
  */
 int fa_fwd(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
            int Hkv, int N, int head_dim, float scale, int causal, int dtype, void* stream);
+
+/*
+ * fa_fwd_kvcache — attention of Nq new queries against Nk cached keys
+ * (decode: Nq = 1; chunked prefill: Nq < Nk).  Q/O are [B, Hq, Nq, d], K/V
+ * [B, Hkv, Nk, d], LSE [B, Hq, Nq]; `causal` is an FA_CAUSAL_* value.  Rows
+ * that see no key (bottom-right with Nq > Nk) get O = 0 and LSE = -inf.
+ * When the call alone would not fill the GPU, the key range is split across
+ * CTAs and merged by a second kernel; that needs `workspace` (16-byte aligned)
+ * of at least fa_fwd_kvcache_workspace_bytes() bytes, otherwise (NULL or
+ * smaller) the call runs unsplit.  Asynchronous on `stream`.
+ *
+ * No reference counterpart: the reference's HF patch sends these calls to
+ * PyTorch SDPA (reference src/flash_attention_sm75/llama_attention_replacement.py:63-65,
+ * reason "kvcache_decode").
+ */
+int fa_fwd_kvcache(const void* Q, const void* K, const void* V, void* O, float* lse, int B,
+                   int Hq, int Hkv, int Nq, int Nk, int head_dim, float scale, int causal,
+                   int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes fa_fwd_kvcache needs to split this problem (0: no split). */
+size_t fa_fwd_kvcache_workspace_bytes(int B, int Hq, int Hkv, int Nq, int Nk, int head_dim);
 
 /* ---- reference-compatible launchers (void, fp16, blocking) ----
  * Same signatures and conventions as the reference: errors are printed to

@@ -71,14 +71,19 @@ def expand_kv_for_gqa(h_q: int, K: torch.Tensor, V: torch.Tensor):
 
 
 def attention_fp32(Q, K, V, causal=False, scale=None, rows: Optional[torch.Tensor] = None,
-                   key_chunk: int = 4096):
+                   key_chunk: int = 4096, causal_offset: int = 0):
     """fp32 attention and LSE on the CPU.
 
-    Q [B, Hq, N, d]; K, V [B, Hkv, N, d] (GQA by head mapping).  ``rows`` is an
-    optional 1-D LongTensor of query indices evaluated (all if None).
+    Q [B, Hq, Nq, d]; K, V [B, Hkv, Nk, d] (GQA by head mapping; Nk = Nq for
+    the reference's square case).  Causal: key j is visible to query i iff
+    j <= i + causal_offset (0 = the reference's top-left mask,
+    attention_ref.py:33-40; Nk - Nq = bottom-right, the KV-cache convention).
+    Rows that see no key get O = 0 and LSE = -inf.  ``rows`` is an optional
+    1-D LongTensor of query indices evaluated (all if None).
     Returns (O fp32 [B, Hq, R, d], LSE fp32 [B, Hq, R]).
     """
     B, Hq, N, d = Q.shape
+    Nk = K.size(2)
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     K, V = expand_kv_for_gqa(Hq, K, V)
@@ -89,12 +94,12 @@ def attention_fp32(Q, K, V, causal=False, scale=None, rows: Optional[torch.Tenso
     m = torch.full((B, Hq, R), float("-inf"))
     l = torch.zeros((B, Hq, R))
     acc = torch.zeros((B, Hq, R, d))
-    for k0 in range(0, N, key_chunk):
-        k1 = min(N, k0 + key_chunk)
+    for k0 in range(0, Nk, key_chunk):
+        k1 = min(Nk, k0 + key_chunk)
         S = torch.matmul(Qf, K[:, :, k0:k1, :].float().transpose(-2, -1)) * scale
         if causal:
             key = torch.arange(k0, k1)
-            S.masked_fill_(key[None, :] > q_idx[:, None], float("-inf"))
+            S.masked_fill_(key[None, :] > q_idx[:, None] + causal_offset, float("-inf"))
         m_new = torch.maximum(m, S.amax(dim=-1))
         m_safe = torch.where(torch.isinf(m_new), torch.zeros_like(m_new), m_new)
         alpha = torch.exp(m - m_safe)
@@ -102,9 +107,15 @@ def attention_fp32(Q, K, V, causal=False, scale=None, rows: Optional[torch.Tenso
         l = l * alpha + P.sum(dim=-1)
         acc = acc * alpha[..., None] + torch.matmul(P, V[:, :, k0:k1, :].float())
         m = m_new
-    O = acc / l[..., None]
+    O = torch.where(l[..., None] > 0, acc / l.clamp_min(1e-38)[..., None], torch.zeros_like(acc))
     lse = torch.where(l > 0, m + torch.log(l), torch.full_like(l, float("-inf")))
     return O, lse
+
+
+def kvcache_offset(Nq: int, Nk: int, mode: int) -> int:
+    """Causal offset of fa_fwd_kvcache's FA_CAUSAL_* modes (1 bottom-right,
+    2 top-left; 0 = not causal)."""
+    return Nk - Nq if mode == 1 else 0
 
 
 # ------------------------------------------------------------------ inputs

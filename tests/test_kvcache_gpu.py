@@ -1,0 +1,126 @@
+"""Parity of fa_fwd_kvcache (Nq != Nk: decode, chunked prefill) against the CPU
+oracle, through the C ABI.
+
+Tolerance as for fa_fwd: |O - O_ref| <= 2e-3 + 1e-2*|O_ref| (fp16; bf16
+1.6e-2 + 2e-2*|ref|), LSE within 1e-4.  Covers GQA row packing (Nq <= 128),
+split-KV with the combine kernel (workspace given) and without (workspace
+None), both causal alignments, ragged Nk, and rows that see no key.
+"""
+import pytest
+import torch
+
+from oracle import attention_oracle as orc
+from tests import abi_ctypes as abi
+
+pytestmark = pytest.mark.gpu
+
+BF16_ATOL, BF16_RTOL = 1.6e-2, 2e-2
+
+
+def _inputs(B, Hq, Hkv, Nq, Nk, d, seed, dtype=torch.float16):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, Nq, d, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, Nk, d, generator=g).to(dtype)
+    v = torch.randn(B, Hkv, Nk, d, generator=g).to(dtype)
+    return q, k, v
+
+
+def run(q, k, v, mode, workspace=True):
+    o = torch.empty_like(q)
+    lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
+    rc = abi.fa_fwd_kvcache(q, k, v, o, lse, causal=mode, workspace=workspace)
+    assert rc == 0, abi.load().fa_error_string(rc)
+    torch.cuda.synchronize()
+    assert abi.load().fa_device_status(1) == 0
+    return o, lse
+
+
+def parity(B, Hq, Hkv, Nq, Nk, d, mode, seed=0, dtype=torch.float16, workspace=True):
+    q, k, v = _inputs(B, Hq, Hkv, Nq, Nk, d, seed, dtype)
+    o, lse = run(q.cuda(), k.cuda(), v.cuda(), mode, workspace)
+    ref_o, ref_lse = orc.attention_fp32(q, k, v, causal=mode != 0,
+                                        causal_offset=orc.kvcache_offset(Nq, Nk, mode))
+    o, lse = o.cpu(), lse.cpu()
+    if dtype == torch.bfloat16:
+        r = orc.check(o, ref_o, atol=BF16_ATOL, rtol=BF16_RTOL)
+    else:
+        r = orc.check(o, ref_o)
+    assert r["ok"], r
+    finite = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse), finite)
+    assert orc.check_lse(lse[finite], ref_lse[finite])["ok"]
+    return o, lse
+
+
+DECODE = [
+    # B, Hq, Hkv, Nq, Nk, d
+    (1, 32, 8, 1, 4096, 128),   # GQA 4: packed, split
+    (4, 8, 1, 1, 1000, 128),    # MQA 8, ragged Nk
+    (2, 16, 16, 1, 2048, 64),   # MHA decode
+    (1, 8, 2, 1, 77, 64),       # single ragged tile
+    (1, 4, 4, 1, 1, 128),       # one key
+]
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("case", DECODE, ids=[str(c) for c in DECODE])
+def test_decode(sm100, case, mode):
+    parity(*case, mode=mode, seed=sum(case))
+
+
+CHUNKED = [
+    (1, 8, 2, 7, 300, 128),     # packed rows (G*Nq = 28)
+    (2, 4, 1, 32, 1024, 64),    # packed, G*Nq = 128
+    (1, 4, 2, 96, 640, 128),    # packed, G*Nq = 192 (two tiles)
+    (1, 4, 2, 129, 700, 128),   # unpacked (Nq > 128)
+    (1, 2, 2, 300, 1000, 64),   # MHA chunk
+    (1, 8, 8, 256, 256, 128),   # square: same as fa_fwd
+]
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("case", CHUNKED, ids=[str(c) for c in CHUNKED])
+def test_chunked_prefill(sm100, case, mode):
+    parity(*case, mode=mode, seed=sum(case) + mode)
+
+
+def test_rows_without_keys(sm100):
+    """Bottom-right with Nq > Nk: the first rows see nothing -> O = 0, LSE = -inf."""
+    o, lse = parity(1, 4, 2, 200, 72, 128, mode=1, seed=5)
+    assert torch.equal(o[:, :, :128], torch.zeros_like(o[:, :, :128]))
+
+
+def test_bf16_decode_and_chunk(sm100):
+    parity(2, 16, 4, 1, 3000, 128, mode=0, seed=1, dtype=torch.bfloat16)
+    parity(1, 8, 2, 50, 600, 64, mode=1, seed=2, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", [(1, 32, 8, 1, 8192, 128), (1, 8, 2, 16, 4096, 64)])
+def test_split_matches_unsplit(sm100, case):
+    """The split-KV path (workspace) and the single-CTA path agree to rounding."""
+    q, k, v = (t.cuda() for t in _inputs(*case, seed=11))
+    lib = abi.load()
+    assert lib.fa_fwd_kvcache_workspace_bytes(*case) > 0  # this shape is split
+    o1, l1 = run(q, k, v, 0, workspace=True)
+    o2, l2 = run(q, k, v, 0, workspace=None)
+    assert (o1.float() - o2.float()).abs().max().item() <= 2e-3
+    assert (l1 - l2).abs().max().item() <= 1e-4
+
+
+def test_square_matches_fa_fwd_bitwise(sm100):
+    """Nq == Nk > 128 runs the same tiles as fa_fwd."""
+    q, k, v = (t.cuda() for t in _inputs(2, 8, 2, 384, 384, 128, seed=4))
+    o1, l1 = run(q, k, v, 1, workspace=None)
+    o2 = torch.empty_like(q)
+    l2 = torch.empty_like(l1)
+    assert abi.fa_fwd(q, k, v, o2, l2, causal=True) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+def test_small_workspace_runs_unsplit(sm100):
+    q, k, v = (t.cuda() for t in _inputs(1, 32, 8, 1, 4096, 128, seed=6))
+    tiny = torch.empty(64, dtype=torch.uint8, device="cuda")
+    o1, l1 = run(q, k, v, 0, workspace=tiny)
+    o2, l2 = run(q, k, v, 0, workspace=None)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
