@@ -362,6 +362,7 @@ def main():
                       f"fp32 torch CPU oracle, {cpu_s:.1f} s"}
         if world == 1:
             line["configs"] = other_configs(lib, abi, dtype, dev)
+            line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
     elif rank == 0:
         line["e2e"] = None
     if world > 1:
@@ -419,6 +420,59 @@ def other_configs(lib, abi, dtype, dev):
         ms = time_steps(fn, n, s) / n
         out[name] = {"tflops": round(c.flops / ms / 1e9, 1), "us": round(ms * 1e3, 2),
                      "gbs": round(c.min_bytes / (ms * 1e-3) / 1e9, 1)}
+    return out
+
+
+# fa_fwd_kvcache workloads (decode and chunked prefill; no reference counterpart):
+# name -> (B, Hq, Hkv, Nq, Nk, d, causal mode)
+KVCACHE_CONFIGS = {
+    "decode_b8_gqa4_8k": (8, 32, 8, 1, 8192, 128, 0),
+    "decode_b1_gqa4_64k": (1, 32, 8, 1, 65536, 128, 0),
+    "decode_b16_mha_4k_d64": (16, 16, 16, 1, 4096, 64, 0),
+    "chunk_512_of_8k_causal": (1, 32, 8, 512, 8192, 128, 1),
+}
+
+
+def kvcache_configs(lib, abi, dtype, dev):
+    """Kernel-only time of fa_fwd_kvcache on seeded N(0,1) inputs with a split
+    workspace.  Decode is HBM-bound: GB/s counts Q, K, V, O and LSE once
+    (K/V > L2, so no flush is needed) and ``hbm_frac`` divides by the measured
+    copy bandwidth in MEASURED_PEAKS.json."""
+    import torch
+    peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    out = {}
+    el = 2
+    for name, (B, Hq, Hkv, Nq, Nk, d, mode) in KVCACHE_CONFIGS.items():
+        g = torch.Generator(device=dev).manual_seed(7)
+        q = torch.randn(B, Hq, Nq, d, device=dev, dtype=torch.float32, generator=g).to(dtype)
+        k = torch.randn(B, Hkv, Nk, d, device=dev, dtype=torch.float32, generator=g).to(dtype)
+        v = torch.randn(B, Hkv, Nk, d, device=dev, dtype=torch.float32, generator=g).to(dtype)
+        o = torch.empty_like(q)
+        lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+        nbytes = lib.fa_fwd_kvcache_workspace_bytes(B, Hq, Hkv, Nq, Nk, d)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+        s = torch.cuda.current_stream(dev)
+        args = (abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), abi.ptr(lse), B, Hq, Hkv, Nq, Nk, d,
+                1.0 / math.sqrt(d), mode, 1 if dtype == torch.bfloat16 else 0, abi.ptr(ws), nbytes,
+                abi.stream_ptr(s))
+        fn = lambda: lib.fa_fwd_kvcache(*args)
+        assert fn() == 0
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        n = 200
+        ms = time_steps(fn, n, s) / n
+        byt = (2 * B * Hkv * Nk * d + 2 * B * Hq * Nq * d) * el + B * Hq * Nq * 4
+        if mode:  # causal chunk: the keys a query row sees, averaged
+            flops = 4.0 * B * Hq * d * sum(min(Nk, i + 1 + Nk - Nq) for i in range(Nq))
+        else:
+            flops = 4.0 * B * Hq * Nq * Nk * d
+        out[name] = {"us": round(ms * 1e3, 2), "gbs": round(byt / (ms * 1e-3) / 1e9, 1),
+                     "hbm_frac": round(byt / (ms * 1e-3) / 1e9 / hbm, 3),
+                     "tflops": round(flops / ms / 1e9, 1), "splits_workspace_bytes": int(nbytes)}
+        del q, k, v, o, lse, ws
     return out
 
 

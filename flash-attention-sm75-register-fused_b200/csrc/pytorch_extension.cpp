@@ -5,7 +5,8 @@
 // current CUDA stream instead of the legacy stream + cudaDeviceSynchronize.
 //
 // Additions: native GQA (K/V may have fewer heads than Q), bf16 inputs,
-// flash_attention_forward_lse returning (O, LSE), and diagnostics.
+// flash_attention_forward_lse returning (O, LSE), flash_attention_forward_kvcache
+// (Nq != Nk: decode and chunked prefill), and diagnostics.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -121,6 +122,48 @@ torch::Tensor naive_attention_forward(torch::Tensor Q, torch::Tensor K, torch::T
   return O;
 }
 
+// Nq new queries against Nk cached keys (decode / chunked prefill); causal is
+// an FA_CAUSAL_* mode.  The split-KV workspace comes from PyTorch's caching
+// allocator on the current stream.  Returns (O, LSE).
+std::tuple<torch::Tensor, torch::Tensor> flash_attention_forward_kvcache(
+    torch::Tensor Q, torch::Tensor K, torch::Tensor V, int64_t causal, float scale) {
+  check_tensor(Q, "Q", true);
+  check_tensor(K, "K", true);
+  check_tensor(V, "V", true);
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype(), "Q, K, V must share a dtype");
+  TORCH_CHECK(Q.device() == K.device() && Q.device() == V.device(),
+              "Q, K, V must be on the same device");
+  TORCH_CHECK(Q.size(0) == K.size(0), "batch mismatch");
+  TORCH_CHECK(Q.size(3) == K.size(3), "head_dim mismatch");
+  TORCH_CHECK(K.sizes() == V.sizes(), "K and V must have identical shapes");
+  const auto head_dim = Q.size(3);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  TORCH_CHECK(causal >= FA_CAUSAL_NONE && causal <= FA_CAUSAL_TOP_LEFT, "bad causal mode ", causal);
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && Q.size(1) <= INT32_MAX && Q.size(2) <= INT32_MAX &&
+                  K.size(2) <= INT32_MAX,
+              "size exceeds int32");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  const int B = static_cast<int>(Q.size(0)), Hq = static_cast<int>(Q.size(1));
+  const int Hkv = static_cast<int>(K.size(1)), Nq = static_cast<int>(Q.size(2));
+  const int Nk = static_cast<int>(K.size(2)), d = static_cast<int>(head_dim);
+  auto O = torch::empty_like(Q);
+  auto lse = torch::empty({Q.size(0), Q.size(1), Q.size(2)}, Q.options().dtype(torch::kFloat32));
+  const size_t ws_bytes = fa_fwd_kvcache_workspace_bytes(B, Hq, Hkv, Nq, Nk, d);
+  torch::Tensor ws;
+  if (ws_bytes > 0)
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)}, Q.options().dtype(torch::kUInt8));
+  const int rc = fa_fwd_kvcache(
+      Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse.data_ptr<float>(), B, Hq, Hkv,
+      Nq, Nk, d, scale, static_cast<int>(causal),
+      Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16,
+      ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_forward_kvcache: ", fa_error_string(rc));
+  return {O, lse};
+}
+
 int device_status(bool reset) { return fa_device_status(reset ? 1 : 0); }
 
 }  // namespace
@@ -132,6 +175,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attention_forward_wmma_qk", &flash_attention_forward_wmma_qk);
   m.def("flash_attention_forward_lse", &flash_attention_forward_lse,
         "Returns (O, LSE) with LSE fp32 [B, Hq, N]");
+  m.def("flash_attention_forward_kvcache", &flash_attention_forward_kvcache,
+        "O, LSE of Nq queries against Nk cached keys; causal: 0 none, 1 bottom-right, 2 top-left");
   m.def("device_status", &device_status, pybind11::arg("reset") = false,
         "Error code recorded by the in-kernel watchdog (0 = none)");
   m.def("set_watchdog_ns", &fa_set_watchdog_ns);

@@ -2,9 +2,9 @@
 
 Same public surface as the reference package
 (src/flash_attention_sm75/__init__.py:1-4): ``flash_attention_forward`` and
-``__version__``.
+``__version__``; ``flash_attention_forward_kvcache`` (Nq != Nk) is an addition.
 """
-from .ops import flash_attention_forward
+from .ops import flash_attention_forward, flash_attention_forward_kvcache
 
 __version__ = "0.1.0"
-__all__ = ["flash_attention_forward"]
+__all__ = ["flash_attention_forward", "flash_attention_forward_kvcache"]

@@ -12,19 +12,25 @@ the same order and with the same fallback reason names:
 ``has_attn_mask``, ``kvcache_decode``.  Differences: bf16 queries are also
 eligible (``not_fp16`` then means "neither fp16 nor bf16"); GQA calls (K/V with
 fewer heads, HF's ``enable_gqa=True``) go to the kernel's native head mapping;
-a head count that does not divide falls back with ``gqa_heads``.
+a head count that does not divide falls back with ``gqa_heads``.  Calls with a
+query shorter than the keys (KV-cache decode, chunked prefill) are served by
+``flash_attention_forward_kvcache`` with SDPA's own causal rule for that case
+(top-left: query i sees keys j <= i); ``apply_patch(kvcache=False)`` restores
+the reference behaviour of sending them to SDPA with reason ``kvcache_decode``.
 """
 import torch
 import torch.nn.functional as F
 
-from .ops import flash_attention_forward
+from .ops import flash_attention_forward, flash_attention_forward_kvcache
 
 _original_sdpa = F.scaled_dot_product_attention
 _patch_active = False
+_route_kvcache = True
 
 _stats = {
     "total": 0,
     "flash": 0,
+    "flash_kvcache": 0,
     "fallback": 0,
     "fallback_reasons": {},
 }
@@ -35,7 +41,7 @@ def _record_fallback(reason: str):
     _stats["fallback_reasons"][reason] = _stats["fallback_reasons"].get(reason, 0) + 1
 
 
-def _ineligible_reason(query, key, dropout_p, attn_mask):
+def _ineligible_reason(query, key, value, dropout_p, attn_mask):
     if not query.is_cuda:
         return "not_cuda"
     if query.dtype not in (torch.float16, torch.bfloat16):
@@ -48,12 +54,14 @@ def _ineligible_reason(query, key, dropout_p, attn_mask):
         return "dropout"
     if attn_mask is not None:
         return "has_attn_mask"
-    if query.size(2) != key.size(2):
+    if query.size(2) != key.size(2) and not _route_kvcache:
         # KV-cache decode / chunked prefill: Q is shorter than K
         return "kvcache_decode"
     if key.dim() != 4 or key.size(1) == 0 or query.size(1) % key.size(1) != 0:
         return "gqa_heads"
     if key.dtype != query.dtype or key.size(-1) != query.size(-1):
+        return "not_fp16"
+    if value.dim() != 4 or value.shape != key.shape or value.dtype != key.dtype:
         return "not_fp16"
     return None
 
@@ -61,17 +69,23 @@ def _ineligible_reason(query, key, dropout_p, attn_mask):
 def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None,
                   **kwargs):
     _stats["total"] += 1
-    reason = _ineligible_reason(query, key, dropout_p, attn_mask)
+    reason = _ineligible_reason(query, key, value, dropout_p, attn_mask)
     if reason is not None:
         _record_fallback(reason)
         return _original_sdpa(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
                               is_causal=is_causal, scale=scale, **kwargs)
     _stats["flash"] += 1
+    if query.size(2) != key.size(2):
+        _stats["flash_kvcache"] += 1
+        return flash_attention_forward_kvcache(query, key, value, causal=is_causal, scale=scale,
+                                               causal_alignment="top_left")
     return flash_attention_forward(query, key, value, causal=is_causal, scale=scale)
 
 
-def apply_patch():
-    global _patch_active
+def apply_patch(kvcache: bool = True):
+    """Patch SDPA; ``kvcache=False`` keeps Nq != Nk calls on the original SDPA."""
+    global _patch_active, _route_kvcache
+    _route_kvcache = bool(kvcache)
     if _patch_active:
         return
     import torch.nn.functional as _F
@@ -97,6 +111,7 @@ def patch_stats():
 def reset_stats():
     _stats["total"] = 0
     _stats["flash"] = 0
+    _stats["flash_kvcache"] = 0
     _stats["fallback"] = 0
     _stats["fallback_reasons"].clear()
 

@@ -16,6 +16,9 @@ Differences that a caller can observe only as speed or as extra options:
   expansion (ops.py:24-26) — so K/V are never copied.
 * bf16 inputs are accepted in addition to fp16.
 * ``return_lse=True`` also returns the fp32 log-sum-exp ``[B, Hq, N]``.
+* ``flash_attention_forward_kvcache`` (no reference counterpart) serves
+  ``Nq != Nk`` — KV-cache decode and chunked prefill — with bottom-right or
+  top-left causal alignment.
 
 There is no CPU path: the CUDA extension must load, or the import fails.
 """
@@ -104,3 +107,42 @@ def flash_attention_forward(Q, K, V, causal=False, scale=None, return_lse=False)
         scale = 1.0 / math.sqrt(head_dim)
 
     return FlashAttentionSM75Function.apply(Q, K, V, causal, scale, return_lse)
+
+
+_CAUSAL_MODES = {"bottom_right": 1, "top_left": 2}
+
+
+def flash_attention_forward_kvcache(Q, K, V, causal=False, scale=None, return_lse=False,
+                                    causal_alignment="bottom_right"):
+    """Attention of ``Nq`` new queries against ``Nk`` cached keys (decode,
+    chunked prefill); forward only.
+
+    Args:
+        Q: [B, H_q,  N_q, D]  float16 / bfloat16, cuda
+        K: [B, H_kv, N_k, D]  same dtype, H_kv divides H_q
+        V: [B, H_kv, N_k, D]  same dtype
+        causal: bool
+        scale: float (default 1/sqrt(D))
+        return_lse: also return LSE [B, H_q, N_q] fp32 (natural log)
+        causal_alignment: "bottom_right" (query i sees keys j <= i + N_k - N_q,
+            the KV-cache convention) or "top_left" (j <= i, the rule of
+            ``F.scaled_dot_product_attention(is_causal=True)`` for N_q != N_k)
+
+    Rows that see no key (bottom-right with N_q > N_k) return O = 0, LSE = -inf.
+    """
+    if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
+        raise ValueError("Q, K, V must be 4D [B, H, N, D]")
+    head_dim = Q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    if causal and causal_alignment not in _CAUSAL_MODES:
+        raise ValueError(f"causal_alignment must be one of {sorted(_CAUSAL_MODES)}")
+    _check_gqa(Q.size(1), K.size(1))
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    mode = _CAUSAL_MODES[causal_alignment] if causal else 0
+    out, lse = _C.flash_attention_forward_kvcache(Q.contiguous(), K.contiguous(), V.contiguous(),
+                                                  mode, float(scale))
+    return (out, lse) if return_lse else out

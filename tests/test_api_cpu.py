@@ -8,8 +8,24 @@ from flash_attention_sm75 import ops
 
 
 def test_public_surface():
-    assert fa.__all__ == ["flash_attention_forward"]
+    # the reference's surface (src/flash_attention_sm75/__init__.py:1-4) plus one addition
+    assert fa.__all__ == ["flash_attention_forward", "flash_attention_forward_kvcache"]
     assert isinstance(fa.__version__, str)
+
+
+def test_kvcache_argument_errors():
+    q = torch.zeros(1, 4, 1, 64, dtype=torch.float16)
+    k = torch.zeros(1, 2, 16, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="4D"):
+        fa.flash_attention_forward_kvcache(q[0], k, k)
+    with pytest.raises(RuntimeError, match="supports head_dim=64 or 128"):
+        fa.flash_attention_forward_kvcache(torch.zeros(1, 4, 1, 96), k, k)
+    with pytest.raises(ValueError, match="causal_alignment"):
+        fa.flash_attention_forward_kvcache(q, k, k, causal=True, causal_alignment="middle")
+    with pytest.raises(RuntimeError, match="not divisible"):
+        fa.flash_attention_forward_kvcache(torch.zeros(1, 3, 1, 64), k, k)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fa.flash_attention_forward_kvcache(q, k, k)  # CPU tensors are rejected by the binding
 
 
 def test_rejects_non_4d():

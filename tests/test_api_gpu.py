@@ -86,19 +86,36 @@ def test_naive_attention(sm100, N, causal):
 
 def test_llama_patch_on_gpu(sm100):
     from flash_attention_sm75 import llama_attention_replacement as patch
-    patch.reset_stats()
     q, k, v = (t.cuda() for t in _inputs(1, 8, 2, 64, 64, True))
+    qd = q[:, :, -3:].contiguous()  # 3 new queries against 64 cached keys
+    patch.reset_stats()
     patch.apply_patch()
     try:
         out = F.scaled_dot_product_attention(q, k, v, is_causal=True)
-        dec = F.scaled_dot_product_attention(q[:, :, :1], k, v, enable_gqa=True)  # decode: fallback
+        dec = F.scaled_dot_product_attention(qd[:, :, :1], k, v, enable_gqa=True)  # decode
+        chk = F.scaled_dot_product_attention(qd, k, v, is_causal=True, enable_gqa=True)
     finally:
         patch.remove_patch()
     ref, _ = orc.attention_fp32(q.cpu(), k.cpu(), v.cpu(), causal=True)
     assert orc.check(out.cpu(), ref)["ok"]
     s = patch.patch_stats()
-    assert s["flash"] == 1 and s["fallback_reasons"] == {"kvcache_decode": 1}
-    assert dec.shape == (1, 8, 1, 64)
+    assert s["flash"] == 3 and s["flash_kvcache"] == 2 and s["fallback"] == 0
+    # decode: all keys; chunk with is_causal: SDPA's top-left rule (key j <= query i)
+    ref_d, _ = orc.attention_fp32(qd[:, :, :1].cpu(), k.cpu(), v.cpu())
+    assert orc.check(dec.cpu(), ref_d)["ok"]
+    ref_c, _ = orc.attention_fp32(qd.cpu(), k.cpu(), v.cpu(), causal=True, causal_offset=0)
+    assert orc.check(chk.cpu(), ref_c)["ok"]
+    assert torch.allclose(chk.float(), patch._original_sdpa(qd, k, v, is_causal=True,
+                                                            enable_gqa=True).float(),
+                          atol=1e-2, rtol=1e-2)
+    # reference behaviour on request: decode goes to SDPA
+    patch.reset_stats()
+    patch.apply_patch(kvcache=False)
+    try:
+        F.scaled_dot_product_attention(qd[:, :, :1], k, v, enable_gqa=True)
+    finally:
+        patch.remove_patch()
+    assert patch.patch_stats()["fallback_reasons"] == {"kvcache_decode": 1}
 
 
 def test_current_stream_semantics(sm100):

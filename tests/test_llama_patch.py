@@ -29,6 +29,7 @@ def test_reason_order_matches_reference():
     class Fake:
         def __init__(self, cuda=True, dtype=torch.float16, shape=(1, 2, 8, 64)):
             self.is_cuda, self.dtype, self._s = cuda, dtype, shape
+            self.shape = torch.Size(shape)
 
         def dim(self):
             return len(self._s)
@@ -36,14 +37,23 @@ def test_reason_order_matches_reference():
         def size(self, i):
             return self._s[i]
 
-    r = patch._ineligible_reason
+    def r(q, k, dropout, mask):
+        return patch._ineligible_reason(q, k, k, dropout, mask)
+
     assert r(Fake(cuda=False), Fake(), 0.0, None) == "not_cuda"
     assert r(Fake(dtype=torch.float32), Fake(), 0.0, None) == "not_fp16"
     assert r(Fake(shape=(2, 8, 64)), Fake(), 0.0, None) == "not_4d"
     assert r(Fake(shape=(1, 2, 8, 96)), Fake(), 0.0, None) == "head_dim_unsupported"
     assert r(Fake(), Fake(), 0.1, None) == "dropout"
     assert r(Fake(), Fake(), 0.0, object()) == "has_attn_mask"
-    assert r(Fake(shape=(1, 2, 1, 64)), Fake(shape=(1, 2, 8, 64)), 0.0, None) == "kvcache_decode"
+    # Nq != Nk: served by the kv-cache kernel, or (kvcache=False) the reference's fallback
+    assert r(Fake(shape=(1, 2, 1, 64)), Fake(shape=(1, 2, 8, 64)), 0.0, None) is None
+    saved = patch._route_kvcache
+    patch._route_kvcache = False
+    try:
+        assert r(Fake(shape=(1, 2, 1, 64)), Fake(shape=(1, 2, 8, 64)), 0.0, None) == "kvcache_decode"
+    finally:
+        patch._route_kvcache = saved
     assert r(Fake(shape=(1, 6, 8, 64)), Fake(shape=(1, 4, 8, 64)), 0.0, None) == "gqa_heads"
     assert r(Fake(), Fake(), 0.0, None) is None
     assert r(Fake(dtype=torch.bfloat16), Fake(dtype=torch.bfloat16), 0.0, None) is None
