@@ -147,6 +147,7 @@ int sm_count() {
 // CTAs per SM run; a combine kernel merges the splits.
 struct Plan {
   bool pack = false;
+  bool dual = false;  // one Q tile: the two softmax groups split the key tiles
   int heads = 0, rows = 0, group = 1, pos_mod = 1, n_qpairs = 0, n_kv_tiles = 0;
   int n_splits = 1, tiles_per_split = 0;
   size_t ws_o_bytes = 0, ws_bytes = 0;
@@ -166,16 +167,22 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   const long long units = static_cast<long long>(k.n_qpairs) * B * k.heads;
   const int sms = sm_count();
   if (allow_split && units < sms && k.n_kv_tiles > 1) {
+    // about two CTAs per SM: measured faster than one wave of longer CTAs,
+    // which leaves SMs idle
     long long want = (2LL * sms + units - 1) / units;
     if (want > k.n_kv_tiles) want = k.n_kv_tiles;
     if (want > 64) want = 64;
     k.tiles_per_split = static_cast<int>((k.n_kv_tiles + want - 1) / want);
     k.n_splits = (k.n_kv_tiles + k.tiles_per_split - 1) / k.tiles_per_split;
   }
-  if (k.n_splits > 1) {
+  // Queries that fit one 128-row tile leave the CTA's second softmax group
+  // idle; in dual mode the two groups take halves of the CTA's key tiles.
+  k.dual = allow_split && k.rows <= 128 && k.n_kv_tiles >= 2;
+  if (k.n_splits > 1 || k.dual) {
+    const size_t slots = static_cast<size_t>(k.n_splits) * (k.dual ? 2 : 1);
     const size_t rows_total = static_cast<size_t>(B) * k.heads * k.rows;
-    k.ws_o_bytes = static_cast<size_t>(k.n_splits) * rows_total * d * sizeof(float);
-    k.ws_bytes = k.ws_o_bytes + static_cast<size_t>(k.n_splits) * rows_total * sizeof(float);
+    k.ws_o_bytes = slots * rows_total * d * sizeof(float);
+    k.ws_bytes = k.ws_o_bytes + slots * rows_total * sizeof(float);
   }
   return k;
 }
@@ -213,7 +220,8 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
                      int dtype, void* workspace, size_t workspace_bytes, void* stream) {
   const bool bf16 = dtype == FA_DTYPE_BF16;
   Plan k = make_plan(B, Hq, Hkv, Nq, Nk, head_dim, workspace != nullptr);
-  if (k.n_splits > 1 && (workspace_bytes < k.ws_bytes || !aligned16(workspace)))
+  const bool partial = k.n_splits > 1 || k.dual;
+  if (partial && (workspace_bytes < k.ws_bytes || !aligned16(workspace)))
     k = make_plan(B, Hq, Hkv, Nq, Nk, head_dim, false);  // too small: no split
   if (static_cast<long long>(k.n_qpairs) * B * k.heads * k.n_splits > 0x7fffffffLL)
     return FA_ERR_TOO_LARGE;
@@ -239,10 +247,11 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.pos_mod = k.pos_mod;
   p.n_splits = k.n_splits;
   p.tiles_per_split = k.tiles_per_split;
-  p.ws_o = k.n_splits > 1 ? static_cast<float*>(workspace) : nullptr;
-  p.ws_lse = k.n_splits > 1
-                 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + k.ws_o_bytes)
-                 : nullptr;
+  p.dual = k.dual ? 1 : 0;
+  const bool use_ws = k.n_splits > 1 || k.dual;
+  p.ws_o = use_ws ? static_cast<float*>(workspace) : nullptr;
+  p.ws_lse = use_ws ? reinterpret_cast<float*>(static_cast<char*>(workspace) + k.ws_o_bytes)
+                    : nullptr;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.debug_flags = g_debug_flags.load(std::memory_order_relaxed);
   p.trace = g_trace.load(std::memory_order_relaxed);
@@ -250,8 +259,7 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (fa::launch_fwd(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
-  if (k.n_splits > 1 && fa::launch_combine(p, head_dim, bf16, s) != cudaSuccess)
-    return FA_ERR_LAUNCH;
+  if (use_ws && fa::launch_combine(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
   return FA_OK;
 }
 

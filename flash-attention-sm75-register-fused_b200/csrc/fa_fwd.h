@@ -29,8 +29,13 @@ struct alignas(64) FwdParams {
   int pos_mod;       // pos(r) = r % pos_mod (packed: the query length; else Nq)
   int n_splits;      // key-range splits per (batch*head, Q pair); 1 = no split
   int tiles_per_split;
-  float* ws_o;       // n_splits > 1: normalised partial O [n_splits][B*heads][Nq][d] fp32
-  float* ws_lse;     // partial LSE [n_splits][B*heads][Nq] (natural log)
+  // dual = 1 (queries fit one 128-row tile): both softmax groups take the same
+  // rows, group 0 the first half of the CTA's K/V tiles and group 1 the
+  // second, each with its own K/V stream; every group writes a partial result
+  // ("sub-split" 2*split + group) for the combine kernel.
+  int dual;
+  float* ws_o;       // partial O [n_splits * (1 + dual)][B*heads][Nq][d] fp32 (normalised)
+  float* ws_lse;     // partial LSE [n_splits * (1 + dual)][B*heads][Nq] (natural log)
   float scale_log2;  // scale * log2(e)
   int debug_flags;
   long long* trace;  // timeline samples, used only in FA_TRACE builds

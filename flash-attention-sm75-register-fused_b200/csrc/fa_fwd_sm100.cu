@@ -179,6 +179,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   24-27 observer warps (d=128): S0(j), PV0(j), S1(j), PV1(j) complete
 //   28-29 group 0 / 1 tile max computed (row 0)
 //   30-31 producer issued the loads of V_j / K_{j+1}
+//   (tile kTraceTiles-1, events 30 / 31: CTA set up / CTA done)
 constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
 #ifdef FA_TRACE
 #define FA_TRACE_AT(tile, ev)                                                          \
@@ -297,13 +298,34 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   // number of those tiles that group g sees (0 when its causal range or the
   // split ends earlier).
   const int j_begin = sp * p.tiles_per_split;
+  const bool dual = p.dual != 0;
   int n_kv[2];
+  int jb[2];  // first K/V tile of each group
+  if (dual) {
+    // both groups on Q tile 0; the split's tiles are halved between them
+    const int n = max(0, min(kv_tiles_for_tile(p, 2 * qp), j_begin + p.tiles_per_split) - j_begin);
+    n_kv[0] = (n + 1) / 2;
+    n_kv[1] = n / 2;
+    jb[0] = j_begin;
+    jb[1] = j_begin + n_kv[0];
+  } else {
 #pragma unroll
-  for (int g = 0; g < 2; ++g) {
-    const int total = (g == 0 || has_q1) ? kv_tiles_for_tile(p, 2 * qp + g) : 0;
-    n_kv[g] = max(0, min(total, j_begin + p.tiles_per_split) - j_begin);
+    for (int g = 0; g < 2; ++g) {
+      const int total = (g == 0 || has_q1) ? kv_tiles_for_tile(p, 2 * qp + g) : 0;
+      n_kv[g] = max(0, min(total, j_begin + p.tiles_per_split) - j_begin);
+      jb[g] = j_begin;
+    }
   }
   const int n_loop = max(n_kv[0], n_kv[1]);
+  // Ring item (load order) of group g's K tile of iteration it; its V tile is
+  // the next item.  Shared mode: one K/V pair per iteration read by both
+  // groups.  Dual mode: K0 V0 K1 V1 per iteration while both groups have
+  // tiles (n_kv[0] >= n_kv[1]), then K0 V0.
+  auto k_item = [&](int g, int it) -> int {
+    if (!dual) return 2 * it;
+    return it < n_kv[1] ? 4 * it + 2 * g : 2 * n_kv[1] + 2 * it;
+  };
+  const int n_items = dual ? 2 * (n_kv[0] + n_kv[1]) : 2 * n_loop;
 
   // ---- set-up: skip the CTA if this launch already failed elsewhere
   if (threadIdx.x == 0) {
@@ -326,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
+  if (threadIdx.x == 0) FA_TRACE_AT(kTraceTiles - 1, 30);  // CTA set up
 
   if (warp < kWarpSoftmax0 || warp >= kWarpSoftmax0 + 8) {
    // ------------------------------------------------ producer warpgroup
@@ -348,24 +371,35 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
                            bar(L::kBarQ + g), c * 64, q_row0 + g * kBlockM, bh, pol_q);
       }
-      // ring item i: K of tile i/2 (i even) or V of tile i/2 (i odd)
-      const int n_items = 2 * n_loop;
+      // ring item i (the inverse of k_item): K (i even) or V (i odd) of
+      // iteration `it` of group g, i.e. of K/V tile jb[g] + it
       int issued = 0;
       for (int i = 0; i < n_items; ++i) {
         const int slot = i % L::kSlots;
         if (i >= L::kSlots &&
             !bar_wait(bar(L::kBarEmpty + slot), ((i / L::kSlots) - 1) & 1, wc, 1))
           break;
+        int it, g;
+        if (!dual) {
+          it = i >> 1;
+          g = 0;
+        } else if (i < 4 * n_kv[1]) {
+          it = i >> 2;
+          g = (i >> 1) & 1;
+        } else {
+          it = n_kv[1] + ((i - 4 * n_kv[1]) >> 1);
+          g = 0;
+        }
         const uint32_t dst = sbase + L::kOffKV + slot * L::kTile;
         const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
                                   : static_cast<const void*>(&p.tm_k);
-        if ((i & 1) && (i >> 1) < kTraceTiles) FA_TRACE_AT(i >> 1, 30);        // V_j issued
-        if (!(i & 1) && i > 0) FA_TRACE_AT((i >> 1) - 1, 31);                   // K_{j+1} issued
+        if ((i & 1) && !dual && it < kTraceTiles) FA_TRACE_AT(it, 30);       // V_j issued
+        if (!(i & 1) && !dual && it > 0) FA_TRACE_AT(it - 1, 31);            // K_{j+1} issued
         ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
           ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
-                           (j_begin + (i >> 1)) * kBlockN, bh_kv, pol_kv);
+                           (jb[g] + it) * kBlockN, bh_kv, pol_kv);
         issued = i + 1;
       }
       // Drain: every copy this thread started must land before the CTA exits.
@@ -393,9 +427,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
       const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
       const uint64_t q_desc1 = ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024);
-      auto issue_s = [&](int g, int j) {
-        const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(2 * j) * L::kTile) >> 4);
-        const uint64_t qd = g ? q_desc1 : q_desc0;
+      // S_g = Q_g K^T with K in ring item `ki` (dual mode: both groups use Q0)
+      auto issue_s = [&](int g, int ki) {
+        const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(ki) * L::kTile) >> 4);
+        const uint64_t qd = (g && !dual) ? q_desc1 : q_desc0;
         if (ptx::elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -406,14 +441,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
         __syncwarp();
       };
-      auto issue_pv = [&](int g, int j) {
-        const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(2 * j + 1) * L::kTile) >> 4);
+      // O_g (+)= P_g V with V in ring item `vi`; `first` starts the accumulator
+      auto issue_pv = [&](int g, int vi, bool first) {
+        const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(vi) * L::kTile) >> 4);
         if (ptx::elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < kBlockN / 16; ++kk)
             ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
                         vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
-                        (j > 0 || kk > 0) ? 1u : 0u);
+                        (!first || kk > 0) ? 1u : 0u);
           ptx::mma_commit(bar(L::kBarO + g));
         }
         __syncwarp();
@@ -433,60 +469,98 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // so each group's softmax overlaps the other group's two MMAs.  S_g(j+1)
       // may overwrite P_g(j) (d=128): tcgen05.mma ops of one thread execute in
       // issue order, so PV_g(j) has read P_g(j) before S_g(j+1) writes it.
-      // A group without tiles in this split issues nothing; with no tiles at
-      // all the producer loads no K/V and this warp waits for nothing.
-      const bool g0 = n_kv[0] > 0;
-      const bool g1 = n_kv[1] > 0;
       bool ok = true;
-      if (n_loop > 0) {
-        if (g0) ok = wait(bar(L::kBarQ), 0, 10);
-        if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
-        if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
-        if (ok) {
-          if (g0) issue_s(0, 0);
-          if (g1) issue_s(1, 0);
-          commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
-        }
-      }
-      for (int j = 0; ok && j < n_loop; ++j) {
-        const int item_v = 2 * j + 1;
-        const int item_k = 2 * j + 2;  // K of tile j+1
-        const bool next0 = j + 1 < n_kv[0];
-        const bool next1 = j + 1 < n_kv[1];
-        // V_j and K_{j+1} are waited for before the P waits, so that a
-        // group's PV and next S go out back to back once its P is ready.
-        // Every release the producer needs before loading them was committed
-        // in an earlier iteration, so these waits cannot depend on this one.
-        if (lane == 0) FA_TRACE_AT(j, 6);
-        if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
-        if ((next0 || next1) &&
-            !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
-          break;
-        if (lane == 0) FA_TRACE_AT(j, 7);
-        if (j < n_kv[0]) {
-          if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
-          ptx::tc_fence_after();
-          if (lane == 0) FA_TRACE_AT(j, 0);
-          issue_pv(0, j);
-          if (lane == 0) FA_TRACE_AT(j, 4);
-          if (next0) {
-            if (lane == 0) FA_TRACE_AT(j, 1);
-            issue_s(0, j + 1);
-            if (lane == 0) FA_TRACE_AT(j, 5);
-            if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
+      if (!dual) {
+        // A group without tiles in this split issues nothing; with no tiles at
+        // all the producer loads no K/V and this warp waits for nothing.
+        const bool g0 = n_kv[0] > 0;
+        const bool g1 = n_kv[1] > 0;
+        if (n_loop > 0) {
+          if (g0) ok = wait(bar(L::kBarQ), 0, 10);
+          if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
+          if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
+          if (ok) {
+            if (g0) issue_s(0, 0);
+            if (g1) issue_s(1, 0);  // shared mode: K_0 is ring item 0 for both groups
+            commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
           }
         }
-        if (j < n_kv[1]) {
-          if (!(ok = wait(bar(L::kBarP + 1), j & 1, 16))) break;
-          ptx::tc_fence_after();
-          if (lane == 0) FA_TRACE_AT(j, 2);
-          issue_pv(1, j);
+        for (int j = 0; ok && j < n_loop; ++j) {
+          const int item_v = 2 * j + 1;
+          const int item_k = 2 * j + 2;  // K of tile j+1
+          const bool next0 = j + 1 < n_kv[0];
+          const bool next1 = j + 1 < n_kv[1];
+          // V_j and K_{j+1} are waited for before the P waits, so that a
+          // group's PV and next S go out back to back once its P is ready.
+          // Every release the producer needs before loading them was committed
+          // in an earlier iteration, so these waits cannot depend on this one.
+          if (lane == 0) FA_TRACE_AT(j, 6);
+          if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
+          if ((next0 || next1) &&
+              !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
+            break;
+          if (lane == 0) FA_TRACE_AT(j, 7);
+          if (j < n_kv[0]) {
+            if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
+            ptx::tc_fence_after();
+            if (lane == 0) FA_TRACE_AT(j, 0);
+            issue_pv(0, item_v, j == 0);
+            if (lane == 0) FA_TRACE_AT(j, 4);
+            if (next0) {
+              if (lane == 0) FA_TRACE_AT(j, 1);
+              issue_s(0, item_k);
+              if (lane == 0) FA_TRACE_AT(j, 5);
+              if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
+            }
+          }
+          if (j < n_kv[1]) {
+            if (!(ok = wait(bar(L::kBarP + 1), j & 1, 16))) break;
+            ptx::tc_fence_after();
+            if (lane == 0) FA_TRACE_AT(j, 2);
+            issue_pv(1, item_v, j == 0);
+          }
+          commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
+          if (next1) {
+            if (lane == 0) FA_TRACE_AT(j, 3);
+            issue_s(1, item_k);
+            commit(bar(L::kBarEmpty + slot_of(item_k)));
+          }
         }
-        commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
-        if (next1) {
-          if (lane == 0) FA_TRACE_AT(j, 3);
-          issue_s(1, j + 1);
-          commit(bar(L::kBarEmpty + slot_of(item_k)));
+      } else {
+        // Dual mode: each group streams its own K/V tiles (ring items from
+        // k_item), so nothing waits for the other group's P; order per
+        // iteration PV0(j) S0(j+1) PV1(j) S1(j+1), items released after use.
+        if (n_loop > 0) {
+          ok = wait(bar(L::kBarQ), 0, 10);
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            if (!ok || n_kv[g] == 0) continue;
+            const int ki = k_item(g, 0);
+            if (!(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 11))) break;
+            issue_s(g, ki);
+            commit(bar(L::kBarEmpty + slot_of(ki)));
+          }
+        }
+        for (int j = 0; ok && j < n_loop; ++j) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            if (j >= n_kv[g]) continue;
+            const bool next = j + 1 < n_kv[g];
+            const int vi = k_item(g, j) + 1;
+            const int ki = next ? k_item(g, j + 1) : 0;
+            if (!(ok = wait(bar(L::kBarFull + slot_of(vi)), phase_of(vi), 12))) break;
+            if (next && !(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 14))) break;
+            if (!(ok = wait(bar(L::kBarP + g), j & 1, 13 + 3 * g))) break;
+            ptx::tc_fence_after();
+            if (lane == 0) FA_TRACE_AT(j, 2 * g);
+            issue_pv(g, vi, j == 0);
+            commit(bar(L::kBarEmpty + slot_of(vi)));
+            if (next) {
+              if (lane == 0) FA_TRACE_AT(j, 1 + 2 * g);
+              issue_s(g, ki);
+              commit(bar(L::kBarEmpty + slot_of(ki)));
+            }
+          }
         }
       }
       // Drain: all MMAs issued above complete before TMEM is released.
@@ -524,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const int n_tiles = n_kv[g];
     const int wq = warp & 3;
     const int r = wq * 32 + lane;               // row within the tile == TMEM lane
-    const int tile = 2 * qp + g;                // global 128-row tile index
+    const int tile = dual ? 2 * qp : 2 * qp + g;  // global 128-row tile index
     const int q_row = tile * kBlockM + r;
     // causal limit of this row: key k is visible iff k < pos + causal_off + 1
     const int vis_end = q_row % p.pos_mod + p.causal_off + 1;
@@ -575,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
       }
 
-      const int key0 = (j_begin + j) * kBlockN;
+      const int key0 = (jb[g] + j) * kBlockN;
       const bool masked =
           (p.causal && key0 + kBlockN > tile_vis_end) || (key0 + kBlockN > p.Nk);
       // Scaled tile maximum.  Unmasked tiles reduce the raw scores and scale
@@ -646,10 +720,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const bool row_ok = q_row < p.Nq;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     const size_t row_index = static_cast<size_t>(bh) * p.Nq + q_row;
+    // partial-result slot of this group (split mode) in the workspace
+    const int ws_slot = dual ? 2 * sp + g : sp;
+    const bool partial = p.n_splits > 1 || dual;
     if (n_tiles == 0) {
       // No visible key for these rows (causal offset below zero): O = 0 and
-      // LSE = -inf.  A split without tiles leaves the rows to other splits.
-      if (p.n_splits == 1 && row_ok) {
+      // LSE = -inf.  A split without tiles leaves the rows to other splits,
+      // except the empty half of a dual split, whose slot the combine reads.
+      if (dual && row_ok) p.ws_lse[static_cast<size_t>(ws_slot) * p.B * p.heads * p.Nq + row_index] = -INFINITY;
+      if (!partial && row_ok) {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.o) + row_index * D);
 #pragma unroll
         for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -662,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         const float inv_l = (l > 0.f) ? 1.0f / l : 0.f;
         const float m_use = (m == -INFINITY) ? 0.f : m;
         const float lse_row = (l > 0.f) ? (m_use + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
-        if (p.n_splits == 1) {
+        if (!partial) {
           T* orow = reinterpret_cast<T*>(p.o) + row_index * D;
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -684,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           if (row_ok && p.lse != nullptr) p.lse[row_index] = lse_row;
         } else {
           // partial result of this key split, normalised by its own row sum
-          const size_t ws_row = static_cast<size_t>(sp) * p.B * p.heads * p.Nq + row_index;
+          const size_t ws_row = static_cast<size_t>(ws_slot) * p.B * p.heads * p.Nq + row_index;
           float* wrow = p.ws_o + ws_row * D;
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -709,6 +788,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   // ---- teardown
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) FA_TRACE_AT(kTraceTiles - 1, 31);  // CTA done
   if (warp == kWarpMma) {
     __syncwarp();
     ptx::tc_fence_after();
@@ -730,7 +810,10 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
   const int lane = threadIdx.x & 31;
   const int q_row = static_cast<int>(row % p.Nq);
   const int total = kv_tiles_for_tile(p, q_row / kBlockM);
-  const int ns = min(p.n_splits, (total + p.tiles_per_split - 1) / p.tiles_per_split);
+  // slots holding data: one per split with tiles (two in dual mode, where an
+  // empty half stores LSE = -inf)
+  const int ns = min(p.n_splits, (total + p.tiles_per_split - 1) / p.tiles_per_split) *
+                 (p.dual ? 2 : 1);
   float mx = -INFINITY;
   for (int s = 0; s < ns; ++s) mx = fmaxf(mx, p.ws_lse[static_cast<size_t>(s) * n_rows + row]);
   float acc[E];
