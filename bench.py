@@ -15,8 +15,10 @@ of the per-rank times).
 A step is one attention forward over the rank's batch, inputs resident in
 HBM (1.07 GB per step read+written, larger than the 126 MB L2, so no L2 flush
 is needed between steps).  `e2e` times the same forward through the public
-Python API with the step's Q/K/V copied from pinned host memory and O copied
-back inside the timed region.
+Python API for host buffers (`flash_attention_forward_host`): the step's Q/K/V
+are copied from pinned host memory and O back inside the timed region, with the
+copies of each (batch, KV-head group) chunk overlapping the other chunks'
+computation.
 """
 import argparse
 import json
@@ -280,7 +282,7 @@ def main():
     import torch
     import torch.distributed as dist
     import flash_attn_sm75_cuda as _C
-    from flash_attention_sm75 import flash_attention_forward
+    from flash_attention_sm75 import flash_attention_forward_host
     from flash_attention_sm75.sharding import batch_range
     from flash_attention_sm75 import capi as abi
 
@@ -354,7 +356,7 @@ def main():
     }
 
     if not args.no_extras and rank == 0:
-        line["e2e"] = e2e_leg(cfg, q, k, v, dtype, dev, flash_attention_forward)
+        line["e2e"] = e2e_leg(cfg, q, k, v, dtype, dev, flash_attention_forward_host)
         flops, cpu_s, cores, slices, rows_n = cpu_sample(cfg)
         line["cpu_baseline"] = {
             "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
@@ -372,22 +374,19 @@ def main():
         print(json.dumps(line), flush=True)
 
 
-def e2e_leg(cfg, q, k, v, dtype, dev, fwd, steps=5):
-    """Public API end to end: pinned host Q/K/V -> device, forward, O -> pinned host."""
+def e2e_leg(cfg, q, k, v, dtype, dev, fwd_host, steps=5):
+    """Public API end to end: ``flash_attention_forward_host`` on pinned host
+    Q/K/V, O returned in pinned host memory (H2D, forward and D2H of each
+    (batch, KV-head group) chunk overlap inside the call)."""
     import torch
     hq = q.cpu().pin_memory()
     hk = k.cpu().pin_memory()
     hv = v.cpu().pin_memory()
     ho = torch.empty_like(hq).pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        out = fwd(dq, dk, dv, causal=cfg.causal)
-        ho.copy_(out, non_blocking=True)
+        fwd_host(hq, hk, hv, causal=cfg.causal, out=ho)
 
     step()
     torch.cuda.synchronize()

@@ -69,6 +69,48 @@ std::tuple<torch::Tensor, torch::Tensor> fwd_impl(const torch::Tensor& Q, const 
   return {O, lse};
 }
 
+// Forward into caller-provided O (and optional LSE) on the current stream;
+// used by the host-buffer pipeline, which computes per-chunk slices in place.
+void flash_attention_forward_out(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
+                                 torch::Tensor O, c10::optional<torch::Tensor> lse, bool causal,
+                                 float scale) {
+  check_tensor(Q, "Q", true);
+  check_tensor(K, "K", true);
+  check_tensor(V, "V", true);
+  check_tensor(O, "O", true);
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype() && Q.dtype() == O.dtype(),
+              "Q, K, V, O must share a dtype");
+  TORCH_CHECK(Q.device() == K.device() && Q.device() == V.device() && Q.device() == O.device(),
+              "Q, K, V, O must be on the same device");
+  TORCH_CHECK(O.sizes() == Q.sizes(), "O must have Q's shape");
+  TORCH_CHECK(Q.size(0) == K.size(0) && Q.size(2) == K.size(2) && Q.size(3) == K.size(3),
+              "Q and K shapes differ beyond the head count");
+  TORCH_CHECK(K.sizes() == V.sizes(), "K and V must have identical shapes");
+  const auto head_dim = Q.size(3);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  float* lse_ptr = nullptr;
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->is_cuda() && lse->dtype() == torch::kFloat32 && lse->is_contiguous() &&
+                    lse->dim() == 3 && lse->size(0) == Q.size(0) && lse->size(1) == Q.size(1) &&
+                    lse->size(2) == Q.size(2),
+                "lse must be a contiguous fp32 CUDA tensor [B, Hq, N]");
+    lse_ptr = lse->data_ptr<float>();
+  }
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && Q.size(1) <= INT32_MAX && Q.size(2) <= INT32_MAX,
+              "size exceeds int32");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  const int rc = fa_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse_ptr,
+                        static_cast<int>(Q.size(0)), static_cast<int>(Q.size(1)),
+                        static_cast<int>(K.size(1)), static_cast<int>(Q.size(2)),
+                        static_cast<int>(head_dim), scale, causal ? 1 : 0,
+                        Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16,
+                        stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_forward: ", fa_error_string(rc));
+}
+
 torch::Tensor flash_attention_forward(torch::Tensor Q, torch::Tensor K, torch::Tensor V,
                                       bool causal, float scale) {
   return std::get<0>(fwd_impl(Q, K, V, causal, scale, false));
@@ -175,6 +217,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attention_forward_wmma_qk", &flash_attention_forward_wmma_qk);
   m.def("flash_attention_forward_lse", &flash_attention_forward_lse,
         "Returns (O, LSE) with LSE fp32 [B, Hq, N]");
+  m.def("flash_attention_forward_out", &flash_attention_forward_out, pybind11::arg("Q"),
+        pybind11::arg("K"), pybind11::arg("V"), pybind11::arg("O"), pybind11::arg("lse"),
+        pybind11::arg("causal"), pybind11::arg("scale"));
   m.def("flash_attention_forward_kvcache", &flash_attention_forward_kvcache,
         "O, LSE of Nq queries against Nk cached keys; causal: 0 none, 1 bottom-right, 2 top-left");
   m.def("device_status", &device_status, pybind11::arg("reset") = false,

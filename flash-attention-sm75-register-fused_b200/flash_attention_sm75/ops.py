@@ -19,6 +19,9 @@ Differences that a caller can observe only as speed or as extra options:
 * ``flash_attention_forward_kvcache`` (no reference counterpart) serves
   ``Nq != Nk`` — KV-cache decode and chunked prefill — with bottom-right or
   top-left causal alignment.
+* ``flash_attention_forward_host`` takes Q, K, V in host memory and returns O
+  in host memory, overlapping the PCIe copies of each (batch, KV-head group)
+  chunk with the computation of the others.
 
 There is no CPU path: the CUDA extension must load, or the import fails.
 """
@@ -146,3 +149,86 @@ def flash_attention_forward_kvcache(Q, K, V, causal=False, scale=None, return_ls
     out, lse = _C.flash_attention_forward_kvcache(Q.contiguous(), K.contiguous(), V.contiguous(),
                                                   mode, float(scale))
     return (out, lse) if return_lse else out
+
+
+_pipeline = {}
+
+
+def _pipeline_streams(index):
+    if index not in _pipeline:
+        _pipeline[index] = tuple(torch.cuda.Stream(device=index) for _ in range(3))
+    return _pipeline[index]
+
+
+def flash_attention_forward_host(Q, K, V, causal=False, scale=None, out=None, device=None,
+                                 chunks=16):
+    """Attention forward of host-resident Q, K, V into host-resident O.
+
+    The work is cut into about ``chunks`` (batch entry, KV-head group) slices.
+    Per slice, Q/K/V are copied to the GPU on a copy stream, the forward runs on
+    a compute stream once they have landed, and O is copied back on a third
+    stream, so transfers in both directions overlap the computation of other
+    slices (use pinned host tensors for asynchronous copies).  Returns ``out``
+    (allocated pinned if None) once it holds the result.
+    """
+    if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
+        raise ValueError("Q must be 4D [B, H, N, D]")
+    if Q.is_cuda or K.is_cuda or V.is_cuda:
+        raise ValueError("flash_attention_forward_host expects host tensors")
+    head_dim = Q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    _check_gqa(Q.size(1), K.size(1))
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+    B, Hq, N, _ = Q.shape
+    Hkv = K.size(1)
+    G = Hq // Hkv
+    if out is None:
+        out = torch.empty(Q.shape, dtype=Q.dtype, pin_memory=True)
+    if out.shape != Q.shape or out.dtype != Q.dtype or not out.is_contiguous() or out.is_cuda:
+        raise ValueError("out must be a contiguous host tensor shaped and typed like Q")
+    if Q.numel() == 0:
+        return out
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None
+                       else torch.device(device).index)
+    parts = max(1, min(Hkv, -(-int(chunks) // B)))
+    bounds = [(i * Hkv // parts, (i + 1) * Hkv // parts) for i in range(parts)]
+    bounds = [(k0, k1) for k0, k1 in bounds if k1 > k0]
+    with torch.cuda.device(dev):
+        cur = torch.cuda.current_stream()
+        s_in, s_comp, s_out = _pipeline_streams(dev.index)
+        dq = torch.empty(Q.shape, dtype=Q.dtype, device=dev)
+        dk = torch.empty(K.shape, dtype=K.dtype, device=dev)
+        dv = torch.empty(V.shape, dtype=V.dtype, device=dev)
+        do = torch.empty(Q.shape, dtype=Q.dtype, device=dev)
+        for t, st in ((dq, s_in), (dk, s_in), (dv, s_in), (dq, s_comp), (dk, s_comp),
+                      (dv, s_comp), (do, s_comp), (do, s_out)):
+            t.record_stream(st)
+        for st in (s_in, s_comp, s_out):
+            st.wait_stream(cur)
+        for b in range(B):
+            for k0, k1 in bounds:
+                h0, h1 = k0 * G, k1 * G
+                with torch.cuda.stream(s_in):
+                    dq[b, h0:h1].copy_(Q[b, h0:h1], non_blocking=True)
+                    dk[b, k0:k1].copy_(K[b, k0:k1], non_blocking=True)
+                    dv[b, k0:k1].copy_(V[b, k0:k1], non_blocking=True)
+                    landed = torch.cuda.Event()
+                    landed.record(s_in)
+                with torch.cuda.stream(s_comp):
+                    s_comp.wait_event(landed)
+                    _C.flash_attention_forward_out(dq[b:b + 1, h0:h1], dk[b:b + 1, k0:k1],
+                                                   dv[b:b + 1, k0:k1], do[b:b + 1, h0:h1], None,
+                                                   bool(causal), float(scale))
+                    done = torch.cuda.Event()
+                    done.record(s_comp)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(done)
+                    out[b, h0:h1].copy_(do[b, h0:h1], non_blocking=True)
+        cur.wait_stream(s_out)
+        s_out.synchronize()
+    return out

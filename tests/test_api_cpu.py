@@ -8,8 +8,9 @@ from flash_attention_sm75 import ops
 
 
 def test_public_surface():
-    # the reference's surface (src/flash_attention_sm75/__init__.py:1-4) plus one addition
-    assert fa.__all__ == ["flash_attention_forward", "flash_attention_forward_kvcache"]
+    # the reference's surface (src/flash_attention_sm75/__init__.py:1-4) plus two additions
+    assert fa.__all__ == ["flash_attention_forward", "flash_attention_forward_kvcache",
+                          "flash_attention_forward_host"]
     assert isinstance(fa.__version__, str)
 
 
@@ -75,3 +76,16 @@ def test_extension_module_binds_reference_names():
                  "flash_attention_forward_scalar", "flash_attention_forward_wmma_qk",
                  "flash_attention_forward_lse", "device_status"):
         assert hasattr(C, name)
+
+
+def test_host_api_argument_errors():
+    q = torch.zeros(1, 4, 16, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="4D"):
+        fa.flash_attention_forward_host(q[0], q, q)
+    with pytest.raises(RuntimeError, match="supports head_dim=64 or 128"):
+        x = torch.zeros(1, 4, 16, 96, dtype=torch.float16)
+        fa.flash_attention_forward_host(x, x, x)
+    with pytest.raises(RuntimeError, match="not divisible"):
+        fa.flash_attention_forward_host(q, q[:, :3], q[:, :3])
+    with pytest.raises(ValueError, match="out must be"):
+        fa.flash_attention_forward_host(q, q, q, out=torch.zeros(1, 4, 16, 32, dtype=torch.float16))

@@ -128,3 +128,18 @@ def test_current_stream_semantics(sm100):
     torch.cuda.synchronize()
     assert torch.equal(o1, o2)
     assert C.device_status(False) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,d,causal,chunks", [
+    (2, 8, 2, 300, 128, True, 16), (1, 4, 4, 1024, 64, False, 3), (3, 6, 3, 200, 64, True, 1)])
+def test_host_pipeline_matches_device_path(sm100, B, Hq, Hkv, N, d, causal, chunks):
+    """Host buffers in and out, copies overlapped per (batch, KV-head group)
+    chunk: the same kernel per head, so bit-identical to the device call."""
+    q, k, v = _inputs(B, Hq, Hkv, N, d, causal)
+    ref = fa.flash_attention_forward(q.cuda(), k.cuda(), v.cuda(), causal=causal).cpu()
+    out = fa.flash_attention_forward_host(q.pin_memory(), k.pin_memory(), v.pin_memory(),
+                                          causal=causal, chunks=chunks)
+    assert not out.is_cuda and torch.equal(out, ref)
+    pre = torch.zeros_like(q).pin_memory()
+    out2 = fa.flash_attention_forward_host(q, k, v, causal=causal, out=pre)  # pageable inputs
+    assert out2 is pre and torch.equal(pre, ref)
