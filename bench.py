@@ -1,7 +1,7 @@
 """Attention-forward benchmark (driver contract: one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c5] [--dtype f16|bf16] [--no-extras]
+                    [--config c5] [--dtype f16|bf16] [--no-extras] [--kvcache-only NAME|all]
 
 Metric: attention-forward TFLOPS, FLOPs = 4*B*H*N^2*d (halved
 for causal, the reference's convention), whole-job aggregate over N GPUs.
@@ -60,6 +60,9 @@ def parse_args():
     ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip e2e, cpu_baseline and the per-config table (profiling runs)")
+    ap.add_argument("--kvcache-only", default=None, metavar="NAME|all",
+                    help="time only fa_fwd_kvcache workloads (decode / chunked prefill) and print "
+                         "their table as one JSON line (profiling runs)")
     return ap.parse_args()
 
 
@@ -288,6 +291,13 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.kvcache_only:
+        if rank == 0:
+            dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+            names = None if args.kvcache_only == "all" else [args.kvcache_only]
+            print(json.dumps({"kvcache": kvcache_configs(abi.load(), abi, dtype, dev, names)}),
+                  flush=True)
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
@@ -432,7 +442,7 @@ KVCACHE_CONFIGS = {
 }
 
 
-def kvcache_configs(lib, abi, dtype, dev):
+def kvcache_configs(lib, abi, dtype, dev, names=None):
     """Kernel-only time of fa_fwd_kvcache on seeded N(0,1) inputs with a split
     workspace.  Decode is HBM-bound: GB/s counts Q, K, V, O and LSE once
     (K/V > L2, so no flush is needed) and ``hbm_frac`` divides by the measured
@@ -444,6 +454,8 @@ def kvcache_configs(lib, abi, dtype, dev):
     out = {}
     el = 2
     for name, (B, Hq, Hkv, Nq, Nk, d, mode) in KVCACHE_CONFIGS.items():
+        if names is not None and name not in names:
+            continue
         g = torch.Generator(device=dev).manual_seed(7)
         q = torch.randn(B, Hq, Nq, d, device=dev, dtype=torch.float32, generator=g).to(dtype)
         k = torch.randn(B, Hkv, Nk, d, device=dev, dtype=torch.float32, generator=g).to(dtype)
