@@ -148,6 +148,7 @@ int sm_count() {
 struct Plan {
   bool pack = false;
   bool dual = false;  // one Q tile: the two softmax groups split the key tiles
+  int n_ctas = 0;     // persistent CTAs (dual mode), 0 = one per work item
   int heads = 0, rows = 0, group = 1, pos_mod = 1, n_qpairs = 0, n_kv_tiles = 0;
   int n_splits = 1, tiles_per_split = 0;
   size_t ws_o_bytes = 0, ws_bytes = 0;
@@ -177,7 +178,31 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   }
   // Queries that fit one 128-row tile leave the CTA's second softmax group
   // idle; in dual mode the two groups take halves of the CTA's key tiles.
+  // Dual launches are persistent: one CTA per SM walks work items of an even
+  // number of key tiles, so no wave tail remains and the ring prefetches the
+  // next item's tiles during the current one.
   k.dual = allow_split && k.rows <= 128 && k.n_kv_tiles >= 2;
+  if (k.dual) {
+    // about six work items per persistent CTA (measured: 3 was slower on the
+    // decode workloads of bench.py, 1-2 leave a wave tail or unbalanced items)
+    constexpr long long kItemsPerCta = 6;
+    const long long tiles = units * k.n_kv_tiles;
+    const long long per = kItemsPerCta * sms;
+    long long tps = (tiles + per - 1) / per;
+    if (tps < 2) tps = 2;
+    // at most 32 splits per row keep the combine short
+    if (tps * 32 < k.n_kv_tiles) tps = (k.n_kv_tiles + 31) / 32;
+    if (tps > k.n_kv_tiles) tps = k.n_kv_tiles;
+    // balance: the same number of tiles (+-2) in every split of a row
+    const long long ns = (k.n_kv_tiles + tps - 1) / tps;
+    tps = (k.n_kv_tiles + ns - 1) / ns;
+    tps += tps & 1;
+    if (tps > k.n_kv_tiles) tps = k.n_kv_tiles;
+    k.tiles_per_split = static_cast<int>(tps);
+    k.n_splits = (k.n_kv_tiles + k.tiles_per_split - 1) / k.tiles_per_split;
+    const long long n_work = units * k.n_splits;
+    k.n_ctas = static_cast<int>(n_work < sms ? n_work : sms);
+  }
   if (k.n_splits > 1 || k.dual) {
     const size_t slots = static_cast<size_t>(k.n_splits) * (k.dual ? 2 : 1);
     const size_t rows_total = static_cast<size_t>(B) * k.heads * k.rows;
@@ -248,6 +273,7 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.n_splits = k.n_splits;
   p.tiles_per_split = k.tiles_per_split;
   p.dual = k.dual ? 1 : 0;
+  p.n_ctas = k.n_ctas;
   const bool use_ws = k.n_splits > 1 || k.dual;
   p.ws_o = use_ws ? static_cast<float*>(workspace) : nullptr;
   p.ws_lse = use_ws ? reinterpret_cast<float*>(static_cast<char*>(workspace) + k.ws_o_bytes)

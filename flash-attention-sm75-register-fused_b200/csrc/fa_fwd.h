@@ -34,6 +34,7 @@ struct alignas(64) FwdParams {
   // second, each with its own K/V stream; every group writes a partial result
   // ("sub-split" 2*split + group) for the combine kernel.
   int dual;
+  int n_ctas;        // CTAs launched; 0 = one per work item, fewer = persistent CTAs
   float* ws_o;       // partial O [n_splits * (1 + dual)][B*heads][Nq][d] fp32 (normalised)
   float* ws_lse;     // partial LSE [n_splits * (1 + dual)][B*heads][Nq] (natural log)
   float scale_log2;  // scale * log2(e)

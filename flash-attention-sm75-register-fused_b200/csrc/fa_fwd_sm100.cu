@@ -60,8 +60,8 @@ constexpr int kWarpSoftmax0 = 0;
 // softmax warpgroups.  256*kRegsSoftmax + 128*kRegsOther must not exceed
 // 384*kLaunchRegs.
 constexpr int kLaunchRegs = 168;
-constexpr int kRegsSoftmax = 208;
-constexpr int kRegsOther = 88;
+constexpr int kRegsSoftmax = 192;
+constexpr int kRegsOther = 120;
 static_assert(256 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kLaunchRegs,
               "register split exceeds the launch allocation");
 // Lazy rescaling: O and l keep a stale row max until the true max exceeds it
@@ -89,7 +89,10 @@ struct Layout {
   static constexpr int kBarP = kBarS + 2;               // 2
   static constexpr int kBarO = kBarP + 2;               // 2
   static constexpr int kBarDrain = kBarO + 2;           // 1
-  static constexpr int kNumBars = kBarDrain + 1;
+  // persistent launches (several work items per CTA): the MMAs that read Q
+  // buffer b for one item have completed, so the next Q may overwrite it
+  static constexpr int kBarQFree = kBarDrain + 1;       // 2
+  static constexpr int kNumBars = kBarQFree + 2;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynBytes = kBytes + 1024;  // slack for 1024-byte alignment
@@ -268,6 +271,76 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
   return a0 + a1;
 }
 
+// One unit of work of a CTA: a (batch*head, Q pair, key split) triple, with
+// the K/V tiles each softmax group processes.  A launch has n_work of them;
+// CTA c takes c, c + gridDim.x, ... (one each unless the launch is persistent).
+struct WorkItem {
+  int bh, qp, sp, bh_kv, q_row0;
+  bool has_q1;
+  int n_kv[2];  // K/V tiles of group g (0: the group idles in this item)
+  int jb[2];    // first K/V tile of group g
+  int n_loop;   // max(n_kv)
+  int n_items;  // K/V ring items the item loads
+};
+
+__device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem& it) {
+  it.sp = w % p.n_splits;
+  const int rest = w / p.n_splits;
+  it.bh = rest / p.n_qpairs;
+  int qp = rest % p.n_qpairs;
+  if (p.causal) qp = p.n_qpairs - 1 - qp;  // causal pairs of one head: heaviest first
+  it.qp = qp;
+  const int b = it.bh / p.heads;
+  const int hq = it.bh % p.heads;
+  it.bh_kv = b * p.Hkv + hq / p.group;
+  it.q_row0 = qp * 2 * kBlockM;
+  it.has_q1 = it.q_row0 + kBlockM < p.Nq;
+  const int j_begin = it.sp * p.tiles_per_split;
+  if (p.dual) {
+    // both groups on Q tile 0; the split's tiles are halved between them
+    const int n =
+        max(0, min(kv_tiles_for_tile(p, 2 * qp), j_begin + p.tiles_per_split) - j_begin);
+    it.n_kv[0] = (n + 1) / 2;
+    it.n_kv[1] = n / 2;
+    it.jb[0] = j_begin;
+    it.jb[1] = j_begin + it.n_kv[0];
+  } else {
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int total = (g == 0 || it.has_q1) ? kv_tiles_for_tile(p, 2 * qp + g) : 0;
+      it.n_kv[g] = max(0, min(total, j_begin + p.tiles_per_split) - j_begin);
+      it.jb[g] = j_begin;
+    }
+  }
+  it.n_loop = max(it.n_kv[0], it.n_kv[1]);
+  it.n_items = p.dual ? 2 * (it.n_kv[0] + it.n_kv[1]) : 2 * it.n_loop;
+}
+
+// Item index (load order, from 0 within the work item) of group g's K tile of
+// iteration i; its V tile is the next item.  Shared mode: one K/V pair per
+// iteration read by both groups.  Dual mode: K0 V0 K1 V1 per iteration while
+// both groups have tiles (n_kv[0] >= n_kv[1]), then K0 V0.
+__device__ __forceinline__ int k_item_of(const WorkItem& it, bool dual, int g, int i) {
+  if (!dual) return 2 * i;
+  return i < it.n_kv[1] ? 4 * i + 2 * g : 2 * it.n_kv[1] + 2 * i;
+}
+
+// Inverse of k_item_of: K/V tile of item index i (g = its group).
+__device__ __forceinline__ int tile_of_item(const WorkItem& it, bool dual, int i, int& g) {
+  int iter;
+  if (!dual) {
+    iter = i >> 1;
+    g = 0;
+  } else if (i < 4 * it.n_kv[1]) {
+    iter = i >> 2;
+    g = (i >> 1) & 1;
+  } else {
+    iter = it.n_kv[1] + ((i - 4 * it.n_kv[1]) >> 1);
+    g = 0;
+  }
+  return it.jb[g] + iter;
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_constant__ FwdParams p) {
   using L = Layout<D>;
@@ -282,56 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
 
-  // ---- work item: (batch*head, Q pair, key split); causal pairs of one head
-  // run heaviest first
-  const int sp = blockIdx.x % p.n_splits;
-  const int rest = blockIdx.x / p.n_splits;
-  const int bh = rest / p.n_qpairs;
-  int qp = rest % p.n_qpairs;
-  if (p.causal) qp = p.n_qpairs - 1 - qp;
-  const int b = bh / p.heads;
-  const int hq = bh % p.heads;
-  const int bh_kv = b * p.Hkv + hq / p.group;
-  const int q_row0 = qp * 2 * kBlockM;
-  const bool has_q1 = q_row0 + kBlockM < p.Nq;
-  // This CTA covers K/V tiles j_begin + it (it = 0, 1, ...); n_kv[g] is the
-  // number of those tiles that group g sees (0 when its causal range or the
-  // split ends earlier).
-  const int j_begin = sp * p.tiles_per_split;
   const bool dual = p.dual != 0;
-  int n_kv[2];
-  int jb[2];  // first K/V tile of each group
-  if (dual) {
-    // both groups on Q tile 0; the split's tiles are halved between them
-    const int n = max(0, min(kv_tiles_for_tile(p, 2 * qp), j_begin + p.tiles_per_split) - j_begin);
-    n_kv[0] = (n + 1) / 2;
-    n_kv[1] = n / 2;
-    jb[0] = j_begin;
-    jb[1] = j_begin + n_kv[0];
-  } else {
-#pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      const int total = (g == 0 || has_q1) ? kv_tiles_for_tile(p, 2 * qp + g) : 0;
-      n_kv[g] = max(0, min(total, j_begin + p.tiles_per_split) - j_begin);
-      jb[g] = j_begin;
-    }
-  }
-  const int n_loop = max(n_kv[0], n_kv[1]);
-  // Ring item (load order) of group g's K tile of iteration it; its V tile is
-  // the next item.  Shared mode: one K/V pair per iteration read by both
-  // groups.  Dual mode: K0 V0 K1 V1 per iteration while both groups have
-  // tiles (n_kv[0] >= n_kv[1]), then K0 V0.
-  auto k_item = [&](int g, int it) -> int {
-    if (!dual) return 2 * it;
-    return it < n_kv[1] ? 4 * it + 2 * g : 2 * n_kv[1] + 2 * it;
-  };
-  const int n_items = dual ? 2 * (n_kv[0] + n_kv[1]) : 2 * n_loop;
+  const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
 
   // ---- set-up: skip the CTA if this launch already failed elsewhere
   if (threadIdx.x == 0) {
     const unsigned long long st = *reinterpret_cast<volatile unsigned long long*>(&g_fa_status);
     *abort_flag = ((st >> 32) == p.epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
     for (int i = 0; i < L::kNumBars; ++i) {
+      // P completes on an arrival of every thread of a softmax group
       const bool is_p = (i == L::kBarP || i == L::kBarP + 1);
       ptx::mbar_init(bar(i), is_p ? 128u : 1u);
     }
@@ -362,53 +394,65 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       const uint64_t pol_q = ptx::policy_evict_first();
       const uint64_t pol_kv = ptx::policy_evict_last();
       const bool skip_q = (p.debug_flags & FA_DEBUG_SKIP_Q_LOAD) != 0;
-      for (int g = 0; g < 2; ++g) {
-        if (g == 1 && !has_q1) break;
-        if (skip_q) break;  // test hook: nothing ever arrives on the Q barriers
-        ptx::mbar_arrive_expect_tx(bar(L::kBarQ + g), L::kTile);
+      // Ring items are numbered across the CTA's work items (slot r % kSlots),
+      // so the next item's K/V tiles load while the current one computes.
+      // Dual mode double-buffers Q (work item k uses buffer k & 1): loading
+      // item k's Q waits until the MMAs of item k-2, which read that buffer,
+      // have completed.  Shared mode uses both Q buffers for its two tiles and
+      // is never launched with more than one item per CTA.
+      int ring = 0, k = 0, q_loads[2] = {0, 0};
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x, ++k) {
+        WorkItem it;
+        decode_item(p, w, it);
+        if (!skip_q) {
+          if (dual) {
+            const int qb = k & 1;
+            if (k >= 2 && !(ok = bar_wait(bar(L::kBarQFree + qb), ((k - 2) >> 1) & 1, wc, 3)))
+              break;
+            ptx::mbar_arrive_expect_tx(bar(L::kBarQ + qb), L::kTile);
 #pragma unroll
-        for (int c = 0; c < L::kColBlocks; ++c)
-          ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
-                           bar(L::kBarQ + g), c * 64, q_row0 + g * kBlockM, bh, pol_q);
-      }
-      // ring item i (the inverse of k_item): K (i even) or V (i odd) of
-      // iteration `it` of group g, i.e. of K/V tile jb[g] + it
-      int issued = 0;
-      for (int i = 0; i < n_items; ++i) {
-        const int slot = i % L::kSlots;
-        if (i >= L::kSlots &&
-            !bar_wait(bar(L::kBarEmpty + slot), ((i / L::kSlots) - 1) & 1, wc, 1))
-          break;
-        int it, g;
-        if (!dual) {
-          it = i >> 1;
-          g = 0;
-        } else if (i < 4 * n_kv[1]) {
-          it = i >> 2;
-          g = (i >> 1) & 1;
-        } else {
-          it = n_kv[1] + ((i - 4 * n_kv[1]) >> 1);
-          g = 0;
+            for (int c = 0; c < L::kColBlocks; ++c)
+              ptx::tma_load_3d(sbase + L::kOffQ + qb * L::kTile + c * L::kBlockBytes, &p.tm_q,
+                               bar(L::kBarQ + qb), c * 64, it.q_row0, it.bh, pol_q);
+            ++q_loads[qb];
+          } else {
+            for (int g = 0; g < 2; ++g) {
+              if (g == 1 && !it.has_q1) break;
+              ptx::mbar_arrive_expect_tx(bar(L::kBarQ + g), L::kTile);
+#pragma unroll
+              for (int c = 0; c < L::kColBlocks; ++c)
+                ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
+                                 bar(L::kBarQ + g), c * 64, it.q_row0 + g * kBlockM, it.bh,
+                                 pol_q);
+              ++q_loads[g];
+            }
+          }
         }
-        const uint32_t dst = sbase + L::kOffKV + slot * L::kTile;
-        const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
-                                  : static_cast<const void*>(&p.tm_k);
-        if ((i & 1) && !dual && it < kTraceTiles) FA_TRACE_AT(it, 30);       // V_j issued
-        if (!(i & 1) && !dual && it > 0) FA_TRACE_AT(it - 1, 31);            // K_{j+1} issued
-        ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
+        for (int i = 0; i < it.n_items; ++i, ++ring) {
+          const int slot = ring % L::kSlots;
+          if (ring >= L::kSlots &&
+              !(ok = bar_wait(bar(L::kBarEmpty + slot), ((ring / L::kSlots) - 1) & 1, wc, 1)))
+            break;
+          int g;
+          const int tile = tile_of_item(it, dual, i, g);
+          const uint32_t dst = sbase + L::kOffKV + slot * L::kTile;
+          const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
+                                    : static_cast<const void*>(&p.tm_k);
+          if ((i & 1) && !dual) FA_TRACE_AT(i >> 1, 30);                // V_j issued
+          if (!(i & 1) && !dual && i > 0) FA_TRACE_AT((i >> 1) - 1, 31);  // K_{j+1} issued
+          ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
 #pragma unroll
-        for (int c = 0; c < L::kColBlocks; ++c)
-          ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
-                           (jb[g] + it) * kBlockN, bh_kv, pol_kv);
-        issued = i + 1;
+          for (int c = 0; c < L::kColBlocks; ++c)
+            ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
+                             tile * kBlockN, it.bh_kv, pol_kv);
+        }
       }
       // Drain: every copy this thread started must land before the CTA exits.
-      for (int i = max(0, issued - L::kSlots); i < issued; ++i)
-        bar_wait(bar(L::kBarFull + i % L::kSlots), (i / L::kSlots) & 1, wc, 2, false);
-      if (!skip_q) {
-        bar_wait(bar(L::kBarQ), 0, wc, 2, false);
-        if (has_q1) bar_wait(bar(L::kBarQ + 1), 0, wc, 2, false);
-      }
+      for (int r = max(0, ring - L::kSlots); r < ring; ++r)
+        bar_wait(bar(L::kBarFull + r % L::kSlots), (r / L::kSlots) & 1, wc, 2, false);
+      for (int b = 0; b < 2; ++b)
+        if (q_loads[b] > 0) bar_wait(bar(L::kBarQ + b), (q_loads[b] - 1) & 1, wc, 2, false);
     }
   } else if (warp == kWarpMma) {
     // ===================================================== MMA issuer
@@ -427,10 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
       const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
       const uint64_t q_desc1 = ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024);
-      // S_g = Q_g K^T with K in ring item `ki` (dual mode: both groups use Q0)
-      auto issue_s = [&](int g, int ki) {
+      // S_g = Q K^T with Q at descriptor qd and K in ring item `ki`
+      auto issue_s = [&](int g, int ki, uint64_t qd) {
         const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(ki) * L::kTile) >> 4);
-        const uint64_t qd = (g && !dual) ? q_desc1 : q_desc0;
         if (ptx::elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -469,99 +512,120 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // so each group's softmax overlaps the other group's two MMAs.  S_g(j+1)
       // may overwrite P_g(j) (d=128): tcgen05.mma ops of one thread execute in
       // issue order, so PV_g(j) has read P_g(j) before S_g(j+1) writes it.
+      // Work items: `ring` numbers K/V ring items across items, cnt[g] counts
+      // the S/P/O completions of group g before the item (barrier parities).
+      // A P arrival of group g for an item follows that group's reads of O
+      // for the previous item, so the first PV of an item may overwrite O.
       bool ok = true;
-      if (!dual) {
-        // A group without tiles in this split issues nothing; with no tiles at
-        // all the producer loads no K/V and this warp waits for nothing.
-        const bool g0 = n_kv[0] > 0;
-        const bool g1 = n_kv[1] > 0;
-        if (n_loop > 0) {
-          if (g0) ok = wait(bar(L::kBarQ), 0, 10);
-          if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
-          if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
-          if (ok) {
-            if (g0) issue_s(0, 0);
-            if (g1) issue_s(1, 0);  // shared mode: K_0 is ring item 0 for both groups
-            commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
-          }
-        }
-        for (int j = 0; ok && j < n_loop; ++j) {
-          const int item_v = 2 * j + 1;
-          const int item_k = 2 * j + 2;  // K of tile j+1
-          const bool next0 = j + 1 < n_kv[0];
-          const bool next1 = j + 1 < n_kv[1];
-          // V_j and K_{j+1} are waited for before the P waits, so that a
-          // group's PV and next S go out back to back once its P is ready.
-          // Every release the producer needs before loading them was committed
-          // in an earlier iteration, so these waits cannot depend on this one.
-          if (lane == 0) FA_TRACE_AT(j, 6);
-          if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
-          if ((next0 || next1) &&
-              !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
-            break;
-          if (lane == 0) FA_TRACE_AT(j, 7);
-          if (j < n_kv[0]) {
-            if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
-            ptx::tc_fence_after();
-            if (lane == 0) FA_TRACE_AT(j, 0);
-            issue_pv(0, item_v, j == 0);
-            if (lane == 0) FA_TRACE_AT(j, 4);
-            if (next0) {
-              if (lane == 0) FA_TRACE_AT(j, 1);
-              issue_s(0, item_k);
-              if (lane == 0) FA_TRACE_AT(j, 5);
-              if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
+      int ring = 0, k = 0;
+      int cnt[2] = {0, 0};
+      for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x, ++k) {
+        WorkItem it;
+        decode_item(p, w, it);
+        const int n_loop = it.n_loop;
+        if (!dual) {
+          // one work item per CTA: Q tiles in buffers 0 / 1, phases from 0.
+          // A group without tiles in this split issues nothing; with no tiles
+          // at all the producer loads no K/V and this warp waits for nothing.
+          const bool g0 = it.n_kv[0] > 0;
+          const bool g1 = it.n_kv[1] > 0;
+          if (n_loop > 0) {
+            if (g0) ok = wait(bar(L::kBarQ), 0, 10);
+            if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
+            if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
+            if (ok) {
+              if (g0) issue_s(0, 0, q_desc0);
+              if (g1) issue_s(1, 0, q_desc1);  // K_0 is ring item 0 for both groups
+              commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
             }
           }
-          if (j < n_kv[1]) {
-            if (!(ok = wait(bar(L::kBarP + 1), j & 1, 16))) break;
-            ptx::tc_fence_after();
-            if (lane == 0) FA_TRACE_AT(j, 2);
-            issue_pv(1, item_v, j == 0);
+          for (int j = 0; ok && j < n_loop; ++j) {
+            const int item_v = 2 * j + 1;
+            const int item_k = 2 * j + 2;  // K of tile j+1
+            const bool next0 = j + 1 < it.n_kv[0];
+            const bool next1 = j + 1 < it.n_kv[1];
+            // V_j and K_{j+1} are waited for before the P waits, so that a
+            // group's PV and next S go out back to back once its P is ready.
+            // Every release the producer needs before loading them was
+            // committed in an earlier iteration, so these waits cannot depend
+            // on this one.
+            if (lane == 0) FA_TRACE_AT(j, 6);
+            if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
+            if ((next0 || next1) &&
+                !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
+              break;
+            if (lane == 0) FA_TRACE_AT(j, 7);
+            if (j < it.n_kv[0]) {
+              if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
+              ptx::tc_fence_after();
+              if (lane == 0) FA_TRACE_AT(j, 0);
+              issue_pv(0, item_v, j == 0);
+              if (lane == 0) FA_TRACE_AT(j, 4);
+              if (next0) {
+                if (lane == 0) FA_TRACE_AT(j, 1);
+                issue_s(0, item_k, q_desc0);
+                if (lane == 0) FA_TRACE_AT(j, 5);
+                if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
+              }
+            }
+            if (j < it.n_kv[1]) {
+              if (!(ok = wait(bar(L::kBarP + 1), j & 1, 16))) break;
+              ptx::tc_fence_after();
+              if (lane == 0) FA_TRACE_AT(j, 2);
+              issue_pv(1, item_v, j == 0);
+            }
+            commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
+            if (next1) {
+              if (lane == 0) FA_TRACE_AT(j, 3);
+              issue_s(1, item_k, q_desc1);
+              commit(bar(L::kBarEmpty + slot_of(item_k)));
+            }
           }
-          commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
-          if (next1) {
-            if (lane == 0) FA_TRACE_AT(j, 3);
-            issue_s(1, item_k);
-            commit(bar(L::kBarEmpty + slot_of(item_k)));
-          }
-        }
-      } else {
-        // Dual mode: each group streams its own K/V tiles (ring items from
-        // k_item), so nothing waits for the other group's P; order per
-        // iteration PV0(j) S0(j+1) PV1(j) S1(j+1), items released after use.
-        if (n_loop > 0) {
-          ok = wait(bar(L::kBarQ), 0, 10);
+        } else {
+          // Dual mode: each group streams its own K/V tiles (items from
+          // k_item_of), so nothing waits for the other group's P; order per
+          // iteration PV0(j) S0(j+1) PV1(j) S1(j+1), items released after use.
+          // Both groups read Q buffer k & 1.
+          const int qb = k & 1;
+          const uint64_t qd = qb ? q_desc1 : q_desc0;
+          if (n_loop > 0) {
+            ok = wait(bar(L::kBarQ + qb), (k >> 1) & 1, 10);
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            if (!ok || n_kv[g] == 0) continue;
-            const int ki = k_item(g, 0);
-            if (!(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 11))) break;
-            issue_s(g, ki);
-            commit(bar(L::kBarEmpty + slot_of(ki)));
-          }
-        }
-        for (int j = 0; ok && j < n_loop; ++j) {
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            if (j >= n_kv[g]) continue;
-            const bool next = j + 1 < n_kv[g];
-            const int vi = k_item(g, j) + 1;
-            const int ki = next ? k_item(g, j + 1) : 0;
-            if (!(ok = wait(bar(L::kBarFull + slot_of(vi)), phase_of(vi), 12))) break;
-            if (next && !(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 14))) break;
-            if (!(ok = wait(bar(L::kBarP + g), j & 1, 13 + 3 * g))) break;
-            ptx::tc_fence_after();
-            if (lane == 0) FA_TRACE_AT(j, 2 * g);
-            issue_pv(g, vi, j == 0);
-            commit(bar(L::kBarEmpty + slot_of(vi)));
-            if (next) {
-              if (lane == 0) FA_TRACE_AT(j, 1 + 2 * g);
-              issue_s(g, ki);
+            for (int g = 0; g < 2; ++g) {
+              if (!ok || it.n_kv[g] == 0) continue;
+              const int ki = ring + k_item_of(it, true, g, 0);
+              if (!(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 11))) break;
+              issue_s(g, ki, qd);
               commit(bar(L::kBarEmpty + slot_of(ki)));
             }
           }
+          for (int j = 0; ok && j < n_loop; ++j) {
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              if (j >= it.n_kv[g]) continue;
+              const bool next = j + 1 < it.n_kv[g];
+              const int vi = ring + k_item_of(it, true, g, j) + 1;
+              const int ki = next ? ring + k_item_of(it, true, g, j + 1) : 0;
+              if (!(ok = wait(bar(L::kBarFull + slot_of(vi)), phase_of(vi), 12))) break;
+              if (next && !(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 14))) break;
+              if (!(ok = wait(bar(L::kBarP + g), (cnt[g] + j) & 1, 13 + 3 * g))) break;
+              ptx::tc_fence_after();
+              if (lane == 0) FA_TRACE_AT(j, 2 * g);
+              issue_pv(g, vi, j == 0);
+              commit(bar(L::kBarEmpty + slot_of(vi)));
+              if (next) {
+                if (lane == 0) FA_TRACE_AT(j, 1 + 2 * g);
+                issue_s(g, ki, qd);
+                commit(bar(L::kBarEmpty + slot_of(ki)));
+              }
+            }
+          }
+          // Q buffer qb may be refilled once this item's MMAs have completed
+          if (ok) commit(bar(L::kBarQFree + qb));
         }
+        cnt[0] += it.n_kv[0];
+        cnt[1] += it.n_kv[1];
+        ring += it.n_items;
       }
       // Drain: all MMAs issued above complete before TMEM is released.
       commit(bar(L::kBarDrain));
@@ -569,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       __syncwarp();
     }
 #ifdef FA_TRACE
-   } else if (lane == 0) {
+   } else if (lane == 0 && !dual) {
     // trace observers: warp 10 (group 0) / 11 (group 1) timestamp the
     // completion of every S and PV MMA of their group
     // (polling without suspension, so the timestamps are not delayed by a
@@ -582,7 +646,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       }
       return false;
     };
-    for (int j = 0; j < n_kv[og]; ++j) {
+    WorkItem it;  // shared mode: one work item per CTA
+    decode_item(p, blockIdx.x, it);
+    for (int j = 0; j < it.n_kv[og]; ++j) {
       if (!poll(bar(L::kBarS + og), j & 1)) break;
       FA_TRACE_AT(j, 24 + 2 * og);
       if (!poll(bar(L::kBarO + og), j & 1)) break;
@@ -595,10 +661,20 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     ptx::setmaxnreg_inc<kRegsSoftmax>();
     const int sw = warp - kWarpSoftmax0;        // softmax warp 0..7
     const int g = sw >> 2;
-    const int n_tiles = n_kv[g];
     const int wq = warp & 3;
     const int r = wq * 32 + lane;               // row within the tile == TMEM lane
-    const int tile = dual ? 2 * qp : 2 * qp + g;  // global 128-row tile index
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + L::tS(g);
+    const uint32_t tP = tmem + lane_off + L::tP(g);
+    const uint32_t tO = tmem + lane_off + L::tO(g);
+    const float sl = p.scale_log2;
+    bool ok = true;
+    int cnt = 0;  // S / P / O completions of this group before the work item
+    for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x) {
+    WorkItem it;
+    decode_item(p, w, it);
+    const int n_tiles = it.n_kv[g];
+    const int tile = dual ? 2 * it.qp : 2 * it.qp + g;  // global 128-row tile index
     const int q_row = tile * kBlockM + r;
     // causal limit of this row: key k is visible iff k < pos + causal_off + 1
     const int vis_end = q_row % p.pos_mod + p.causal_off + 1;
@@ -613,17 +689,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
                                                                 : lo % p.pos_mod;
       tile_vis_end = min_pos + p.causal_off + 1;
     }
-    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_off + L::tS(g);
-    const uint32_t tP = tmem + lane_off + L::tP(g);
-    const uint32_t tO = tmem + lane_off + L::tO(g);
-    const float sl = p.scale_log2;
 
     float m = -INFINITY;  // running max of the scaled scores (log2 units)
     float l = 0.f;        // running sum of exp2(s - m)
-    bool ok = n_tiles > 0;
     for (int j = 0; ok && j < n_tiles; ++j) {
-      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), j & 1, wc, 20 + g));
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), (cnt + j) & 1, wc, 20 + g));
       if (!ok) break;
       if (lane == 0) FA_TRACE_AT(j, 16 + sw);
       ptx::tc_fence_after();
@@ -649,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
       }
 
-      const int key0 = (jb[g] + j) * kBlockN;
+      const int key0 = (it.jb[g] + j) * kBlockN;
       const bool masked =
           (p.causal && key0 + kBlockN > tile_vis_end) || (key0 + kBlockN > p.Nk);
       // Scaled tile maximum.  Unmasked tiles reduce the raw scores and scale
@@ -719,9 +789,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     // ---- epilogue: O / l -> global (or the split workspace), LSE
     const bool row_ok = q_row < p.Nq;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    const size_t row_index = static_cast<size_t>(bh) * p.Nq + q_row;
+    const size_t row_index = static_cast<size_t>(it.bh) * p.Nq + q_row;
     // partial-result slot of this group (split mode) in the workspace
-    const int ws_slot = dual ? 2 * sp + g : sp;
+    const int ws_slot = dual ? 2 * it.sp + g : it.sp;
     const bool partial = p.n_splits > 1 || dual;
     if (n_tiles == 0) {
       // No visible key for these rows (causal offset below zero): O = 0 and
@@ -735,7 +805,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         if (p.lse != nullptr) p.lse[row_index] = -INFINITY;
       }
     } else {
-      if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarO + g), (n_tiles - 1) & 1, wc, 22 + g));
+      if (ok)
+        ok = __all_sync(0xffffffffu,
+                        bar_wait(bar(L::kBarO + g), (cnt + n_tiles - 1) & 1, wc, 22 + g));
       if (ok) {
         ptx::tc_fence_after();
         const float inv_l = (l > 0.f) ? 1.0f / l : 0.f;
@@ -782,6 +854,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           if (row_ok) p.ws_lse[ws_row] = lse_row;
         }
       }
+    }
+    cnt += n_tiles;
     }
   }
 
@@ -880,7 +954,8 @@ static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream
 }
 
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
-  const int grid = p.n_qpairs * p.B * p.heads * p.n_splits;
+  const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
+  const int grid = (p.n_ctas > 0 && p.n_ctas < n_work) ? p.n_ctas : n_work;
   if (head_dim == 64) return bf16 ? launch_impl<64, true>(p, grid, stream) : launch_impl<64, false>(p, grid, stream);
   return bf16 ? launch_impl<128, true>(p, grid, stream) : launch_impl<128, false>(p, grid, stream);
 }
