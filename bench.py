@@ -63,6 +63,9 @@ def parse_args():
     ap.add_argument("--kvcache-only", default=None, metavar="NAME|all",
                     help="time only fa_fwd_kvcache workloads (decode / chunked prefill) and print "
                          "their table as one JSON line (profiling runs)")
+    ap.add_argument("--backward-only", default=None, metavar="NAME|all",
+                    help="time only fa_bwd workloads (attention backward) and print their table "
+                         "as one JSON line (profiling runs)")
     return ap.parse_args()
 
 
@@ -298,6 +301,13 @@ def main():
             print(json.dumps({"kvcache": kvcache_configs(abi.load(), abi, dtype, dev, names)}),
                   flush=True)
         return
+    if args.backward_only:
+        if rank == 0:
+            dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+            names = None if args.backward_only == "all" else [args.backward_only]
+            print(json.dumps({"backward": backward_configs(abi.load(), abi, dtype, dev, names)}),
+                  flush=True)
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
@@ -375,6 +385,7 @@ def main():
         if world == 1:
             line["configs"] = other_configs(lib, abi, dtype, dev)
             line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
+            line["backward"] = backward_configs(lib, abi, dtype, dev)
     elif rank == 0:
         line["e2e"] = None
     if world > 1:
@@ -484,6 +495,60 @@ def kvcache_configs(lib, abi, dtype, dev, names=None):
                      "hbm_frac": round(byt / (ms * 1e-3) / 1e9 / hbm, 3),
                      "tflops": round(flops / ms / 1e9, 1), "splits_workspace_bytes": int(nbytes)}
         del q, k, v, o, lse, ws
+    return out
+
+
+# fa_bwd workloads (attention backward; no reference counterpart):
+# name -> (B, Hq, Hkv, N, d, causal)
+BACKWARD_CONFIGS = {
+    "bwd_c5": (4, 32, 32, 8192, 128, False),
+    "bwd_c5c": (4, 32, 32, 8192, 128, True),
+    "bwd_c4_gqa": (2, 32, 8, 4096, 128, True),
+    "bwd_c2_d64": (4, 12, 12, 1024, 64, False),
+}
+
+
+def backward_configs(lib, abi, dtype, dev, names=None):
+    """Kernel-only time of fa_bwd (prep + dK/dV + dQ kernels) on seeded N(0,1)
+    inputs, O and LSE from fa_fwd.  TFLOPS counts the five matrix products of
+    the FlashAttention-2 backward, 10*B*Hq*N^2*d (causal: the visible pairs
+    only); the kernels recompute S and dP in both passes (14*N^2*d executed)."""
+    import torch
+    out = {}
+    for name, (B, Hq, Hkv, N, d, causal) in BACKWARD_CONFIGS.items():
+        if names is not None and name not in names:
+            continue
+        g = torch.Generator(device=dev).manual_seed(11)
+        mk = lambda h: torch.randn(B, h, N, d, device=dev, dtype=torch.float32,
+                                   generator=g).to(dtype)
+        q, k, v, do = mk(Hq), mk(Hkv), mk(Hkv), mk(Hq)
+        o = torch.empty_like(q)
+        lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        nbytes = lib.fa_bwd_workspace_bytes(B, Hq, N)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+        s = torch.cuda.current_stream(dev)
+        scale = 1.0 / math.sqrt(d)
+        dt = 1 if dtype == torch.bfloat16 else 0
+        assert lib.fa_fwd(abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), abi.ptr(lse), B, Hq, Hkv,
+                          N, d, scale, int(causal), dt, abi.stream_ptr(s)) == 0
+        args = (abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), abi.ptr(do), abi.ptr(lse),
+                abi.ptr(dq), abi.ptr(dk), abi.ptr(dv), B, Hq, Hkv, N, d, scale, int(causal), dt,
+                abi.ptr(ws), nbytes, abi.stream_ptr(s))
+        fn = lambda: lib.fa_bwd(*args)
+        assert fn() == 0
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        pairs = N * (N + 1) / 2 if causal else float(N) * N
+        flops = 10.0 * B * Hq * d * pairs
+        n = max(10, min(500, int(4e12 / flops)))
+        ms = time_steps(fn, n, s) / n
+        if lib.fa_device_status(0) != 0:
+            raise RuntimeError("device watchdog fired in fa_bwd")
+        out[name] = {"tflops": round(flops / ms / 1e9, 1), "us": round(ms * 1e3, 2),
+                     "shape": f"B={B} Hq={Hq} Hkv={Hkv} N={N} d={d} causal={int(causal)}"}
+        del q, k, v, do, o, lse, dq, dk, dv, ws
     return out
 
 

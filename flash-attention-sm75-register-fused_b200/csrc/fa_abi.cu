@@ -58,9 +58,32 @@ bool make_map(CUtensorMap* map, const void* base, int d, int n, long long bh, bo
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+PFN_cuCtxGetCurrent_v4000 ctx_get_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(ptr);
+  });
+  return fn;
+}
+
+// Checks that the current device is an sm_100 part and that its primary
+// context is current on the calling thread.  The tensor-map encoder is a
+// driver call that needs a current context, and a thread that has only
+// touched cached allocations (PyTorch's autograd worker, a fresh host
+// thread) may not have one yet; cudaSetDevice binds the primary context.
 int check_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  CUcontext ctx = nullptr;
+  const auto get_ctx = ctx_get_fn();
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+    if (cudaSetDevice(dev) != cudaSuccess) return FA_ERR_CUDA;
+  }
   static int major_cache[64] = {0};
   int major = (dev >= 0 && dev < 64) ? major_cache[dev] : 0;
   if (major == 0) {
@@ -315,6 +338,63 @@ int fa_fwd_kvcache(const void* Q, const void* K, const void* V, void* O, float* 
   if (empty) return FA_OK;
   return launch_attention(Q, K, V, O, lse, B, Hq, Hkv, Nq, Nk, head_dim, scale, causal, dtype,
                           workspace, workspace_bytes, stream);
+}
+
+size_t fa_bwd_workspace_bytes(int B, int Hq, int N) {
+  if (B <= 0 || Hq <= 0 || N <= 0) return 0;
+  const size_t n_pad = (static_cast<size_t>(N) + 127) / 128 * 128;
+  return 2 * static_cast<size_t>(B) * Hq * n_pad * sizeof(float);
+}
+
+int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+           const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
+           int head_dim, float scale, int causal, int dtype, void* workspace,
+           size_t workspace_bytes, void* stream) {
+  if (B < 0 || Hq < 0 || Hkv < 0 || N < 0) return FA_ERR_INVALID_ARG;
+  if (head_dim != 64 && head_dim != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_DTYPE;
+  if (causal != 0 && causal != 1) return FA_ERR_INVALID_ARG;
+  if (B == 0 || Hq == 0 || N == 0) return FA_OK;
+  if (Hkv == 0) return FA_ERR_INVALID_ARG;
+  if (Hq % Hkv != 0) return FA_ERR_GQA_DIVISIBILITY;
+  if (!Q || !K || !V || !O || !dO || !lse || !dQ || !dK || !dV || !workspace)
+    return FA_ERR_INVALID_ARG;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(dO) ||
+      !aligned16(dQ) || !aligned16(dK) || !aligned16(dV) || !aligned16(workspace) ||
+      (reinterpret_cast<uintptr_t>(lse) & 3u))
+    return FA_ERR_ALIGNMENT;
+  if (workspace_bytes < fa_bwd_workspace_bytes(B, Hq, N)) return FA_ERR_INVALID_ARG;
+  if (!std::isfinite(scale)) return FA_ERR_INVALID_ARG;
+  const long long n_tiles = (static_cast<long long>(N) + 127) / 128;
+  if (N > (1 << 30) || static_cast<long long>(B) * Hq * n_tiles > 0x7fffffffLL)
+    return FA_ERR_TOO_LARGE;
+  if (int rc = check_device()) return rc;
+
+  fa::BwdParams p;
+  const bool bf16 = dtype == FA_DTYPE_BF16;
+  const long long bhq = static_cast<long long>(B) * Hq, bhk = static_cast<long long>(B) * Hkv;
+  if (!make_map(&p.tm_q, Q, head_dim, N, bhq, bf16) || !make_map(&p.tm_do, dO, head_dim, N, bhq, bf16) ||
+      !make_map(&p.tm_k, K, head_dim, N, bhk, bf16) || !make_map(&p.tm_v, V, head_dim, N, bhk, bf16))
+    return FA_ERR_TENSOR_MAP;
+  p.dq = dQ;
+  p.dk = dK;
+  p.dv = dV;
+  p.n_tiles = static_cast<int>(n_tiles);
+  p.n_pad = p.n_tiles * 128;
+  p.l2 = static_cast<const float*>(workspace);
+  p.dd = static_cast<const float*>(workspace) + static_cast<size_t>(bhq) * p.n_pad;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.N = N;
+  p.group = Hq / Hkv;
+  p.causal = causal;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
+  p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+  const cudaError_t e = fa::launch_bwd(p, O, dO, lse, head_dim, bf16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
 size_t fa_fwd_kvcache_workspace_bytes(int B, int Hq, int Hkv, int Nq, int Nk, int head_dim) {

@@ -63,7 +63,27 @@ __host__ __device__ inline int kv_tiles_for_tile(const FwdParams& p, int t) {
   return n < p.n_kv_tiles ? static_cast<int>(n) : p.n_kv_tiles;
 }
 
+// Backward parameters (dK/dV and dQ kernels).  Q, K, V, dO as 3-D TMA maps
+// like the forward; l2 / dd hold per query row LSE*log2(e) (+inf past N) and
+// rowsum(dO * O) (0 past N), each [B*Hq][n_pad] with n_pad = 128 * n_tiles.
+struct alignas(64) BwdParams {
+  CUtensorMap tm_q, tm_k, tm_v, tm_do;
+  void* dq;          // [B, Hq, N, d]
+  void* dk;          // [B, Hkv, N, d]
+  void* dv;          // [B, Hkv, N, d]
+  const float* l2;
+  const float* dd;
+  int B, Hq, Hkv, N, n_pad, group, n_tiles, causal;
+  float scale, scale_log2;
+  unsigned epoch;
+  unsigned long long timeout_ns;
+};
+
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream);
+// dD / L2 preprocessing (reads O, dO, LSE) and the two backward kernels.
+cudaError_t launch_bwd(const BwdParams& p, const void* o, const void* dout, const float* lse,
+                       int head_dim, bool bf16, cudaStream_t stream);
+int bwd_smem_bytes_for(int head_dim);
 // Merges the n_splits partial results of p.ws_o / p.ws_lse into p.o / p.lse.
 cudaError_t launch_combine(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream);
 int smem_bytes_for(int head_dim);

@@ -988,3 +988,6 @@ cudaError_t read_status(unsigned long long* out, bool reset) {
 }
 
 }  // namespace fa
+
+// Backward kernels (same translation unit: they share the device helpers above).
+#include "fa_bwd_sm100.cuh"

@@ -206,6 +206,52 @@ std::tuple<torch::Tensor, torch::Tensor> flash_attention_forward_kvcache(
   return {O, lse};
 }
 
+// Gradients of flash_attention_forward_lse: (dQ, dK, dV) from dO, the inputs,
+// the forward's O and LSE.  The workspace comes from PyTorch's allocator.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> flash_attention_backward(
+    torch::Tensor dO, torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor O,
+    torch::Tensor lse, bool causal, float scale) {
+  check_tensor(Q, "Q", true);
+  check_tensor(K, "K", true);
+  check_tensor(V, "V", true);
+  check_tensor(O, "O", true);
+  check_tensor(dO, "dO", true);
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype() && Q.dtype() == O.dtype() &&
+                  Q.dtype() == dO.dtype(),
+              "Q, K, V, O, dO must share a dtype");
+  TORCH_CHECK(O.sizes() == Q.sizes() && dO.sizes() == Q.sizes(), "O and dO must have Q's shape");
+  TORCH_CHECK(K.sizes() == V.sizes() && Q.size(0) == K.size(0) && Q.size(2) == K.size(2) &&
+                  Q.size(3) == K.size(3),
+              "K, V shapes do not match Q");
+  TORCH_CHECK(lse.is_cuda() && lse.dtype() == torch::kFloat32 && lse.is_contiguous() &&
+                  lse.dim() == 3 && lse.size(0) == Q.size(0) && lse.size(1) == Q.size(1) &&
+                  lse.size(2) == Q.size(2),
+              "lse must be a contiguous fp32 CUDA tensor [B, Hq, N]");
+  const auto head_dim = Q.size(3);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && Q.size(1) <= INT32_MAX && Q.size(2) <= INT32_MAX,
+              "size exceeds int32");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  const int B = static_cast<int>(Q.size(0)), Hq = static_cast<int>(Q.size(1));
+  const int N = static_cast<int>(Q.size(2));
+  auto dQ = torch::empty_like(Q);
+  auto dK = torch::empty_like(K);
+  auto dV = torch::empty_like(V);
+  const size_t ws_bytes = fa_bwd_workspace_bytes(B, Hq, N);
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes > 0 ? ws_bytes : 16)},
+                         Q.options().dtype(torch::kUInt8));
+  const int rc = fa_bwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), dO.data_ptr(),
+                        lse.data_ptr<float>(), dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), B, Hq,
+                        static_cast<int>(K.size(1)), N, static_cast<int>(head_dim), scale,
+                        causal ? 1 : 0, Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16,
+                        ws.data_ptr(), ws_bytes, stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_backward: ", fa_error_string(rc));
+  return {dQ, dK, dV};
+}
+
 int device_status(bool reset) { return fa_device_status(reset ? 1 : 0); }
 
 }  // namespace
@@ -220,6 +266,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attention_forward_out", &flash_attention_forward_out, pybind11::arg("Q"),
         pybind11::arg("K"), pybind11::arg("V"), pybind11::arg("O"), pybind11::arg("lse"),
         pybind11::arg("causal"), pybind11::arg("scale"));
+  m.def("flash_attention_backward", &flash_attention_backward,
+        "(dQ, dK, dV) from dO, Q, K, V, O, LSE (fp32 [B, Hq, N]), causal, scale");
   m.def("flash_attention_forward_kvcache", &flash_attention_forward_kvcache,
         "O, LSE of Nq queries against Nk cached keys; causal: 0 none, 1 bottom-right, 2 top-left");
   m.def("device_status", &device_status, pybind11::arg("reset") = false,

@@ -19,6 +19,9 @@ SIGNATURES = {
     "fa_fwd_kvcache": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                                c_int, c_float, c_int, c_int, c_vp, ctypes.c_size_t, c_vp]),
     "fa_fwd_kvcache_workspace_bytes": (ctypes.c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "fa_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
+                       c_int, c_int, c_float, c_int, c_int, c_vp, ctypes.c_size_t, c_vp]),
+    "fa_bwd_workspace_bytes": (ctypes.c_size_t, [c_int, c_int, c_int]),
     "launch_flash_attention_forward": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
                                               c_float, c_bool]),
     "launch_flash_attention_forward_scalar": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
@@ -106,3 +109,21 @@ def fa_fwd_kvcache(q, k, v, o, lse=None, causal=CAUSAL_NONE, scale=None, stream=
     return lib.fa_fwd_kvcache(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), B, Hq, Hkv, Nq, Nk, d,
                               float(scale), int(causal), dtype, ptr(ws), nbytes,
                               stream_ptr(stream))
+
+
+def fa_bwd(q, k, v, o, do, lse, dq, dk, dv, causal=False, scale=None, stream=None):
+    """Call fa_bwd on torch CUDA tensors ([B, H, N, d]; lse [B, Hq, N] fp32);
+    allocates the workspace.  Returns the status."""
+    import math
+    import torch
+    B, Hq, N, d = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    lib = load()
+    nbytes = lib.fa_bwd_workspace_bytes(B, Hq, N)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    return lib.fa_bwd(ptr(q), ptr(k), ptr(v), ptr(o), ptr(do), ptr(lse), ptr(dq), ptr(dk), ptr(dv),
+                      B, Hq, Hkv, N, d, float(scale), int(bool(causal)), dtype, ptr(ws), nbytes,
+                      stream_ptr(stream))

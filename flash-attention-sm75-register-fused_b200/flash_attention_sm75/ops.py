@@ -22,6 +22,9 @@ Differences that a caller can observe only as speed or as extra options:
 * ``flash_attention_forward_host`` takes Q, K, V in host memory and returns O
   in host memory, overlapping the PCIe copies of each (batch, KV-head group)
   chunk with the computation of the others.
+* ``flash_attention`` is the same forward with a backward pass (dQ, dK, dV
+  from the saved LSE); ``flash_attention_forward`` keeps the reference's
+  forward-only Function.
 
 There is no CPU path: the CUDA extension must load, or the import fails.
 """
@@ -232,3 +235,42 @@ def flash_attention_forward_host(Q, K, V, causal=False, scale=None, out=None, de
         cur.wait_stream(s_out)
         s_out.synchronize()
     return out
+
+
+class FlashAttentionFunction(torch.autograd.Function):
+    """Forward and backward (no reference counterpart: the reference's Function
+    raises in backward, ops.py:47-52)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, causal, scale):
+        _check_gqa(Q.size(1), K.size(1))
+        Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+        out, lse = _C.flash_attention_forward_lse(Q, K, V, bool(causal), float(scale))
+        ctx.save_for_backward(Q, K, V, out, lse)
+        ctx.causal, ctx.scale = bool(causal), float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, out, lse = ctx.saved_tensors
+        dQ, dK, dV = _C.flash_attention_backward(dO.contiguous(), Q, K, V, out, lse, ctx.causal,
+                                                 ctx.scale)
+        return dQ, dK, dV, None, None
+
+
+def flash_attention(Q, K, V, causal=False, scale=None):
+    """``flash_attention_forward`` with autograd support (dQ, dK, dV on the GPU).
+
+    Same arguments and checks as ``flash_attention_forward`` (Q [B, Hq, N, D],
+    K/V [B, Hkv, N, D], D in {64, 128}, fp16/bf16, top-left causal).
+    """
+    if Q.dim() != 4:
+        raise ValueError("Q must be 4D [B, H, N, D]")
+    head_dim = Q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    return FlashAttentionFunction.apply(Q, K, V, causal, scale)

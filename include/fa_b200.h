@@ -91,6 +91,24 @@ int fa_fwd_kvcache(const void* Q, const void* K, const void* V, void* O, float* 
 /* Workspace bytes fa_fwd_kvcache needs to split this problem (0: no split). */
 size_t fa_fwd_kvcache_workspace_bytes(int B, int Hq, int Hkv, int Nq, int Nk, int head_dim);
 
+/*
+ * fa_bwd — gradients of fa_fwd (square, causal 0/1 top-left, GQA): from Q, K, V,
+ * the forward's O and LSE ([B, Hq, N] fp32, natural log) and dO = dL/dO, writes
+ * dQ [B, Hq, N, d], dK and dV [B, Hkv, N, d] (GQA: summed over each group's
+ * query heads).  `workspace` (16-byte aligned) needs fa_bwd_workspace_bytes()
+ * bytes.  Asynchronous on `stream`; same error codes as fa_fwd.
+ *
+ * No reference counterpart: the reference's autograd Function raises in
+ * backward (reference src/flash_attention_sm75/ops.py:47-52).
+ */
+int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+           const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
+           int head_dim, float scale, int causal, int dtype, void* workspace,
+           size_t workspace_bytes, void* stream);
+
+/* Workspace bytes of fa_bwd: per query row LSE*log2(e) and rowsum(dO*O), padded to 128 rows. */
+size_t fa_bwd_workspace_bytes(int B, int Hq, int N);
+
 /* ---- reference-compatible launchers (void, fp16, blocking) ----
  * Same signatures and conventions as the reference: errors are printed to
  * stderr, the work runs on the legacy default stream and the call ends with

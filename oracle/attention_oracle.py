@@ -215,3 +215,51 @@ def check_lse(lse: torch.Tensor, ref: torch.Tensor, atol: float = LSE_ATOL):
     err = (lse.float() - ref.float()).abs()
     m = err.max().item() if err.numel() else 0.0
     return {"max_abs_err": m, "ok": bool(m <= atol)}
+
+
+def attention_grads_fp32(Q, K, V, dO, causal=False, scale=None):
+    """dQ, dK, dV of the fp32 attention (attention_ref.py:10-45 restated with
+    autograd) for the upstream gradient dO.  GQA K/V are expanded by
+    repeat_interleave, so their gradients are summed over each group.
+    Materialises the N x N scores: small sizes only."""
+    B, Hq, N, d = Q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    q = Q.detach().float().requires_grad_(True)
+    k = K.detach().float().requires_grad_(True)
+    v = V.detach().float().requires_grad_(True)
+    kx, vx = expand_kv_for_gqa(Hq, k, v)
+    s = torch.matmul(q, kx.transpose(-2, -1)) * scale
+    if causal:
+        mask = torch.triu(torch.ones(N, k.size(2), dtype=torch.bool), diagonal=1)
+        s = s.masked_fill(mask, float("-inf"))
+    o = torch.matmul(torch.softmax(s, dim=-1), vx)
+    o.backward(dO.float())
+    return q.grad, k.grad, v.grad
+
+
+def attention_grads_formulas(Q, K, V, dO, causal=False, scale=None):
+    """The same gradients from the FlashAttention-2 backward formulas
+    (P, D = rowsum(dO * O), dS = P * (dP - D), dQ = scale dS K, dK = scale dS^T Q,
+    dV = P^T dO), used to cross-check attention_grads_fp32."""
+    B, Hq, N, d = Q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    G = Hq // K.size(1)
+    kx, vx = expand_kv_for_gqa(Hq, K.float(), V.float())
+    q, do = Q.float(), dO.float()
+    s = torch.matmul(q, kx.transpose(-2, -1)) * scale
+    if causal:
+        mask = torch.triu(torch.ones(N, K.size(2), dtype=torch.bool), diagonal=1)
+        s = s.masked_fill(mask, float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    o = torch.matmul(p, vx)
+    dd = (do * o).sum(-1, keepdim=True)
+    dv = torch.matmul(p.transpose(-2, -1), do)
+    dp = torch.matmul(do, vx.transpose(-2, -1))
+    ds = p * (dp - dd)
+    dq = torch.matmul(ds, kx) * scale
+    dk = torch.matmul(ds.transpose(-2, -1), q) * scale
+    dk = dk.view(B, K.size(1), G, N, d).sum(2)
+    dv = dv.view(B, K.size(1), G, N, d).sum(2)
+    return dq, dk, dv

@@ -8,9 +8,9 @@ from flash_attention_sm75 import ops
 
 
 def test_public_surface():
-    # the reference's surface (src/flash_attention_sm75/__init__.py:1-4) plus two additions
+    # the reference's surface (src/flash_attention_sm75/__init__.py:1-4) plus additions
     assert fa.__all__ == ["flash_attention_forward", "flash_attention_forward_kvcache",
-                          "flash_attention_forward_host"]
+                          "flash_attention_forward_host", "flash_attention"]
     assert isinstance(fa.__version__, str)
 
 
