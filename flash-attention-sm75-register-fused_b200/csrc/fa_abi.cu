@@ -281,7 +281,12 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
       !make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16))
     return FA_ERR_TENSOR_MAP;
   p.o = O;
+  p.o_rs = head_dim;
   p.lse = lse;
+  p.ranges = 0;
+  p.causal_br = 0;
+  p.q_lim = p.k_lim = 0;
+  p.q_lo = p.q_hi = p.k_lo = p.k_hi = nullptr;
   p.B = B;
   p.heads = k.heads;
   p.Hkv = Hkv;
@@ -309,6 +314,83 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (fa::launch_fwd(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
   if (use_ws && fa::launch_combine(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
+  return FA_OK;
+}
+
+// [T, H, d] packed rows viewed as 3-D (d, H, T) with a (64, 1, 128) box: one
+// head's 128 consecutive tokens, laid out in shared memory exactly like a
+// (64, 128, 1) box of make_map.  Rows >= T read as zeros.
+bool make_map_packed(CUtensorMap* map, const void* base, int d, int h, long long t, bool bf16) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(h),
+                              static_cast<cuuint64_t>(t)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
+                                 static_cast<cuuint64_t>(h) * static_cast<cuuint64_t>(d) * 2};
+  const cuuint32_t box[3] = {64, 1, 128};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r =
+      fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Launch of the attention kernel over per-batch row ranges (fa_fwd_varlen:
+// packed = true; fa_fwd_padded: packed = false).  Nq / Nk are the largest
+// sequence lengths (padded: the padded lengths); q_lim / k_lim bound the rows.
+int launch_ranged(bool packed, const void* Q, const void* K, const void* V, void* O, float* lse,
+                  const int* q_lo, const int* q_hi, const int* k_lo, const int* k_hi, int B,
+                  int Hq, int Hkv, int Nq, int Nk, int q_lim, int k_lim, int head_dim,
+                  float scale, int causal, int dtype, void* stream) {
+  const bool bf16 = dtype == FA_DTYPE_BF16;
+  fa::FwdParams p;
+  const bool maps_ok =
+      packed ? (make_map_packed(&p.tm_q, Q, head_dim, Hq, q_lim, bf16) &&
+                make_map_packed(&p.tm_k, K, head_dim, Hkv, k_lim > 0 ? k_lim : 1, bf16) &&
+                make_map_packed(&p.tm_v, V, head_dim, Hkv, k_lim > 0 ? k_lim : 1, bf16))
+             : (make_map(&p.tm_q, Q, head_dim, Nq, static_cast<long long>(B) * Hq, bf16) &&
+                make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16) &&
+                make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16));
+  if (!maps_ok) return FA_ERR_TENSOR_MAP;
+  p.o = O;
+  p.o_rs = packed ? Hq * head_dim : head_dim;
+  p.lse = lse;
+  p.ranges = packed ? 1 : 2;
+  p.causal_br = causal == FA_CAUSAL_BOTTOM_RIGHT ? 1 : 0;
+  p.q_lim = q_lim;
+  p.k_lim = k_lim;
+  p.q_lo = q_lo;
+  p.q_hi = q_hi;
+  p.k_lo = k_lo;
+  p.k_hi = k_hi;
+  p.B = B;
+  p.heads = Hq;
+  p.Hkv = Hkv;
+  p.Nq = Nq;
+  p.Nk = Nk;
+  p.group = Hq / Hkv;
+  p.n_qpairs = (Nq + 255) / 256;
+  p.n_kv_tiles = (Nk + 127) / 128;
+  p.causal = causal != FA_CAUSAL_NONE ? 1 : 0;
+  // packed: per-sequence offsets come from causal_br in the kernel; padded:
+  // the rule of the full padded rows
+  p.causal_off = (!packed && causal == FA_CAUSAL_BOTTOM_RIGHT) ? Nk - Nq : 0;
+  p.pos_mod = 0x7fffffff;
+  p.n_splits = 1;
+  p.tiles_per_split = p.n_kv_tiles;
+  p.dual = 0;
+  p.n_ctas = 0;
+  p.ws_o = nullptr;
+  p.ws_lse = nullptr;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.debug_flags = g_debug_flags.load(std::memory_order_relaxed);
+  p.trace = g_trace.load(std::memory_order_relaxed);
+  p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
+  p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+  if (fa::launch_fwd(p, head_dim, bf16, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return FA_ERR_LAUNCH;
   return FA_OK;
 }
 
@@ -395,6 +477,45 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaError_t e = fa::launch_bwd(p, O, dO, lse, head_dim, bf16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+int fa_fwd_varlen(const void* Q, const void* K, const void* V, void* O, float* lse,
+                  const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                  int total_q, int total_k, int max_seqlen_q, int max_seqlen_k, int head_dim,
+                  float scale, int causal, int dtype, void* stream) {
+  if (total_q < 0 || total_k < 0 || max_seqlen_q < 0 || max_seqlen_k < 0)
+    return FA_ERR_INVALID_ARG;
+  bool empty = false;
+  // the shape checks of a [B, Hq, max_seqlen_q, d] call; rows then come from
+  // the offsets
+  if (int rc = check_args(Q, K, V, O, lse, B, Hq, Hkv, max_seqlen_q, max_seqlen_k > 0 ? max_seqlen_k : 1,
+                          head_dim, scale, causal, dtype, &empty))
+    return rc;
+  if (empty || total_q == 0) return FA_OK;
+  if (!cu_seqlens_q || !cu_seqlens_k) return FA_ERR_INVALID_ARG;
+  if (static_cast<long long>(total_q) * Hq * head_dim > (1LL << 40) ||
+      static_cast<long long>(total_k) * Hkv * head_dim > (1LL << 40))
+    return FA_ERR_TOO_LARGE;
+  // total_k = 0: every key range clamps to empty, so every row gets O = 0 and
+  // LSE = -inf and K/V are never read (their maps still need one row)
+  return launch_ranged(true, Q, K, V, O, lse, cu_seqlens_q, cu_seqlens_q + 1, cu_seqlens_k,
+                       cu_seqlens_k + 1, B, Hq, Hkv, max_seqlen_q,
+                       max_seqlen_k > 0 ? max_seqlen_k : 1, total_q, total_k, head_dim, scale,
+                       causal, dtype, stream);
+}
+
+int fa_fwd_padded(const void* Q, const void* K, const void* V, void* O, float* lse,
+                  const int* q_start, const int* q_end, const int* k_start, const int* k_end,
+                  int B, int Hq, int Hkv, int Nq, int Nk, int head_dim, float scale, int causal,
+                  int dtype, void* stream) {
+  bool empty = false;
+  if (int rc = check_args(Q, K, V, O, lse, B, Hq, Hkv, Nq, Nk, head_dim, scale, causal, dtype,
+                          &empty))
+    return rc;
+  if (empty) return FA_OK;
+  if (!q_start || !q_end || !k_start || !k_end) return FA_ERR_INVALID_ARG;
+  return launch_ranged(false, Q, K, V, O, lse, q_start, q_end, k_start, k_end, B, Hq, Hkv, Nq,
+                       Nk, Nq, Nk, head_dim, scale, causal, dtype, stream);
 }
 
 size_t fa_fwd_kvcache_workspace_bytes(int B, int Hq, int Hkv, int Nq, int Nk, int head_dim) {

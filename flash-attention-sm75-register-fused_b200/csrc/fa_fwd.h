@@ -14,7 +14,8 @@ struct alignas(64) FwdParams {
   CUtensorMap tm_q;  // 3-D (d, Nq, B*heads), box (64, 128, 1), 128-byte swizzle
   CUtensorMap tm_k;  // 3-D (d, Nk, B*Hkv)
   CUtensorMap tm_v;  // 3-D (d, Nk, B*Hkv)
-  void* o;           // [B*heads, Nq, d] f16/bf16
+  void* o;           // [B*heads, Nq, d] f16/bf16 (packed varlen: [total_q, heads, d])
+  int o_rs;          // elements between consecutive query rows of one head in O
   float* lse;        // [B*heads, Nq] fp32 or nullptr
   // Query rows are grouped as (batch*heads, Nq).  Unpacked: heads = Hq,
   // Nq = the query length.  GQA-packed (short queries): heads = Hkv and the
@@ -38,6 +39,28 @@ struct alignas(64) FwdParams {
   float* ws_o;       // partial O [n_splits * (1 + dual)][B*heads][Nq][d] fp32 (normalised)
   float* ws_lse;     // partial LSE [n_splits * (1 + dual)][B*heads][Nq] (natural log)
   float scale_log2;  // scale * log2(e)
+  // Per-batch row ranges (ranges != 0; no packing, split or dual mode then).
+  // Sequence b's queries are rows [q_lo[b], q_hi[b]) and its keys rows
+  // [k_lo[b], k_hi[b]); Nq / Nk are the largest lengths (they size the grid).
+  //   ranges = 1, packed varlen: Q/O [total_q, heads, d], K/V [total_k, Hkv, d]
+  //     (maps (d, H, T), box (64, 1, 128)); q_lo = cu_seqlens_q, q_hi =
+  //     cu_seqlens_q + 1; LSE [heads, q_lim]; causal_off is added to the
+  //     per-sequence offset nk - nq (bottom-right) or 0 (top-left), chosen by
+  //     causal_br.
+  //   ranges = 2, padded batch: the fixed [B, heads, N, d] layout with valid
+  //     rows [lo, hi) per batch entry; the causal rule stays that of the full
+  //     padded rows (key j visible to row i iff j <= i + causal_off).
+  // Rows outside a sequence's range are not written.
+  // Rows are clamped to [0, q_lim) / [0, k_lim) (packed: total_q / total_k,
+  // padded: Nq / Nk), so no range reaches outside the tensors.  Query rows of
+  // a sequence past the grid's 256*n_qpairs rows are not computed.
+  int ranges;
+  int causal_br;
+  int q_lim, k_lim;
+  const int* q_lo;
+  const int* q_hi;
+  const int* k_lo;
+  const int* k_hi;
   int debug_flags;
   long long* trace;  // timeline samples, used only in FA_TRACE builds
   unsigned epoch;    // launch counter, tags device status words
@@ -47,20 +70,28 @@ struct alignas(64) FwdParams {
 // Number of K/V tiles a 128-row query tile t needs (all tiles when not causal).
 // Shared by the attention kernel and the split combine so that both agree on
 // which splits hold data for a row.
-__host__ __device__ inline int kv_tiles_for_tile(const FwdParams& p, int t) {
-  if (!p.causal) return p.n_kv_tiles;
+// nq query rows, n_kv K/V tiles, key j visible to row r iff
+// j <= r % pos_mod + causal_off (causal).  Tiles past the last row need none.
+__host__ __device__ inline int kv_tiles_core(int causal, int nq, int n_kv, int causal_off,
+                                             int pos_mod, int t) {
   const int lo = t * 128;
-  const int hi = (lo + 127 < p.Nq - 1) ? lo + 127 : p.Nq - 1;
+  if (lo >= nq) return 0;
+  if (!causal) return n_kv;
+  const int hi = (lo + 127 < nq - 1) ? lo + 127 : nq - 1;
   int max_pos;
-  if (p.pos_mod >= p.Nq) {
+  if (pos_mod >= nq) {
     max_pos = hi;
   } else {
-    max_pos = (hi / p.pos_mod != lo / p.pos_mod) ? p.pos_mod - 1 : hi % p.pos_mod;
+    max_pos = (hi / pos_mod != lo / pos_mod) ? pos_mod - 1 : hi % pos_mod;
   }
-  const long long kmax = static_cast<long long>(max_pos) + p.causal_off;  // last visible key
+  const long long kmax = static_cast<long long>(max_pos) + causal_off;  // last visible key
   if (kmax < 0) return 0;
   const long long n = kmax / 128 + 1;
-  return n < p.n_kv_tiles ? static_cast<int>(n) : p.n_kv_tiles;
+  return n < n_kv ? static_cast<int>(n) : n_kv;
+}
+
+__host__ __device__ inline int kv_tiles_for_tile(const FwdParams& p, int t) {
+  return kv_tiles_core(p.causal, p.Nq, p.n_kv_tiles, p.causal_off, p.pos_mod, t);
 }
 
 // Backward parameters (dK/dV and dQ kernels).  Q, K, V, dO as 3-D TMA maps

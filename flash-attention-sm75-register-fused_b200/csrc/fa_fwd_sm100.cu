@@ -281,7 +281,36 @@ struct WorkItem {
   int jb[2];    // first K/V tile of group g
   int n_loop;   // max(n_kv)
   int n_items;  // K/V ring items the item loads
+  // The item's sequence: nq query rows and nk keys (local row r, key j).
+  int nq, nk;
+  int causal_off;      // key j visible to local row r iff j <= r % pos_mod + causal_off
+  int qy, qz, ky, kz;  // TMA row base and plane (head) of Q and K/V
 };
+
+// O element offset (rows o_rs apart) and LSE index (rows 1 apart) of local
+// query row 0 of work item w, and its number of query rows.  Recomputed for
+// the epilogue rather than kept live through the softmax loop.
+__device__ __forceinline__ void item_out(const FwdParams& p, int w, long long& o_row0,
+                                         long long& lse_row0, int& nq) {
+  const int bh = (w / p.n_splits) / p.n_qpairs;
+  if (p.ranges == 0) {
+    nq = p.Nq;
+    lse_row0 = static_cast<long long>(bh) * p.Nq;
+    o_row0 = lse_row0 * p.o_rs;
+    return;
+  }
+  const int b = bh / p.heads;
+  const int ql = min(max(__ldg(p.q_lo + b), 0), p.q_lim);
+  nq = min(max(__ldg(p.q_hi + b), ql), p.q_lim) - ql;
+  if (p.ranges == 1) {
+    const int hq = bh % p.heads;
+    o_row0 = static_cast<long long>(ql) * p.o_rs + static_cast<long long>(hq) * (p.o_rs / p.heads);
+    lse_row0 = static_cast<long long>(hq) * p.q_lim + ql;
+  } else {
+    lse_row0 = static_cast<long long>(bh) * p.Nq + ql;
+    o_row0 = lse_row0 * p.o_rs;
+  }
+}
 
 __device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem& it) {
   it.sp = w % p.n_splits;
@@ -294,12 +323,42 @@ __device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem&
   const int hq = it.bh % p.heads;
   it.bh_kv = b * p.Hkv + hq / p.group;
   it.q_row0 = qp * 2 * kBlockM;
-  it.has_q1 = it.q_row0 + kBlockM < p.Nq;
+  int n_kv_tiles = p.n_kv_tiles;
+  if (p.ranges == 0) {
+    it.nq = p.Nq;
+    it.nk = p.Nk;
+    it.causal_off = p.causal_off;
+    it.qy = 0;
+    it.qz = it.bh;
+    it.ky = 0;
+    it.kz = it.bh_kv;
+  } else {
+    const int ql = min(max(__ldg(p.q_lo + b), 0), p.q_lim);
+    const int kl = min(max(__ldg(p.k_lo + b), 0), p.k_lim);
+    it.nq = min(max(__ldg(p.q_hi + b), ql), p.q_lim) - ql;
+    it.nk = min(max(__ldg(p.k_hi + b), kl), p.k_lim) - kl;
+    it.ky = kl;
+    it.qy = ql;
+    if (p.ranges == 1) {  // packed varlen: planes are heads, rows are tokens
+      it.causal_off = p.causal_off + (p.causal_br ? it.nk - it.nq : 0);
+      it.qz = hq;
+      it.kz = hq / p.group;
+    } else {  // padded batch: the absolute causal rule in local rows
+      it.causal_off = p.causal_off + ql - kl;
+      it.qz = it.bh;
+      it.kz = it.bh_kv;
+    }
+    n_kv_tiles = (it.nk + kBlockN - 1) / kBlockN;
+  }
+  it.has_q1 = it.q_row0 + kBlockM < it.nq;
+  auto tiles_of = [&](int t) {
+    return kv_tiles_core(p.causal, it.nq, n_kv_tiles, it.causal_off, p.pos_mod, t);
+  };
   const int j_begin = it.sp * p.tiles_per_split;
   if (p.dual) {
     // both groups on Q tile 0; the split's tiles are halved between them
     const int n =
-        max(0, min(kv_tiles_for_tile(p, 2 * qp), j_begin + p.tiles_per_split) - j_begin);
+        max(0, min(tiles_of(2 * qp), j_begin + p.tiles_per_split) - j_begin);
     it.n_kv[0] = (n + 1) / 2;
     it.n_kv[1] = n / 2;
     it.jb[0] = j_begin;
@@ -307,7 +366,7 @@ __device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem&
   } else {
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
-      const int total = (g == 0 || it.has_q1) ? kv_tiles_for_tile(p, 2 * qp + g) : 0;
+      const int total = (g == 0 || it.has_q1) ? tiles_of(2 * qp + g) : 0;
       it.n_kv[g] = max(0, min(total, j_begin + p.tiles_per_split) - j_begin);
       it.jb[g] = j_begin;
     }
@@ -338,7 +397,7 @@ __device__ __forceinline__ int tile_of_item(const WorkItem& it, bool dual, int i
     iter = it.n_kv[1] + ((i - 4 * it.n_kv[1]) >> 1);
     g = 0;
   }
-  return it.jb[g] + iter;
+  return (g ? it.jb[1] : it.jb[0]) + iter;
 }
 
 template <int D, bool BF16>
@@ -414,17 +473,25 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 #pragma unroll
             for (int c = 0; c < L::kColBlocks; ++c)
               ptx::tma_load_3d(sbase + L::kOffQ + qb * L::kTile + c * L::kBlockBytes, &p.tm_q,
-                               bar(L::kBarQ + qb), c * 64, it.q_row0, it.bh, pol_q);
-            ++q_loads[qb];
+                               bar(L::kBarQ + qb), c * 64, it.qy + it.q_row0, it.qz, pol_q);
+            if (qb) ++q_loads[1]; else ++q_loads[0];
           } else {
+            // a group without K/V tiles needs no Q (the MMA warp waits for
+            // Q tile g only when n_kv[g] > 0)
             for (int g = 0; g < 2; ++g) {
-              if (g == 1 && !it.has_q1) break;
+              if (it.n_kv[g] == 0) continue;
               ptx::mbar_arrive_expect_tx(bar(L::kBarQ + g), L::kTile);
+              const int row = it.qy + it.q_row0 + g * kBlockM;
 #pragma unroll
-              for (int c = 0; c < L::kColBlocks; ++c)
-                ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
-                                 bar(L::kBarQ + g), c * 64, it.q_row0 + g * kBlockM, it.bh,
-                                 pol_q);
+              for (int c = 0; c < L::kColBlocks; ++c) {
+                const int c0 = c * 64;
+                if (p.ranges == 1)
+                  ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
+                                   bar(L::kBarQ + g), c0, it.qz, row, pol_q);
+                else
+                  ptx::tma_load_3d(sbase + L::kOffQ + g * L::kTile + c * L::kBlockBytes, &p.tm_q,
+                                   bar(L::kBarQ + g), c0, row, it.qz, pol_q);
+              }
               ++q_loads[g];
             }
           }
@@ -442,10 +509,16 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           if ((i & 1) && !dual) FA_TRACE_AT(i >> 1, 30);                // V_j issued
           if (!(i & 1) && !dual && i > 0) FA_TRACE_AT((i >> 1) - 1, 31);  // K_{j+1} issued
           ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
+          const int row = it.ky + tile * kBlockN;
 #pragma unroll
-          for (int c = 0; c < L::kColBlocks; ++c)
-            ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
-                             tile * kBlockN, it.bh_kv, pol_kv);
+          for (int c = 0; c < L::kColBlocks; ++c) {
+            if (p.ranges == 1)
+              ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
+                               it.kz, row, pol_kv);
+            else
+              ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
+                               row, it.kz, pol_kv);
+          }
         }
       }
       // Drain: every copy this thread started must land before the CTA exits.
@@ -673,21 +746,24 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x) {
     WorkItem it;
     decode_item(p, w, it);
-    const int n_tiles = it.n_kv[g];
+    const int n_tiles = g ? it.n_kv[1] : it.n_kv[0];
+    const int jb = g ? it.jb[1] : it.jb[0];
     const int tile = dual ? 2 * it.qp : 2 * it.qp + g;  // global 128-row tile index
     const int q_row = tile * kBlockM + r;
-    // causal limit of this row: key k is visible iff k < pos + causal_off + 1
-    const int vis_end = q_row % p.pos_mod + p.causal_off + 1;
+    // key limit of this row: key k is visible iff k < row_end (causal:
+    // pos + causal_off + 1; always at most nk)
+    int row_end = it.nk;
     // smallest limit over the tile's rows: a K/V tile needs masking when any
-    // of its keys lies at or beyond it (or beyond Nk)
-    int tile_vis_end;
-    {
+    // of its keys lies at or beyond it
+    int tile_end = it.nk;
+    if (p.causal) {
+      row_end = min(row_end, q_row % p.pos_mod + it.causal_off + 1);
       const int lo = tile * kBlockM;
-      const int hi = min(lo + kBlockM - 1, p.Nq - 1);
-      const int min_pos = (p.pos_mod >= p.Nq)                   ? lo
+      const int hi = min(lo + kBlockM - 1, it.nq - 1);
+      const int min_pos = (p.pos_mod >= it.nq)                  ? lo
                           : (hi / p.pos_mod != lo / p.pos_mod) ? 0
                                                                 : lo % p.pos_mod;
-      tile_vis_end = min_pos + p.causal_off + 1;
+      tile_end = min(tile_end, min_pos + it.causal_off + 1);
     }
 
     float m = -INFINITY;  // running max of the scaled scores (log2 units)
@@ -719,17 +795,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
       }
 
-      const int key0 = (it.jb[g] + j) * kBlockN;
-      const bool masked =
-          (p.causal && key0 + kBlockN > tile_vis_end) || (key0 + kBlockN > p.Nk);
+      const int key0 = (jb + j) * kBlockN;
+      const bool masked = key0 + kBlockN > tile_end;
       // Scaled tile maximum.  Unmasked tiles reduce the raw scores and scale
       // once (the exponent then folds scale and max into one packed FMA);
       // masked tiles are pre-scaled so that -inf marks excluded keys.
       float m_tile;
       float sl_eff = sl;
       if (masked) {
-        int lim = p.Nk - key0;
-        if (p.causal) lim = min(lim, vis_end - key0);
+        const int lim = row_end - key0;
 #pragma unroll
         for (int c = 0; c < kBlockN; c += 2) ptx::fmul2(x[c], x[c + 1], x[c], x[c + 1], sl, sl);
 #pragma unroll
@@ -787,9 +861,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     }
 
     // ---- epilogue: O / l -> global (or the split workspace), LSE
-    const bool row_ok = q_row < p.Nq;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    const size_t row_index = static_cast<size_t>(it.bh) * p.Nq + q_row;
+    long long o_row0, lse_row0;
+    int nq;
+    item_out(p, w, o_row0, lse_row0, nq);
+    const bool row_ok = q_row < nq;
+    // split workspace row (the split modes have no row ranges: lse_row0 = bh*Nq)
+    const size_t row_index = static_cast<size_t>(lse_row0) + q_row;
+    T* const orow = reinterpret_cast<T*>(p.o) + o_row0 + static_cast<long long>(q_row) * p.o_rs;
+    const long long lse_index = lse_row0 + q_row;
     // partial-result slot of this group (split mode) in the workspace
     const int ws_slot = dual ? 2 * it.sp + g : it.sp;
     const bool partial = p.n_splits > 1 || dual;
@@ -799,10 +879,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // except the empty half of a dual split, whose slot the combine reads.
       if (dual && row_ok) p.ws_lse[static_cast<size_t>(ws_slot) * p.B * p.heads * p.Nq + row_index] = -INFINITY;
       if (!partial && row_ok) {
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.o) + row_index * D);
+        uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
         for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0u, 0u, 0u, 0u);
-        if (p.lse != nullptr) p.lse[row_index] = -INFINITY;
+        if (p.lse != nullptr) p.lse[lse_index] = -INFINITY;
       }
     } else {
       if (ok)
@@ -814,7 +894,6 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         const float m_use = (m == -INFINITY) ? 0.f : m;
         const float lse_row = (l > 0.f) ? (m_use + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
         if (!partial) {
-          T* orow = reinterpret_cast<T*>(p.o) + row_index * D;
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
@@ -832,7 +911,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
                 dst[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
             }
           }
-          if (row_ok && p.lse != nullptr) p.lse[row_index] = lse_row;
+          if (row_ok && p.lse != nullptr) p.lse[lse_index] = lse_row;
         } else {
           // partial result of this key split, normalised by its own row sum
           const size_t ws_row = static_cast<size_t>(ws_slot) * p.B * p.heads * p.Nq + row_index;

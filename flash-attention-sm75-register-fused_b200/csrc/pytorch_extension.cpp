@@ -206,6 +206,108 @@ std::tuple<torch::Tensor, torch::Tensor> flash_attention_forward_kvcache(
   return {O, lse};
 }
 
+void check_rows(const torch::Tensor& t, const char* name, int64_t n, const torch::Tensor& like) {
+  TORCH_CHECK(t.is_cuda() && t.device() == like.device(), std::string(name) +
+                                                              " must be on the inputs' device");
+  TORCH_CHECK(t.dtype() == torch::kInt32 && t.dim() == 1 && t.is_contiguous() && t.size(0) == n,
+              std::string(name) + " must be a contiguous int32 tensor of ", n, " entries");
+}
+
+void check_packed(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
+  TORCH_CHECK(t.dtype() == torch::kFloat16 || t.dtype() == torch::kBFloat16,
+              std::string(name) + " must be FP16 or BF16");
+  TORCH_CHECK(t.is_contiguous(), std::string(name) + " must be contiguous");
+  TORCH_CHECK(t.dim() == 3, std::string(name) + " must be [total, H, D]");
+}
+
+// Packed variable-length batch: Q [total_q, Hq, d], K/V [total_k, Hkv, d],
+// cu_seqlens_* int32 [B + 1] on the device.  Returns O [total_q, Hq, d] and
+// LSE fp32 [Hq, total_q].
+std::tuple<torch::Tensor, torch::Tensor> flash_attention_forward_varlen(
+    torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor cu_seqlens_q,
+    torch::Tensor cu_seqlens_k, int64_t max_seqlen_q, int64_t max_seqlen_k, int64_t causal,
+    float scale) {
+  check_packed(Q, "Q");
+  check_packed(K, "K");
+  check_packed(V, "V");
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype(), "Q, K, V must share a dtype");
+  TORCH_CHECK(Q.device() == K.device() && Q.device() == V.device(),
+              "Q, K, V must be on the same device");
+  TORCH_CHECK(K.sizes() == V.sizes(), "K and V must have identical shapes");
+  TORCH_CHECK(Q.size(2) == K.size(2), "head_dim mismatch");
+  const auto head_dim = Q.size(2);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  TORCH_CHECK(causal >= FA_CAUSAL_NONE && causal <= FA_CAUSAL_TOP_LEFT, "bad causal mode ", causal);
+  TORCH_CHECK(cu_seqlens_q.dim() == 1 && cu_seqlens_q.size(0) >= 1,
+              "cu_seqlens_q must be [B + 1]");
+  const int64_t B = cu_seqlens_q.size(0) - 1;
+  check_rows(cu_seqlens_q, "cu_seqlens_q", B + 1, Q);
+  check_rows(cu_seqlens_k, "cu_seqlens_k", B + 1, Q);
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && K.size(0) <= INT32_MAX && max_seqlen_q >= 0 &&
+                  max_seqlen_q <= INT32_MAX && max_seqlen_k >= 0 && max_seqlen_k <= INT32_MAX,
+              "size exceeds int32");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::zeros_like(Q);
+  auto lse = torch::full({Q.size(1), Q.size(0)}, -INFINITY, Q.options().dtype(torch::kFloat32));
+  const int rc = fa_fwd_varlen(
+      Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse.data_ptr<float>(),
+      cu_seqlens_q.data_ptr<int>(), cu_seqlens_k.data_ptr<int>(), static_cast<int>(B),
+      static_cast<int>(Q.size(1)), static_cast<int>(K.size(1)), static_cast<int>(Q.size(0)),
+      static_cast<int>(K.size(0)), static_cast<int>(max_seqlen_q), static_cast<int>(max_seqlen_k),
+      static_cast<int>(head_dim), scale, static_cast<int>(causal),
+      Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16, stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_forward_varlen: ", fa_error_string(rc));
+  return {O, lse};
+}
+
+// Padded batch: Q [B, Hq, Nq, d], K/V [B, Hkv, Nk, d] and per batch entry the
+// valid query rows [q_start, q_end) and key rows [k_start, k_end) (int32 [B]
+// on the device).  Rows outside a query range come back as O = 0, LSE = -inf.
+std::tuple<torch::Tensor, torch::Tensor> flash_attention_forward_padded(
+    torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor q_start, torch::Tensor q_end,
+    torch::Tensor k_start, torch::Tensor k_end, int64_t causal, float scale) {
+  check_tensor(Q, "Q", true);
+  check_tensor(K, "K", true);
+  check_tensor(V, "V", true);
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype(), "Q, K, V must share a dtype");
+  TORCH_CHECK(Q.device() == K.device() && Q.device() == V.device(),
+              "Q, K, V must be on the same device");
+  TORCH_CHECK(Q.size(0) == K.size(0), "batch mismatch");
+  TORCH_CHECK(Q.size(3) == K.size(3), "head_dim mismatch");
+  TORCH_CHECK(K.sizes() == V.sizes(), "K and V must have identical shapes");
+  const auto head_dim = Q.size(3);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  TORCH_CHECK(causal >= FA_CAUSAL_NONE && causal <= FA_CAUSAL_TOP_LEFT, "bad causal mode ", causal);
+  const int64_t B = Q.size(0);
+  check_rows(q_start, "q_start", B, Q);
+  check_rows(q_end, "q_end", B, Q);
+  check_rows(k_start, "k_start", B, Q);
+  check_rows(k_end, "k_end", B, Q);
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && Q.size(1) <= INT32_MAX && Q.size(2) <= INT32_MAX &&
+                  K.size(2) <= INT32_MAX,
+              "size exceeds int32");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::zeros_like(Q);
+  auto lse = torch::full({Q.size(0), Q.size(1), Q.size(2)}, -INFINITY,
+                         Q.options().dtype(torch::kFloat32));
+  const int rc = fa_fwd_padded(
+      Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse.data_ptr<float>(),
+      q_start.data_ptr<int>(), q_end.data_ptr<int>(), k_start.data_ptr<int>(),
+      k_end.data_ptr<int>(), static_cast<int>(B), static_cast<int>(Q.size(1)),
+      static_cast<int>(K.size(1)), static_cast<int>(Q.size(2)), static_cast<int>(K.size(2)),
+      static_cast<int>(head_dim), scale, static_cast<int>(causal),
+      Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16, stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_forward_padded: ", fa_error_string(rc));
+  return {O, lse};
+}
+
 // Gradients of flash_attention_forward_lse: (dQ, dK, dV) from dO, the inputs,
 // the forward's O and LSE.  The workspace comes from PyTorch's allocator.
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> flash_attention_backward(
@@ -270,6 +372,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "(dQ, dK, dV) from dO, Q, K, V, O, LSE (fp32 [B, Hq, N]), causal, scale");
   m.def("flash_attention_forward_kvcache", &flash_attention_forward_kvcache,
         "O, LSE of Nq queries against Nk cached keys; causal: 0 none, 1 bottom-right, 2 top-left");
+  m.def("flash_attention_forward_varlen", &flash_attention_forward_varlen,
+        "(O [total_q, Hq, d], LSE [Hq, total_q]) of a packed variable-length batch");
+  m.def("flash_attention_forward_padded", &flash_attention_forward_padded,
+        "(O, LSE) of a padded batch with per-entry valid query / key row ranges");
   m.def("device_status", &device_status, pybind11::arg("reset") = false,
         "Error code recorded by the in-kernel watchdog (0 = none)");
   m.def("set_watchdog_ns", &fa_set_watchdog_ns);

@@ -22,6 +22,10 @@ SIGNATURES = {
     "fa_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                        c_int, c_int, c_float, c_int, c_int, c_vp, ctypes.c_size_t, c_vp]),
     "fa_bwd_workspace_bytes": (ctypes.c_size_t, [c_int, c_int, c_int]),
+    "fa_fwd_varlen": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
+                              c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_vp]),
+    "fa_fwd_padded": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
+                              c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_vp]),
     "launch_flash_attention_forward": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
                                               c_float, c_bool]),
     "launch_flash_attention_forward_scalar": (None, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
@@ -127,3 +131,37 @@ def fa_bwd(q, k, v, o, do, lse, dq, dk, dv, causal=False, scale=None, stream=Non
     return lib.fa_bwd(ptr(q), ptr(k), ptr(v), ptr(o), ptr(do), ptr(lse), ptr(dq), ptr(dk), ptr(dv),
                       B, Hq, Hkv, N, d, float(scale), int(bool(causal)), dtype, ptr(ws), nbytes,
                       stream_ptr(stream))
+
+
+def fa_fwd_varlen(q, k, v, o, lse, cu_q, cu_k, max_q, max_k, causal=CAUSAL_NONE, scale=None,
+                  stream=None):
+    """Call fa_fwd_varlen on packed torch CUDA tensors (Q/O [total_q, Hq, d],
+    K/V [total_k, Hkv, d], LSE [Hq, total_q] or None, cu_* int32 [B + 1] on the
+    device).  Returns the status."""
+    import math
+    import torch
+    Tq, Hq, d = q.shape
+    Tk, Hkv = k.shape[0], k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    return load().fa_fwd_varlen(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), ptr(cu_q), ptr(cu_k),
+                                cu_q.numel() - 1, Hq, Hkv, Tq, Tk, int(max_q), int(max_k), d,
+                                float(scale), int(causal), dtype, stream_ptr(stream))
+
+
+def fa_fwd_padded(q, k, v, o, lse, q_start, q_end, k_start, k_end, causal=CAUSAL_NONE,
+                  scale=None, stream=None):
+    """Call fa_fwd_padded on torch CUDA tensors (Q/O [B, Hq, Nq, d], K/V
+    [B, Hkv, Nk, d], LSE [B, Hq, Nq] or None, row ranges int32 [B] on the
+    device).  Returns the status."""
+    import math
+    import torch
+    B, Hq, Nq, d = q.shape
+    Hkv, Nk = k.shape[1], k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    return load().fa_fwd_padded(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), ptr(q_start),
+                                ptr(q_end), ptr(k_start), ptr(k_end), B, Hq, Hkv, Nq, Nk, d,
+                                float(scale), int(causal), dtype, stream_ptr(stream))

@@ -154,6 +154,92 @@ def flash_attention_forward_kvcache(Q, K, V, causal=False, scale=None, return_ls
     return (out, lse) if return_lse else out
 
 
+def _rows_tensor(x, n, device, name):
+    """int32 device tensor of n row offsets from a tensor or a sequence of ints."""
+    t = torch.as_tensor(x, dtype=torch.int32, device=device).contiguous()
+    if t.dim() != 1 or t.numel() != n:
+        raise ValueError(f"{name} must hold {n} row offsets, got shape {tuple(t.shape)}")
+    return t
+
+
+def flash_attention_varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                   max_seqlen_k, causal=False, scale=None, return_lse=False,
+                                   causal_alignment="bottom_right"):
+    """Attention over a packed batch of variable-length sequences; forward only.
+
+    Args:
+        q: [total_q, H_q, D]  float16 / bfloat16, cuda (sequences one after another)
+        k, v: [total_k, H_kv, D]  same dtype, H_kv divides H_q
+        cu_seqlens_q, cu_seqlens_k: B + 1 row offsets (int32 tensor or ints);
+            sequence b owns rows [cu[b], cu[b+1])
+        max_seqlen_q, max_seqlen_k: upper bounds of the sequence lengths
+        causal: bool; causal_alignment "bottom_right" (query i of a sequence
+            sees keys j <= i + n_k - n_q) or "top_left" (j <= i)
+        scale: float (default 1/sqrt(D))
+        return_lse: also return LSE [H_q, total_q] fp32 (natural log)
+
+    Rows that see no key (and rows outside every sequence) return O = 0,
+    LSE = -inf.
+    """
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("q, k, v must be 3D [total, H, D]")
+    head_dim = q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    if causal and causal_alignment not in _CAUSAL_MODES:
+        raise ValueError(f"causal_alignment must be one of {sorted(_CAUSAL_MODES)}")
+    _check_gqa(q.size(1), k.size(1))
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    cu_q = torch.as_tensor(cu_seqlens_q, dtype=torch.int32, device=q.device).contiguous()
+    cu_k = _rows_tensor(cu_seqlens_k, cu_q.numel(), q.device, "cu_seqlens_k")
+    mode = _CAUSAL_MODES[causal_alignment] if causal else 0
+    out, lse = _C.flash_attention_forward_varlen(q.contiguous(), k.contiguous(), v.contiguous(),
+                                                 cu_q, cu_k, int(max_seqlen_q),
+                                                 int(max_seqlen_k), mode, float(scale))
+    return (out, lse) if return_lse else out
+
+
+def flash_attention_forward_padded(Q, K, V, q_start, q_end, k_start, k_end, causal=False,
+                                   scale=None, return_lse=False, causal_alignment="bottom_right"):
+    """Attention of a padded batch without repacking; forward only.
+
+    Args:
+        Q: [B, H_q, N_q, D], K/V: [B, H_kv, N_k, D] (as ``flash_attention_forward_kvcache``)
+        q_start, q_end: per batch entry, valid query rows [q_start[b], q_end[b])
+        k_start, k_end: per batch entry, valid key rows [k_start[b], k_end[b])
+            (int32 tensors or sequences of B ints; left padding: start > 0,
+            right padding: end < N)
+        causal, causal_alignment: the causal rule of the full padded rows
+            ("bottom_right": key j visible to query i iff j <= i + N_k - N_q;
+            "top_left": j <= i), restricted to the valid keys
+
+    Padding keys are never attended.  Rows outside a query range, and rows
+    that see no key, return O = 0, LSE = -inf.
+    """
+    if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
+        raise ValueError("Q, K, V must be 4D [B, H, N, D]")
+    head_dim = Q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    if causal and causal_alignment not in _CAUSAL_MODES:
+        raise ValueError(f"causal_alignment must be one of {sorted(_CAUSAL_MODES)}")
+    _check_gqa(Q.size(1), K.size(1))
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    B = Q.size(0)
+    ranges = [_rows_tensor(x, B, Q.device, name) for x, name in
+              ((q_start, "q_start"), (q_end, "q_end"), (k_start, "k_start"), (k_end, "k_end"))]
+    mode = _CAUSAL_MODES[causal_alignment] if causal else 0
+    out, lse = _C.flash_attention_forward_padded(Q.contiguous(), K.contiguous(), V.contiguous(),
+                                                 *ranges, mode, float(scale))
+    return (out, lse) if return_lse else out
+
+
 _pipeline = {}
 
 

@@ -92,6 +92,50 @@ int fa_fwd_kvcache(const void* Q, const void* K, const void* V, void* O, float* 
 size_t fa_fwd_kvcache_workspace_bytes(int B, int Hq, int Hkv, int Nq, int Nk, int head_dim);
 
 /*
+ * fa_fwd_varlen — attention over a packed batch of variable-length sequences
+ * (the cu_seqlens layout): Q/O [total_q, Hq, d], K/V [total_k, Hkv, d], all
+ * contiguous.  Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1])
+ * and key rows [cu_seqlens_k[b], cu_seqlens_k[b+1]); the offsets are int32
+ * DEVICE arrays of B + 1 non-decreasing entries (clamped to [0, total]).
+ * max_seqlen_q / max_seqlen_k bound the lengths (query rows of a longer
+ * sequence past max_seqlen_q, rounded up to 256, are not computed).
+ * `causal`: FA_CAUSAL_BOTTOM_RIGHT (key j visible to query i of a sequence iff
+ * j <= i + nk - nq), FA_CAUSAL_TOP_LEFT (j <= i) or FA_CAUSAL_NONE.  LSE (may be
+ * NULL) is fp32 [Hq, total_q].  Rows that see no key get O = 0, LSE = -inf.
+ * Keys past a sequence's end are masked; the V rows that follow it in the
+ * packed buffer (the next sequence's) are multiplied by exactly 0, so they
+ * must be finite.  Asynchronous on `stream`.
+ *
+ * No reference counterpart: the reference's HF patch sends masked (padded /
+ * varlen) batches to PyTorch SDPA (reference
+ * src/flash_attention_sm75/llama_attention_replacement.py:61-62, reason
+ * "has_attn_mask").
+ */
+int fa_fwd_varlen(const void* Q, const void* K, const void* V, void* O, float* lse,
+                  const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int Hq, int Hkv,
+                  int total_q, int total_k, int max_seqlen_q, int max_seqlen_k, int head_dim,
+                  float scale, int causal, int dtype, void* stream);
+
+/*
+ * fa_fwd_padded — attention of a padded batch in the fixed layout (Q/O
+ * [B, Hq, Nq, d], K/V [B, Hkv, Nk, d], LSE [B, Hq, Nq]): batch entry b's valid
+ * queries are rows [q_start[b], q_end[b]) and its valid keys rows
+ * [k_start[b], k_end[b]) (int32 DEVICE arrays of B entries, clamped to
+ * [0, Nq] / [0, Nk]).  Padding keys are never attended; rows of O and LSE
+ * outside a query range are not written.  `causal` follows fa_fwd_kvcache on
+ * the full padded rows (BOTTOM_RIGHT: key j visible to query i iff
+ * j <= i + Nk - Nq; TOP_LEFT: j <= i), restricted to the valid keys; valid
+ * rows that then see no key get O = 0, LSE = -inf.  Covers left padding
+ * (start > 0), right padding (end < N) and both.  Asynchronous on `stream`.
+ *
+ * No reference counterpart (reference llama_attention_replacement.py:61-62).
+ */
+int fa_fwd_padded(const void* Q, const void* K, const void* V, void* O, float* lse,
+                  const int* q_start, const int* q_end, const int* k_start, const int* k_end,
+                  int B, int Hq, int Hkv, int Nq, int Nk, int head_dim, float scale, int causal,
+                  int dtype, void* stream);
+
+/*
  * fa_bwd — gradients of fa_fwd (square, causal 0/1 top-left, GQA): from Q, K, V,
  * the forward's O and LSE ([B, Hq, N] fp32, natural log) and dO = dL/dO, writes
  * dQ [B, Hq, N, d], dK and dV [B, Hkv, N, d] (GQA: summed over each group's

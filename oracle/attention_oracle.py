@@ -118,6 +118,61 @@ def kvcache_offset(Nq: int, Nk: int, mode: int) -> int:
     return Nk - Nq if mode == 1 else 0
 
 
+def attention_varlen_fp32(q, k, v, cu_q, cu_k, causal_mode: int = 0, scale=None):
+    """fp32 attention of a packed variable-length batch, one sequence at a time.
+
+    q [total_q, Hq, d], k/v [total_k, Hkv, d]; sequence b owns query rows
+    [cu_q[b], cu_q[b+1]) and key rows [cu_k[b], cu_k[b+1]).  causal_mode:
+    0 none, 1 bottom-right (j <= i + nk - nq), 2 top-left (j <= i), per
+    sequence.  Returns (O fp32 [total_q, Hq, d], LSE fp32 [Hq, total_q]); rows
+    outside every sequence stay O = 0, LSE = -inf.
+    """
+    Tq, Hq, d = q.shape
+    O = torch.zeros((Tq, Hq, d))
+    lse = torch.full((Hq, Tq), float("-inf"))
+    cu_q = [int(x) for x in cu_q]
+    cu_k = [int(x) for x in cu_k]
+    for b in range(len(cu_q) - 1):
+        q0, q1, k0, k1 = cu_q[b], cu_q[b + 1], cu_k[b], cu_k[b + 1]
+        if q1 <= q0:
+            continue
+        Qs = q[q0:q1].permute(1, 0, 2)[None]
+        Ks = k[k0:k1].permute(1, 0, 2)[None]
+        Vs = v[k0:k1].permute(1, 0, 2)[None]
+        o, l = attention_fp32(Qs, Ks, Vs, causal=causal_mode != 0, scale=scale,
+                              causal_offset=kvcache_offset(q1 - q0, k1 - k0, causal_mode))
+        O[q0:q1] = o[0].permute(1, 0, 2)
+        lse[:, q0:q1] = l[0]
+    return O, lse
+
+
+def attention_padded_fp32(Q, K, V, q_start, q_end, k_start, k_end, causal_mode: int = 0,
+                          scale=None):
+    """fp32 attention of a padded batch: batch entry b attends from query rows
+    [q_start[b], q_end[b]) to key rows [k_start[b], k_end[b]) of Q [B, Hq, Nq, d]
+    and K/V [B, Hkv, Nk, d], with the causal rule of the full padded rows
+    (1 bottom-right: j <= i + Nk - Nq; 2 top-left: j <= i).  Rows outside a
+    query range stay O = 0, LSE = -inf.  Returns (O fp32 [B, Hq, Nq, d], LSE
+    fp32 [B, Hq, Nq]).
+    """
+    B, Hq, Nq, d = Q.shape
+    Nk = K.size(2)
+    O = torch.zeros((B, Hq, Nq, d))
+    lse = torch.full((B, Hq, Nq), float("-inf"))
+    base = kvcache_offset(Nq, Nk, causal_mode)
+    for b in range(B):
+        q0, q1 = int(q_start[b]), int(q_end[b])
+        k0, k1 = int(k_start[b]), int(k_end[b])
+        if q1 <= q0:
+            continue
+        o, l = attention_fp32(Q[b:b + 1, :, q0:q1], K[b:b + 1, :, k0:k1], V[b:b + 1, :, k0:k1],
+                              causal=causal_mode != 0, scale=scale,
+                              causal_offset=base + q0 - k0)
+        O[b, :, q0:q1] = o[0]
+        lse[b, :, q0:q1] = l[0]
+    return O, lse
+
+
 # ------------------------------------------------------------------ inputs
 @dataclass(frozen=True)
 class AttnConfig:

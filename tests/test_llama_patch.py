@@ -58,3 +58,34 @@ def test_reason_order_matches_reference():
     assert r(Fake(), Fake(), 0.0, None) is None
     assert r(Fake(dtype=torch.bfloat16), Fake(dtype=torch.bfloat16), 0.0, None) is None
     assert r(Fake(shape=(1, 8, 8, 128)), Fake(shape=(1, 2, 8, 128)), 0.0, None) is None
+
+
+def test_padded_mask_structure_cpu():
+    """The mask analysis that routes masked calls to the padded kernel (CPU
+    tensors; the routing itself needs CUDA tensors)."""
+    from tests.test_varlen_cpu import padded_mask
+    B, N = 3, 40
+    qr = [(0, 40), (7, 40), (0, 25)]
+    kr = [(0, 40), (7, 40), (0, 25)]
+    for mode in (0, 1, 2):
+        m = padded_mask(B, N, N, qr, kr, mode)
+        got = patch.padded_structure(m, B, N, N)
+        assert got is not None
+        want_mode = 0 if mode == 0 else 2  # square: top-left and bottom-right coincide
+        assert got[0] == want_mode
+        assert got[1].tolist() == [0, 7, 0] and got[2].tolist() == [40, 40, 25]
+        assert got[3].tolist() == [0, 7, 0] and got[4].tolist() == [40, 40, 25]
+        # the additive form of the same mask
+        add = torch.zeros(m.shape).masked_fill(~m, torch.finfo(torch.float32).min)
+        assert patch.padded_structure(add, B, N, N)[0] == want_mode
+    # decode over a left-padded cache: one query row, keys [pad, Nk)
+    m = padded_mask(2, 1, 50, [(0, 1), (0, 1)], [(10, 50), (0, 50)], 1)
+    got = patch.padded_structure(m, 2, 1, 50)
+    assert got is not None and got[3].tolist() == [10, 0] and got[4].tolist() == [50, 50]
+    # holes, biases and per-head masks are not padded batches
+    m = padded_mask(B, N, N, qr, kr, 1)
+    m[1, 0, 20, 10] = False
+    assert patch.padded_structure(m, B, N, N) is None
+    bias = torch.randn(1, 1, N, N)
+    assert patch.padded_structure(bias, 1, N, N) is None
+    assert patch.padded_structure(torch.ones(1, 2, N, N, dtype=torch.bool), 1, N, N) is None
