@@ -45,9 +45,11 @@ struct BwdLayout {
   static constexpr int kBarFix = 0;
   static constexpr int kBarFull = 1;
   static constexpr int kBarEmpty = kBarFull + kSlots;
-  static constexpr int kBarS = kBarEmpty + kSlots;   // S and dP (or S^T, dP^T) computed
-  static constexpr int kBarP = kBarS + 1;            // P / dS written (128 arrivals)
-  static constexpr int kBarG = kBarP + 1;            // all gradient MMAs completed
+  // S and dP (or S^T, dP^T) computed: one barrier per half of the step's 128
+  // queries in the dK/dV kernel (kBarS + h), one (kBarS) in the dQ kernel
+  static constexpr int kBarS = kBarEmpty + kSlots;
+  static constexpr int kBarP = kBarS + 2;            // P / dS written (128 arrivals), per half
+  static constexpr int kBarG = kBarP + 2;            // all gradient MMAs completed
   static constexpr int kNumBars = kBarG + 1;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kBytes = kOffMisc + 16;
@@ -117,7 +119,7 @@ __device__ __forceinline__ bool bwd_setup(uint8_t* smem_raw, uint8_t*& smem, uin
     const unsigned long long st = *reinterpret_cast<volatile unsigned long long*>(&g_fa_status);
     *abort_flag = ((st >> 32) == epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
     for (int i = 0; i < L::kNumBars; ++i)
-      ptx::mbar_init(sbase + L::kOffBar + 8u * i, i == L::kBarP ? 128u : 1u);
+      ptx::mbar_init(sbase + L::kOffBar + 8u * i, (i == L::kBarP || i == L::kBarP + 1) ? 128u : 1u);
     ptx::fence_barrier_init();
   }
   __syncthreads();
@@ -228,115 +230,155 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       bar_wait(bar(L::kBarFix), 0, wc, 42, false);
     }
   } else if (warp == kBwdWarpMma) {
+    // Each step's 128 queries are processed as two halves h of 64.  Issue
+    // order: S(0,h0) dP(0,h0) S(0,h1) dP(0,h1), then per step s and half h
+    //   [P(s,h) ready]  dV += P^T(s,h) dO(s,h)  dK += dS^T(s,h) Q(s,h)
+    //                   S(s+1,h)  dP(s+1,h)
+    // so the elementwise phase of one half runs while the tensor pipe works on
+    // the other.  S(s+1,h) overwrites the TMEM columns holding P^T(s,h) and
+    // dP(s+1,h) those holding dS^T(s,h); tcgen05.mma ops of one thread execute
+    // in issue order, so the gradient products have read them first.
     constexpr uint32_t fmt = BF16 ? 1u : 0u;
-    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 128, fmt, 0, 0);
+    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 64, fmt, 0, 0);
     constexpr uint32_t idesc_g = ptx::make_idesc_f16(128, D, fmt, 0, 1);
     auto slot_of = [](int i) { return i % L::kSlots; };
     auto phase_of = [](int i) { return static_cast<uint32_t>((i / L::kSlots) & 1); };
     auto wait = [&](uint32_t bb, uint32_t ph, int site) {
       return __all_sync(0xffffffffu, bar_wait(bb, ph, wc, site));
     };
-    auto commit = [&](uint32_t bb) {
-      if (ptx::elect_one()) ptx::mma_commit(bb);
-      __syncwarp();
-    };
     const uint64_t k_desc = ptx::smem_desc_sw128(sbase + L::kOffFix, 16, 1024);
     const uint64_t v_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);              // K-major
     const uint64_t ring_mn = ptx::smem_desc_sw128(sbase + L::kOffRing, L::kBlockBytes, 1024);  // MN-major
+    // S^T(s,h) = K Q^T and dP^T(s,h) = V dO^T for queries [64h, 64h+64) of
+    // step s (B = 64 rows of the Q / dO tile: 8 KB into each 64-column block)
+    auto issue_scores = [&](int s, int h) {
+      const uint64_t q_off = static_cast<uint64_t>((slot_of(2 * s) * L::kTile + h * 8192) >> 4);
+      const uint64_t d_off = static_cast<uint64_t>((slot_of(2 * s + 1) * L::kTile + h * 8192) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
+          ptx::mma_ss(tmem + L::tS + 64 * h, k_desc + off, ring_k + q_off + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
+          ptx::mma_ss(tmem + L::tDP + 64 * h, v_desc + off, ring_k + d_off + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(bar(L::kBarS + h));
+      }
+      __syncwarp();
+    };
+    // dV += P^T dO and dK += dS^T Q over queries [64h, 64h+64) of step s
+    // (A from TMEM: P^T / dS^T packed in the half's first 32 columns; B
+    // MN-major, K = queries, 16 rows = 2 KB per K step)
+    auto issue_grads = [&](int s, int h) {
+      const uint64_t q_off = static_cast<uint64_t>((slot_of(2 * s) * L::kTile) >> 4);
+      const uint64_t d_off = static_cast<uint64_t>((slot_of(2 * s + 1) * L::kTile) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t off = static_cast<uint64_t>(((4 * h + k) * 2048) >> 4);
+          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tS + 64 * h + 8 * k, ring_mn + d_off + off, idesc_g,
+                      (s > 0 || h > 0 || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t off = static_cast<uint64_t>(((4 * h + k) * 2048) >> 4);
+          ptx::mma_ts(tmem + L::tAcc1, tmem + L::tDP + 64 * h + 8 * k, ring_mn + q_off + off, idesc_g,
+                      (s > 0 || h > 0 || k > 0) ? 1u : 0u);
+        }
+        if (h == 1) {  // the step's Q and dO tiles are read for the last time
+          ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * s)));
+          ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * s + 1)));
+        }
+      }
+      __syncwarp();
+    };
     bool ok = wait(bar(L::kBarFix), 0, 43);
-    for (int s = 0; ok && s < n_steps; ++s) {
-      const int iq = 2 * s, id = 2 * s + 1;
-      if (!(ok = wait(bar(L::kBarFull + slot_of(iq)), phase_of(iq), 44))) break;
-      if (!(ok = wait(bar(L::kBarFull + slot_of(id)), phase_of(id), 44))) break;
-      const uint64_t q_off = static_cast<uint64_t>((slot_of(iq) * L::kTile) >> 4);
-      const uint64_t d_off = static_cast<uint64_t>((slot_of(id) * L::kTile) >> 4);
-      ptx::tc_fence_after();
-      // S^T = K Q^T and dP^T = V dO^T (both operands K-major, K = d)
-      if (ptx::elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tS, k_desc + off, ring_k + q_off + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tDP, v_desc + off, ring_k + d_off + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(L::kBarS));
+    if (ok && n_steps > 0) {
+      ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 44) &&
+           wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 44);
+      if (ok) {
+        ptx::tc_fence_after();
+        issue_scores(0, 0);
+        issue_scores(0, 1);
       }
-      __syncwarp();
-      if (!(ok = wait(bar(L::kBarP), s & 1, 45))) break;
-      ptx::tc_fence_after();
-      // dV += P^T dO and dK += dS^T Q (A from TMEM, B MN-major: K = queries)
-      if (ptx::elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>((kk * 2048) >> 4);
-          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tS + kk * 8, ring_mn + d_off + off, idesc_g,
-                      (s > 0 || kk > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>((kk * 2048) >> 4);
-          ptx::mma_ts(tmem + L::tAcc1, tmem + L::tDP + kk * 8, ring_mn + q_off + off, idesc_g,
-                      (s > 0 || kk > 0) ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(L::kBarEmpty + slot_of(iq)));
-        ptx::mma_commit(bar(L::kBarEmpty + slot_of(id)));
-      }
-      __syncwarp();
     }
-    commit(bar(L::kBarG));
+    for (int s = 0; ok && s < n_steps; ++s) {
+      const bool next = s + 1 < n_steps;
+      if (next) {
+        const int iq = 2 * s + 2, id = 2 * s + 3;
+        if (!(ok = wait(bar(L::kBarFull + slot_of(iq)), phase_of(iq), 44))) break;
+        if (!(ok = wait(bar(L::kBarFull + slot_of(id)), phase_of(id), 44))) break;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!(ok = wait(bar(L::kBarP + h), s & 1, 45))) break;
+        ptx::tc_fence_after();
+        issue_grads(s, h);
+        if (next) issue_scores(s + 1, h);
+      }
+    }
+    if (ptx::elect_one()) ptx::mma_commit(bar(L::kBarG));
+    __syncwarp();
     bar_wait(bar(L::kBarG), 0, wc, 46, false);
     __syncwarp();
   } else if (warp < 4) {
-    // rows = keys of tile t; columns = the step's 128 queries
+    // rows = keys of tile t; columns = the step's 128 queries, in two halves
     const int r = warp * 32 + lane;
     const int key = t * 128 + r;
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float sl = p.scale_log2;
     bool ok = true;
     for (int s = 0; ok && s < n_steps; ++s) {
-      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), s & 1, wc, 47));
-      if (!ok) break;
-      ptx::tc_fence_after();
       const int qt = step_tile(s);
-      const float* l2v = reinterpret_cast<const float*>(smem + L::kOffVec + ((2 * s) % L::kSlots) * L::kVec);
-      const float* ddv = reinterpret_cast<const float*>(smem + L::kOffVec + ((2 * s + 1) % L::kSlots) * L::kVec);
+      const float4* l2v = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s) % L::kSlots) * L::kVec);
+      const float4* ddv = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s + 1) % L::kSlots) * L::kVec);
       const bool diag = p.causal && qt == t;  // query < key is masked
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + h), s & 1, wc, 47));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        uint32_t pk[32], gk[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        ptx::tmem_ld32(tmem + lane_off + L::tS + 32 * c, sv);
-        ptx::tmem_ld32(tmem + lane_off + L::tDP + 32 * c, dv);
-        ptx::tmem_wait_ld();
-        pin_after_wait<32>(sv);
-        pin_after_wait<32>(dv);
-        uint32_t pk[16], gk[16];
+        for (int c = 0; c < 2; ++c) {
+          uint32_t sv[32], dv[32];
+          ptx::tmem_ld32(tmem + lane_off + L::tS + 64 * h + 32 * c, sv);
+          ptx::tmem_ld32(tmem + lane_off + L::tDP + 64 * h + 32 * c, dv);
+          ptx::tmem_wait_ld();
+          pin_after_wait<32>(sv);
+          pin_after_wait<32>(dv);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int q0 = 32 * c + i;  // query within the tile
-          float pe[2], ge[2];
+          for (int i = 0; i < 32; i += 4) {
+            const int q0 = 64 * h + 32 * c + i;  // query within the tile
+            const float4 lv = l2v[q0 / 4];
+            const float4 dd = ddv[q0 / 4];
+            const float lq[4] = {lv.x, lv.y, lv.z, lv.w};
+            const float dq[4] = {dd.x, dd.y, dd.z, dd.w};
+            float pe[4], ge[4];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float lv = l2v[q0 + e];
-            float pv = ptx::ex2_approx(fmaf(__uint_as_float(sv[i + e]), sl, -lv));
-            if (diag && q0 + e < r) pv = 0.f;
-            pe[e] = pv;
-            ge[e] = pv * (__uint_as_float(dv[i + e]) - ddv[q0 + e]);
+            for (int e = 0; e < 4; ++e) {
+              float pv = ptx::ex2_approx(fmaf(__uint_as_float(sv[i + e]), sl, -lq[e]));
+              if (diag && q0 + e < r) pv = 0.f;
+              pe[e] = pv;
+              ge[e] = pv * (__uint_as_float(dv[i + e]) - dq[e]);
+            }
+            pk[16 * c + i / 2] = pack2<BF16>(pe[0], pe[1]);
+            pk[16 * c + i / 2 + 1] = pack2<BF16>(pe[2], pe[3]);
+            gk[16 * c + i / 2] = pack2<BF16>(ge[0], ge[1]);
+            gk[16 * c + i / 2 + 1] = pack2<BF16>(ge[2], ge[3]);
           }
-          pk[i / 2] = pack2<BF16>(pe[0], pe[1]);
-          gk[i / 2] = pack2<BF16>(ge[0], ge[1]);
         }
-        // P^T into S columns 16c.., dS^T into dP columns 16c.. (both already read)
-        ptx::tmem_st16(tmem + lane_off + L::tS + 16 * c, pk);
-        ptx::tmem_st16(tmem + lane_off + L::tDP + 16 * c, gk);
+        // P^T into S columns 64h.., dS^T into dP columns 64h.. (both already read)
+        ptx::tmem_st32(tmem + lane_off + L::tS + 64 * h, pk);
+        ptx::tmem_st32(tmem + lane_off + L::tDP + 64 * h, gk);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(L::kBarP + h));
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(L::kBarP));
     }
     if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarG), 0, wc, 48));
     if (ok) {
@@ -404,61 +446,85 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       bar_wait(bar(L::kBarFix), 0, wc, 52, false);
     }
   } else if (warp == kBwdWarpMma) {
+    // Keys of each K/V tile in two halves h of 64, issued as
+    //   S(0,h0) dP(0,h0) S(0,h1) dP(0,h1), then per tile j and half h:
+    //   [dS(j,h) ready]  dQ += dS(j,h) K(j,h)  S(j+1,h)  dP(j+1,h)
+    // (the elementwise phase of one half overlaps the other half's products;
+    // S(j+1,h) overwrites the columns of dS(j,h) after dQ has read them, in
+    // issue order).
     constexpr uint32_t fmt = BF16 ? 1u : 0u;
-    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 128, fmt, 0, 0);
+    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 64, fmt, 0, 0);
     constexpr uint32_t idesc_g = ptx::make_idesc_f16(128, D, fmt, 0, 1);
     auto slot_of = [](int i) { return i % L::kSlots; };
     auto phase_of = [](int i) { return static_cast<uint32_t>((i / L::kSlots) & 1); };
     auto wait = [&](uint32_t bb, uint32_t ph, int site) {
       return __all_sync(0xffffffffu, bar_wait(bb, ph, wc, site));
     };
-    auto commit = [&](uint32_t bb) {
-      if (ptx::elect_one()) ptx::mma_commit(bb);
-      __syncwarp();
-    };
     const uint64_t q_desc = ptx::smem_desc_sw128(sbase + L::kOffFix, 16, 1024);
     const uint64_t do_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);
     const uint64_t ring_mn = ptx::smem_desc_sw128(sbase + L::kOffRing, L::kBlockBytes, 1024);
+    // S(j,h) = Q K^T, dP(j,h) = dO V^T over keys [64h, 64h+64) of tile j
+    auto issue_scores = [&](int j, int h) {
+      const uint64_t k_off = static_cast<uint64_t>((slot_of(2 * j) * L::kTile + h * 8192) >> 4);
+      const uint64_t v_off = static_cast<uint64_t>((slot_of(2 * j + 1) * L::kTile + h * 8192) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
+          ptx::mma_ss(tmem + L::tS + 64 * h, q_desc + off, ring_k + k_off + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
+          ptx::mma_ss(tmem + L::tDP + 64 * h, do_desc + off, ring_k + v_off + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(bar(L::kBarS + h));
+        if (h == 1) ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * j + 1)));  // V_j read
+      }
+      __syncwarp();
+    };
+    // dQ += dS(j,h) K(j,h) (A = dS from TMEM, B = K_j MN-major: K = keys)
+    auto issue_grad = [&](int j, int h) {
+      const uint64_t k_off = static_cast<uint64_t>((slot_of(2 * j) * L::kTile) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t off = static_cast<uint64_t>(((4 * h + k) * 2048) >> 4);
+          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tS + 64 * h + 8 * k, ring_mn + k_off + off, idesc_g,
+                      (j > 0 || h > 0 || k > 0) ? 1u : 0u);
+        }
+        if (h == 1) ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * j)));  // K_j read
+      }
+      __syncwarp();
+    };
     bool ok = wait(bar(L::kBarFix), 0, 53);
-    for (int j = 0; ok && j < n_kv; ++j) {
-      const int ik = 2 * j, iv = 2 * j + 1;
-      if (!(ok = wait(bar(L::kBarFull + slot_of(ik)), phase_of(ik), 54))) break;
-      if (!(ok = wait(bar(L::kBarFull + slot_of(iv)), phase_of(iv), 54))) break;
-      const uint64_t k_off = static_cast<uint64_t>((slot_of(ik) * L::kTile) >> 4);
-      const uint64_t v_off = static_cast<uint64_t>((slot_of(iv) * L::kTile) >> 4);
-      ptx::tc_fence_after();
-      // S = Q K^T, dP = dO V^T (K = d, both operands K-major)
-      if (ptx::elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tS, q_desc + off, ring_k + k_off + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tDP, do_desc + off, ring_k + v_off + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(L::kBarS));
-        ptx::mma_commit(bar(L::kBarEmpty + slot_of(iv)));  // V_j read
+    if (ok && n_kv > 0) {
+      ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 54) &&
+           wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 54);
+      if (ok) {
+        ptx::tc_fence_after();
+        issue_scores(0, 0);
+        issue_scores(0, 1);
       }
-      __syncwarp();
-      if (!(ok = wait(bar(L::kBarP), j & 1, 55))) break;
-      ptx::tc_fence_after();
-      // dQ += dS K_j (A = dS from TMEM, B = K_j MN-major: K = keys)
-      if (ptx::elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>((kk * 2048) >> 4);
-          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tS + kk * 8, ring_mn + k_off + off, idesc_g,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(L::kBarEmpty + slot_of(ik)));
-      }
-      __syncwarp();
     }
-    commit(bar(L::kBarG));
+    for (int j = 0; ok && j < n_kv; ++j) {
+      const bool next = j + 1 < n_kv;
+      if (next) {
+        const int ik = 2 * j + 2, iv = 2 * j + 3;
+        if (!(ok = wait(bar(L::kBarFull + slot_of(ik)), phase_of(ik), 54))) break;
+        if (!(ok = wait(bar(L::kBarFull + slot_of(iv)), phase_of(iv), 54))) break;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!(ok = wait(bar(L::kBarP + h), j & 1, 55))) break;
+        ptx::tc_fence_after();
+        issue_grad(j, h);
+        if (next) issue_scores(j + 1, h);
+      }
+    }
+    if (ptx::elect_one()) ptx::mma_commit(bar(L::kBarG));
+    __syncwarp();
     bar_wait(bar(L::kBarG), 0, wc, 56, false);
     __syncwarp();
   } else if (warp < 4) {
@@ -470,37 +536,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     const float dval = p.dd[static_cast<size_t>(bh) * p.n_pad + q_row];
     bool ok = true;
     for (int j = 0; ok && j < n_kv; ++j) {
-      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), j & 1, wc, 57));
-      if (!ok) break;
-      ptx::tc_fence_after();
       // keys >= N and (causal) keys > this query get P = 0
       int lim = p.N - j * 128;
       if (p.causal && j == t) lim = min(lim, r + 1);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + h), j & 1, wc, 57));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        uint32_t gk[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        ptx::tmem_ld32(tmem + lane_off + L::tS + 32 * c, sv);
-        ptx::tmem_ld32(tmem + lane_off + L::tDP + 32 * c, dv);
-        ptx::tmem_wait_ld();
-        pin_after_wait<32>(sv);
-        pin_after_wait<32>(dv);
-        uint32_t gk[16];
+        for (int c = 0; c < 2; ++c) {
+          uint32_t sv[32], dv[32];
+          ptx::tmem_ld32(tmem + lane_off + L::tS + 64 * h + 32 * c, sv);
+          ptx::tmem_ld32(tmem + lane_off + L::tDP + 64 * h + 32 * c, dv);
+          ptx::tmem_wait_ld();
+          pin_after_wait<32>(sv);
+          pin_after_wait<32>(dv);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float ge[2];
+          for (int i = 0; i < 32; i += 2) {
+            float ge[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float pv = ptx::ex2_approx(fmaf(__uint_as_float(sv[i + e]), sl, -lv));
-            if (32 * c + i + e >= lim) pv = 0.f;
-            ge[e] = pv * (__uint_as_float(dv[i + e]) - dval);
+            for (int e = 0; e < 2; ++e) {
+              float pv = ptx::ex2_approx(fmaf(__uint_as_float(sv[i + e]), sl, -lv));
+              if (64 * h + 32 * c + i + e >= lim) pv = 0.f;
+              ge[e] = pv * (__uint_as_float(dv[i + e]) - dval);
+            }
+            gk[16 * c + i / 2] = pack2<BF16>(ge[0], ge[1]);
           }
-          gk[i / 2] = pack2<BF16>(ge[0], ge[1]);
         }
-        ptx::tmem_st16(tmem + lane_off + L::tS + 16 * c, gk);  // dS into S columns (read)
+        ptx::tmem_st32(tmem + lane_off + L::tS + 64 * h, gk);  // dS into S columns (read)
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(L::kBarP + h));
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(L::kBarP));
     }
     if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarG), 0, wc, 58));
     if (ok) {
