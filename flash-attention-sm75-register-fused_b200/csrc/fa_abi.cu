@@ -473,6 +473,7 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
   p.causal = causal;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.trace = g_trace.load(std::memory_order_relaxed);
   p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaError_t e = fa::launch_bwd(p, O, dO, lse, head_dim, bf16, static_cast<cudaStream_t>(stream));

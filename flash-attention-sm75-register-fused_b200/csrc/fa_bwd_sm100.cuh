@@ -19,17 +19,25 @@
 // S and dP are recomputed by both main kernels, so no atomics are needed (GQA
 // groups accumulate dK / dV inside one CTA).
 //
-// Warps (256 threads): 0-3 elementwise (one TMEM lane = one row each),
-// 4 TMA producer, 5 MMA issuer + TMEM owner, 6-7 idle.
-// TMEM (512 columns): S 0..127 (its first 64 columns then hold P or dS as
-// f16 pairs), dP 128..255 (dS^T in 128..191), accumulators at 256 and 256+d.
+// Development builds (-DFA_TRACE) record clock64 timelines of the first
+// CTAs into BwdParams::trace (dK/dV kernel: per step s, MMA warp events 1-5,
+// elementwise warp 0 events 8-15, 17-18, producer event 16).
+//
+// Warps (384 threads): 0-7 elementwise in two groups g (warps 4g..4g+3, one
+// TMEM lane = one row per thread, columns [64g, 64g+64) of the 128), 8 TMA
+// producer, 9 MMA issuer + TMEM owner, 10-11 idle.
+// TMEM (512 columns), dK/dV kernel: S^T 0..127, dP^T 128..255, dV and dK
+// accumulators at 256 and 256+d; group g packs its P^T / dS^T (f16 pairs)
+// into the first 32 of its own 64 S / dP columns.  dQ kernel: S, dP, the dQ
+// accumulator at 256 and packed dS at 256+d (group g: columns 32g..).
 
 namespace fa {
 namespace {
 
-constexpr int kBwdThreads = 256;
-constexpr int kBwdWarpLoad = 4;
-constexpr int kBwdWarpMma = 5;
+constexpr int kBwdThreads = 384;
+constexpr int kBwdWarpLoad = 8;
+constexpr int kBwdWarpMma = 9;
+constexpr int kBwdElemThreads = 256;  // warps 0-7: two groups of 64 columns each
 
 template <int D>
 struct BwdLayout {
@@ -45,10 +53,11 @@ struct BwdLayout {
   static constexpr int kBarFix = 0;
   static constexpr int kBarFull = 1;
   static constexpr int kBarEmpty = kBarFull + kSlots;
-  // S and dP (or S^T, dP^T) computed: one barrier per half of the step's 128
-  // queries in the dK/dV kernel (kBarS + h), one (kBarS) in the dQ kernel
+  // kBarS: S (S^T) computed; kBarS + 1: dP (dP^T) computed
   static constexpr int kBarS = kBarEmpty + kSlots;
-  static constexpr int kBarP = kBarS + 2;            // P / dS written (128 arrivals), per half
+  // 128 arrivals each.  dK/dV kernel: kBarP = P^T written, kBarP + 1 = dS^T
+  // written.  dQ kernel: kBarP = S read, kBarP + 1 = dS written.
+  static constexpr int kBarP = kBarS + 2;
   static constexpr int kBarG = kBarP + 2;            // all gradient MMAs completed
   static constexpr int kNumBars = kBarG + 1;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
@@ -56,12 +65,14 @@ struct BwdLayout {
   static constexpr int kDynBytes = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t tS = 0, tDP = 128, tAcc0 = 256, tAcc1 = 256 + D;
+  static constexpr uint32_t tDS = 256 + D;  // dQ kernel: packed dS (64 columns)
   static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
 };
 
-// D_r = sum_c dO[r][c] O[r][c] and L2_r = LSE_r * log2(e) for every padded row
-// r < n_pad of every (batch, query head); rows >= N get D = 0, L2 = +inf so that
-// their P is exactly 0.  One warp per row.
+// Per padded row r < n_pad of every (batch, query head): nl2_r = -LSE_r*log2(e)
+// and nd_r = -D_r = -sum_c dO[r][c] O[r][c] (negated so that the main kernels
+// form s*scale*log2(e) - LSE*log2(e) and dP - D with one packed FMA / add);
+// rows >= N get nl2 = -inf, nd = 0, so their P is 0.  One warp per row.
 template <bool BF16>
 __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict__ o,
                                                           const void* __restrict__ dout,
@@ -94,8 +105,8 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
   if (lane == 0) {
-    dd[row] = acc;
-    l2[row] = (r < N) ? lse[bh * N + r] * 1.4426950408889634f : INFINITY;
+    dd[row] = -acc;
+    l2[row] = (r < N) ? -lse[bh * N + r] * 1.4426950408889634f : -INFINITY;
   }
 }
 
@@ -119,7 +130,8 @@ __device__ __forceinline__ bool bwd_setup(uint8_t* smem_raw, uint8_t*& smem, uin
     const unsigned long long st = *reinterpret_cast<volatile unsigned long long*>(&g_fa_status);
     *abort_flag = ((st >> 32) == epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
     for (int i = 0; i < L::kNumBars; ++i)
-      ptx::mbar_init(sbase + L::kOffBar + 8u * i, (i == L::kBarP || i == L::kBarP + 1) ? 128u : 1u);
+      ptx::mbar_init(sbase + L::kOffBar + 8u * i,
+                     (i == L::kBarP || i == L::kBarP + 1) ? static_cast<uint32_t>(kBwdElemThreads) : 1u);
     ptx::fence_barrier_init();
   }
   __syncthreads();
@@ -169,6 +181,65 @@ __device__ __forceinline__ void bwd_store_row(uint32_t t_acc, float mul, void* d
   }
 }
 
+// One in kBwdEmuEvery pairs of exponentials is evaluated by the FMA-pipe
+// polynomial (exp2_poly2) instead of the MUFU unit, which is the elementwise
+// phase's narrowest pipe.
+#ifndef FA_BWD_EMU_EVERY
+#define FA_BWD_EMU_EVERY 4
+#endif
+constexpr int kBwdEmuEvery = FA_BWD_EMU_EVERY;
+
+// p[i] = 2^(s[i] * sl + nl[i]) for 32 scores of this thread's row, masked
+// (MASK) to 0 outside lo <= i < hi.  nl is per column (dK/dV kernel) or one
+// value (dQ kernel: nl_col == nullptr).
+template <bool MASK>
+__device__ __forceinline__ void bwd_exp32(float* p, const uint32_t (&sv)[32], float sl,
+                                          const float4* nl_col, float nl_row, int lo, int hi) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    float4 nl;
+    if (nl_col != nullptr) nl = nl_col[i / 4];
+    else nl = make_float4(nl_row, nl_row, nl_row, nl_row);
+    float t0, t1, t2, t3;
+    ptx::ffma2(t0, t1, __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]), sl, sl, nl.x, nl.y);
+    ptx::ffma2(t2, t3, __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]), sl, sl, nl.z, nl.w);
+    if ((i / 2) % kBwdEmuEvery == 0) {
+      ptx::exp2_poly2(p[i], p[i + 1], t0, t1);
+    } else {
+      p[i] = ptx::ex2_approx(t0);
+      p[i + 1] = ptx::ex2_approx(t1);
+    }
+    p[i + 2] = ptx::ex2_approx(t2);
+    p[i + 3] = ptx::ex2_approx(t3);
+    if (MASK) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (i + e < lo || i + e >= hi) p[i + e] = 0.f;
+    }
+  }
+}
+
+// g = P * (dP + nd), 32 values packed to f16/bf16 pairs; nd per column
+// (nd_col) or one value (nd_col == nullptr).
+template <bool BF16>
+__device__ __forceinline__ void bwd_ds32(uint32_t (&gk)[16], const float* p,
+                                         const uint32_t (&dv)[32], const float4* nd_col,
+                                         float nd_row) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    float4 nd;
+    if (nd_col != nullptr) nd = nd_col[i / 4];
+    else nd = make_float4(nd_row, nd_row, nd_row, nd_row);
+    float a0, a1, a2, a3;
+    ptx::fadd2(a0, a1, __uint_as_float(dv[i]), __uint_as_float(dv[i + 1]), nd.x, nd.y);
+    ptx::fadd2(a2, a3, __uint_as_float(dv[i + 2]), __uint_as_float(dv[i + 3]), nd.z, nd.w);
+    ptx::fmul2(a0, a1, a0, a1, p[i], p[i + 1]);
+    ptx::fmul2(a2, a3, a2, a3, p[i + 2], p[i + 3]);
+    gk[i / 2] = pack2<BF16>(a0, a1);
+    gk[i / 2 + 1] = pack2<BF16>(a2, a3);
+  }
+}
+
 // ------------------------------------------------------------------ dK, dV
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
@@ -213,6 +284,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
         if (i >= L::kSlots && !bar_wait(bar(L::kBarEmpty + slot), ((i / L::kSlots) - 1) & 1, wc, 41))
           break;
         const int s = i >> 1;
+        if (!(i & 1)) FA_TRACE_AT(s, 16);
         const int bhq = step_head(s);
         const int qt = step_tile(s);
         const void* map = (i & 1) ? static_cast<const void*>(&p.tm_do) : static_cast<const void*>(&p.tm_q);
@@ -230,16 +302,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       bar_wait(bar(L::kBarFix), 0, wc, 42, false);
     }
   } else if (warp == kBwdWarpMma) {
-    // Each step's 128 queries are processed as two halves h of 64.  Issue
-    // order: S(0,h0) dP(0,h0) S(0,h1) dP(0,h1), then per step s and half h
-    //   [P(s,h) ready]  dV += P^T(s,h) dO(s,h)  dK += dS^T(s,h) Q(s,h)
-    //                   S(s+1,h)  dP(s+1,h)
-    // so the elementwise phase of one half runs while the tensor pipe works on
-    // the other.  S(s+1,h) overwrites the TMEM columns holding P^T(s,h) and
-    // dP(s+1,h) those holding dS^T(s,h); tcgen05.mma ops of one thread execute
-    // in issue order, so the gradient products have read them first.
+    // Issue order, step s (S^T and dP^T of step 0 first):
+    //   [P^T(s) written]   dV += P^T(s) dO(s)   S^T(s+1)
+    //   [dS^T(s) written]  dK += dS^T(s) Q(s)   dP^T(s+1)
+    // The elementwise warps compute P^T(s) while dP^T(s) is still on the
+    // tensor pipe and dS^T(s) while dV(s) and S^T(s+1) run.  S^T(s+1)
+    // overwrites the TMEM columns of P^T(s) and dP^T(s+1) those of dS^T(s);
+    // tcgen05.mma ops of one thread execute in issue order, so dV(s) / dK(s)
+    // have read them first.
     constexpr uint32_t fmt = BF16 ? 1u : 0u;
-    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 64, fmt, 0, 0);
+    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 128, fmt, 0, 0);
     constexpr uint32_t idesc_g = ptx::make_idesc_f16(128, D, fmt, 0, 1);
     auto slot_of = [](int i) { return i % L::kSlots; };
     auto phase_of = [](int i) { return static_cast<uint32_t>((i / L::kSlots) & 1); };
@@ -250,144 +322,152 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     const uint64_t v_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);              // K-major
     const uint64_t ring_mn = ptx::smem_desc_sw128(sbase + L::kOffRing, L::kBlockBytes, 1024);  // MN-major
-    // S^T(s,h) = K Q^T and dP^T(s,h) = V dO^T for queries [64h, 64h+64) of
-    // step s (B = 64 rows of the Q / dO tile: 8 KB into each 64-column block)
-    auto issue_scores = [&](int s, int h) {
-      const uint64_t q_off = static_cast<uint64_t>((slot_of(2 * s) * L::kTile + h * 8192) >> 4);
-      const uint64_t d_off = static_cast<uint64_t>((slot_of(2 * s + 1) * L::kTile + h * 8192) >> 4);
+    // D = A B^T with A the fixed K (V) tile and B ring item `item` (Q or dO), K = d
+    auto issue_score = [&](uint32_t d_col, uint64_t a_desc, int item, uint32_t done_bar) {
+      const uint64_t b_off = static_cast<uint64_t>((slot_of(item) * L::kTile) >> 4);
       if (ptx::elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tS + 64 * h, k_desc + off, ring_k + q_off + off, idesc_s, kk > 0 ? 1u : 0u);
+          ptx::mma_ss(tmem + d_col, a_desc + off, ring_k + b_off + off, idesc_s, kk > 0 ? 1u : 0u);
         }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tDP + 64 * h, v_desc + off, ring_k + d_off + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(L::kBarS + h));
+        ptx::mma_commit(done_bar);
       }
       __syncwarp();
     };
-    // dV += P^T dO and dK += dS^T Q over queries [64h, 64h+64) of step s
-    // (A from TMEM: P^T / dS^T packed in the half's first 32 columns; B
-    // MN-major, K = queries, 16 rows = 2 KB per K step)
-    auto issue_grads = [&](int s, int h) {
-      const uint64_t q_off = static_cast<uint64_t>((slot_of(2 * s) * L::kTile) >> 4);
-      const uint64_t d_off = static_cast<uint64_t>((slot_of(2 * s + 1) * L::kTile) >> 4);
+    // acc += A B with A packed in TMEM (queries 64g.. of group g at columns
+    // a_col + 64g ..+32) and B ring item `item` MN-major (K = the step's 128
+    // queries, 16 rows = 2 KB per K step)
+    auto issue_grad = [&](uint32_t acc_col, uint32_t a_col, int item, bool first) {
+      const uint64_t b_off = static_cast<uint64_t>((slot_of(item) * L::kTile) >> 4);
       if (ptx::elect_one()) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t off = static_cast<uint64_t>(((4 * h + k) * 2048) >> 4);
-          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tS + 64 * h + 8 * k, ring_mn + d_off + off, idesc_g,
-                      (s > 0 || h > 0 || k > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t off = static_cast<uint64_t>(((4 * h + k) * 2048) >> 4);
-          ptx::mma_ts(tmem + L::tAcc1, tmem + L::tDP + 64 * h + 8 * k, ring_mn + q_off + off, idesc_g,
-                      (s > 0 || h > 0 || k > 0) ? 1u : 0u);
-        }
-        if (h == 1) {  // the step's Q and dO tiles are read for the last time
-          ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * s)));
-          ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * s + 1)));
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          ptx::mma_ts(tmem + acc_col, tmem + a_col + 8 * kk + (kk >= 4 ? 32 : 0),
+                      ring_mn + b_off + static_cast<uint64_t>((kk * 2048) >> 4), idesc_g,
+                      (!first || kk > 0) ? 1u : 0u);
       }
       __syncwarp();
     };
     bool ok = wait(bar(L::kBarFix), 0, 43);
     if (ok && n_steps > 0) {
-      ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 44) &&
-           wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 44);
+      ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 44);
       if (ok) {
         ptx::tc_fence_after();
-        issue_scores(0, 0);
-        issue_scores(0, 1);
+        issue_score(L::tS, k_desc, 0, bar(L::kBarS));
+        ok = wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 44);
       }
+      if (ok) issue_score(L::tDP, v_desc, 1, bar(L::kBarS + 1));
     }
     for (int s = 0; ok && s < n_steps; ++s) {
       const bool next = s + 1 < n_steps;
+      const int iq = 2 * s, id = 2 * s + 1;
+      if (lane == 0) FA_TRACE_AT(s, 5);
+      if (!(ok = wait(bar(L::kBarP), s & 1, 45))) break;
+      if (lane == 0) FA_TRACE_AT(s, 1);
+      ptx::tc_fence_after();
+      issue_grad(L::tAcc0, L::tS, id, s == 0);  // dV += P^T dO
       if (next) {
-        const int iq = 2 * s + 2, id = 2 * s + 3;
-        if (!(ok = wait(bar(L::kBarFull + slot_of(iq)), phase_of(iq), 44))) break;
-        if (!(ok = wait(bar(L::kBarFull + slot_of(id)), phase_of(id), 44))) break;
+        if (!(ok = wait(bar(L::kBarFull + slot_of(iq + 2)), phase_of(iq + 2), 44))) break;
+        issue_score(L::tS, k_desc, iq + 2, bar(L::kBarS));  // S^T(s+1)
       }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (!(ok = wait(bar(L::kBarP + h), s & 1, 45))) break;
-        ptx::tc_fence_after();
-        issue_grads(s, h);
-        if (next) issue_scores(s + 1, h);
+      if (lane == 0) FA_TRACE_AT(s, 2);
+      if (!(ok = wait(bar(L::kBarP + 1), s & 1, 45))) break;
+      if (lane == 0) FA_TRACE_AT(s, 3);
+      ptx::tc_fence_after();
+      issue_grad(L::tAcc1, L::tDP, iq, s == 0);  // dK += dS^T Q
+      // the step's Q / dO tiles and their vectors are read for the last time
+      if (ptx::elect_one()) {
+        ptx::mma_commit(bar(L::kBarEmpty + slot_of(iq)));
+        ptx::mma_commit(bar(L::kBarEmpty + slot_of(id)));
       }
+      __syncwarp();
+      if (next) {
+        if (!(ok = wait(bar(L::kBarFull + slot_of(id + 2)), phase_of(id + 2), 44))) break;
+        issue_score(L::tDP, v_desc, id + 2, bar(L::kBarS + 1));  // dP^T(s+1)
+      }
+      if (lane == 0) FA_TRACE_AT(s, 4);
     }
     if (ptx::elect_one()) ptx::mma_commit(bar(L::kBarG));
     __syncwarp();
     bar_wait(bar(L::kBarG), 0, wc, 46, false);
     __syncwarp();
-  } else if (warp < 4) {
-    // rows = keys of tile t; columns = the step's 128 queries, in two halves
-    const int r = warp * 32 + lane;
+  } else if (warp < 8) {
+    // rows = keys of tile t; group g takes queries [64g, 64g+64) of the step.
+    // P^T stays in registers (fp32) between the two phases.
+    const int g = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
     const int key = t * 128 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t col0 = 64u * g;
     const float sl = p.scale_log2;
     bool ok = true;
     for (int s = 0; ok && s < n_steps; ++s) {
       const int qt = step_tile(s);
-      const float4* l2v = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s) % L::kSlots) * L::kVec);
-      const float4* ddv = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s + 1) % L::kSlots) * L::kVec);
+      const float4* l2v = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s) % L::kSlots) * L::kVec) + 16 * g;
+      const float4* ddv = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s + 1) % L::kSlots) * L::kVec) + 16 * g;
       const bool diag = p.causal && qt == t;  // query < key is masked
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + h), s & 1, wc, 47));
-        if (!ok) break;
-        ptx::tc_fence_after();
-        uint32_t pk[32], gk[32];
+      if (threadIdx.x == 0) FA_TRACE_AT(s, 8);
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), s & 1, wc, 47));
+      if (!ok) break;
+      if (threadIdx.x == 0) FA_TRACE_AT(s, 9);
+      ptx::tc_fence_after();
+      float pr[64];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t sv[32], dv[32];
-          ptx::tmem_ld32(tmem + lane_off + L::tS + 64 * h + 32 * c, sv);
-          ptx::tmem_ld32(tmem + lane_off + L::tDP + 64 * h + 32 * c, dv);
-          ptx::tmem_wait_ld();
-          pin_after_wait<32>(sv);
-          pin_after_wait<32>(dv);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32];
+        ptx::tmem_ld32(tmem + lane_off + L::tS + col0 + 32 * c, sv);
+        ptx::tmem_wait_ld();
+        pin_after_wait<32>(sv);
+        if (threadIdx.x == 0) FA_TRACE_AT(s, c ? 15 : 13);
+        // diagonal tile: query q = col0 + 32c + i is kept when q >= key r
+        if (diag)
+          bwd_exp32<true>(pr + 32 * c, sv, sl, l2v + 8 * c, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
+        else
+          bwd_exp32<false>(pr + 32 * c, sv, sl, l2v + 8 * c, 0.f, 0, 32);
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const int q0 = 64 * h + 32 * c + i;  // query within the tile
-            const float4 lv = l2v[q0 / 4];
-            const float4 dd = ddv[q0 / 4];
-            const float lq[4] = {lv.x, lv.y, lv.z, lv.w};
-            const float dq[4] = {dd.x, dd.y, dd.z, dd.w};
-            float pe[4], ge[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float pv = ptx::ex2_approx(fmaf(__uint_as_float(sv[i + e]), sl, -lq[e]));
-              if (diag && q0 + e < r) pv = 0.f;
-              pe[e] = pv;
-              ge[e] = pv * (__uint_as_float(dv[i + e]) - dq[e]);
-            }
-            pk[16 * c + i / 2] = pack2<BF16>(pe[0], pe[1]);
-            pk[16 * c + i / 2 + 1] = pack2<BF16>(pe[2], pe[3]);
-            gk[16 * c + i / 2] = pack2<BF16>(ge[0], ge[1]);
-            gk[16 * c + i / 2 + 1] = pack2<BF16>(ge[2], ge[3]);
-          }
-        }
-        // P^T into S columns 64h.., dS^T into dP columns 64h.. (both already read)
-        ptx::tmem_st32(tmem + lane_off + L::tS + 64 * h, pk);
-        ptx::tmem_st32(tmem + lane_off + L::tDP + 64 * h, gk);
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(L::kBarP + h));
+        for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(pr[32 * c + 2 * i], pr[32 * c + 2 * i + 1]);
+        if (threadIdx.x == 0) FA_TRACE_AT(s, c ? 17 : 14);
+        // P^T into the group's S columns col0 + 16c.. (already read)
+        ptx::tmem_st16(tmem + lane_off + L::tS + col0 + 16 * c, pk);
       }
+      ptx::tmem_wait_st();
+      if (threadIdx.x == 0) FA_TRACE_AT(s, 18);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(L::kBarP));
+      if (threadIdx.x == 0) FA_TRACE_AT(s, 10);
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + 1), s & 1, wc, 47));
+      if (!ok) break;
+      if (threadIdx.x == 0) FA_TRACE_AT(s, 11);
+      ptx::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dv[32];
+        ptx::tmem_ld32(tmem + lane_off + L::tDP + col0 + 32 * c, dv);
+        ptx::tmem_wait_ld();
+        pin_after_wait<32>(dv);
+        uint32_t gk[16];
+        bwd_ds32<BF16>(gk, pr + 32 * c, dv, ddv + 8 * c, 0.f);
+        // dS^T into the group's dP columns col0 + 16c.. (already read)
+        ptx::tmem_st16(tmem + lane_off + L::tDP + col0 + 16 * c, gk);
+      }
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(L::kBarP + 1));
+      if (threadIdx.x == 0) FA_TRACE_AT(s, 12);
     }
     if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarG), 0, wc, 48));
     if (ok) {
+      // group 0 writes the dV rows, group 1 the dK rows
       ptx::tc_fence_after();
       const bool store = key < p.N;
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       const size_t row = static_cast<size_t>(bhk) * p.N + key;
-      bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc0, 1.0f, reinterpret_cast<T*>(p.dv) + row * D, store);
-      bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc1, p.scale, reinterpret_cast<T*>(p.dk) + row * D, store);
+      if (g == 0)
+        bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc0, 1.0f, reinterpret_cast<T*>(p.dv) + row * D, store);
+      else
+        bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc1, p.scale, reinterpret_cast<T*>(p.dk) + row * D, store);
     }
   }
   bwd_teardown<L>(tmem, warp);
@@ -446,14 +526,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       bar_wait(bar(L::kBarFix), 0, wc, 52, false);
     }
   } else if (warp == kBwdWarpMma) {
-    // Keys of each K/V tile in two halves h of 64, issued as
-    //   S(0,h0) dP(0,h0) S(0,h1) dP(0,h1), then per tile j and half h:
-    //   [dS(j,h) ready]  dQ += dS(j,h) K(j,h)  S(j+1,h)  dP(j+1,h)
-    // (the elementwise phase of one half overlaps the other half's products;
-    // S(j+1,h) overwrites the columns of dS(j,h) after dQ has read them, in
-    // issue order).
+    // Issue order, K/V tile j (S and dP of tile 0 first):
+    //   [S(j) read]      S(j+1)
+    //   [dS(j) written]  dQ += dS(j) K_j   dP(j+1)
+    // dS has its own TMEM columns, so S(j+1) overwrites S(j) as soon as the
+    // elementwise warps hold P(j) in registers; they compute P(j+1) while
+    // dQ(j) and dP(j+1) run.  dP(j+1) overwrites dP(j) after they have read
+    // it, and it completes after dQ(j) (issue order), before dS(j+1) is written.
     constexpr uint32_t fmt = BF16 ? 1u : 0u;
-    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 64, fmt, 0, 0);
+    constexpr uint32_t idesc_s = ptx::make_idesc_f16(128, 128, fmt, 0, 0);
     constexpr uint32_t idesc_g = ptx::make_idesc_f16(128, D, fmt, 0, 1);
     auto slot_of = [](int i) { return i % L::kSlots; };
     auto phase_of = [](int i) { return static_cast<uint32_t>((i / L::kSlots) & 1); };
@@ -464,115 +545,114 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     const uint64_t do_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);
     const uint64_t ring_mn = ptx::smem_desc_sw128(sbase + L::kOffRing, L::kBlockBytes, 1024);
-    // S(j,h) = Q K^T, dP(j,h) = dO V^T over keys [64h, 64h+64) of tile j
-    auto issue_scores = [&](int j, int h) {
-      const uint64_t k_off = static_cast<uint64_t>((slot_of(2 * j) * L::kTile + h * 8192) >> 4);
-      const uint64_t v_off = static_cast<uint64_t>((slot_of(2 * j + 1) * L::kTile + h * 8192) >> 4);
+    // D = A B^T with A the fixed Q (dO) tile and B ring item `item` (K or V), K = d
+    auto issue_score = [&](uint32_t d_col, uint64_t a_desc, int item, uint32_t done_bar) {
+      const uint64_t b_off = static_cast<uint64_t>((slot_of(item) * L::kTile) >> 4);
       if (ptx::elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tS + 64 * h, q_desc + off, ring_k + k_off + off, idesc_s, kk > 0 ? 1u : 0u);
+          ptx::mma_ss(tmem + d_col, a_desc + off, ring_k + b_off + off, idesc_s, kk > 0 ? 1u : 0u);
         }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + L::tDP + 64 * h, do_desc + off, ring_k + v_off + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(L::kBarS + h));
-        if (h == 1) ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * j + 1)));  // V_j read
-      }
-      __syncwarp();
-    };
-    // dQ += dS(j,h) K(j,h) (A = dS from TMEM, B = K_j MN-major: K = keys)
-    auto issue_grad = [&](int j, int h) {
-      const uint64_t k_off = static_cast<uint64_t>((slot_of(2 * j) * L::kTile) >> 4);
-      if (ptx::elect_one()) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t off = static_cast<uint64_t>(((4 * h + k) * 2048) >> 4);
-          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tS + 64 * h + 8 * k, ring_mn + k_off + off, idesc_g,
-                      (j > 0 || h > 0 || k > 0) ? 1u : 0u);
-        }
-        if (h == 1) ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * j)));  // K_j read
+        ptx::mma_commit(done_bar);
       }
       __syncwarp();
     };
     bool ok = wait(bar(L::kBarFix), 0, 53);
     if (ok && n_kv > 0) {
-      ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 54) &&
-           wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 54);
+      ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 54);
       if (ok) {
         ptx::tc_fence_after();
-        issue_scores(0, 0);
-        issue_scores(0, 1);
+        issue_score(L::tS, q_desc, 0, bar(L::kBarS));
+        ok = wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 54);
       }
+      if (ok) issue_score(L::tDP, do_desc, 1, bar(L::kBarS + 1));
     }
     for (int j = 0; ok && j < n_kv; ++j) {
       const bool next = j + 1 < n_kv;
+      const int ik = 2 * j, iv = 2 * j + 1;
+      if (!(ok = wait(bar(L::kBarP), j & 1, 55))) break;
       if (next) {
-        const int ik = 2 * j + 2, iv = 2 * j + 3;
-        if (!(ok = wait(bar(L::kBarFull + slot_of(ik)), phase_of(ik), 54))) break;
-        if (!(ok = wait(bar(L::kBarFull + slot_of(iv)), phase_of(iv), 54))) break;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (!(ok = wait(bar(L::kBarP + h), j & 1, 55))) break;
+        if (!(ok = wait(bar(L::kBarFull + slot_of(ik + 2)), phase_of(ik + 2), 54))) break;
         ptx::tc_fence_after();
-        issue_grad(j, h);
-        if (next) issue_scores(j + 1, h);
+        issue_score(L::tS, q_desc, ik + 2, bar(L::kBarS));  // S(j+1)
+      }
+      if (!(ok = wait(bar(L::kBarP + 1), j & 1, 55))) break;
+      ptx::tc_fence_after();
+      // dQ += dS K_j (A = dS from TMEM, B = K_j MN-major: K = keys)
+      const uint64_t k_off = static_cast<uint64_t>((slot_of(ik) * L::kTile) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          ptx::mma_ts(tmem + L::tAcc0, tmem + L::tDS + 8 * kk,
+                      ring_mn + k_off + static_cast<uint64_t>((kk * 2048) >> 4), idesc_g,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        ptx::mma_commit(bar(L::kBarEmpty + slot_of(ik)));  // K_j read
+        ptx::mma_commit(bar(L::kBarEmpty + slot_of(iv)));  // V_j read
+      }
+      __syncwarp();
+      if (next) {
+        if (!(ok = wait(bar(L::kBarFull + slot_of(iv + 2)), phase_of(iv + 2), 54))) break;
+        issue_score(L::tDP, do_desc, iv + 2, bar(L::kBarS + 1));  // dP(j+1)
       }
     }
     if (ptx::elect_one()) ptx::mma_commit(bar(L::kBarG));
     __syncwarp();
     bar_wait(bar(L::kBarG), 0, wc, 56, false);
     __syncwarp();
-  } else if (warp < 4) {
-    const int r = warp * 32 + lane;
+  } else if (warp < 8) {
+    // rows = queries of tile t; group g takes keys [64g, 64g+64) of each K/V tile
+    const int g = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
     const int q_row = t * 128 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int col0 = 64 * g;
     const float sl = p.scale_log2;
-    const float lv = p.l2[static_cast<size_t>(bh) * p.n_pad + q_row];
-    const float dval = p.dd[static_cast<size_t>(bh) * p.n_pad + q_row];
+    const float nlv = p.l2[static_cast<size_t>(bh) * p.n_pad + q_row];  // -LSE*log2(e)
+    const float ndv = p.dd[static_cast<size_t>(bh) * p.n_pad + q_row];  // -D
     bool ok = true;
     for (int j = 0; ok && j < n_kv; ++j) {
       // keys >= N and (causal) keys > this query get P = 0
-      int lim = p.N - j * 128;
-      if (p.causal && j == t) lim = min(lim, r + 1);
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + h), j & 1, wc, 57));
-        if (!ok) break;
-        ptx::tc_fence_after();
-        uint32_t gk[32];
+      int lim = p.N - j * 128 - col0;
+      if (p.causal && j == t) lim = min(lim, r + 1 - col0);
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), j & 1, wc, 57));
+      if (!ok) break;
+      ptx::tc_fence_after();
+      // keys of the group past N or (causal) past this query: masked tiles only
+      const bool masked = (p.causal && j == t) || p.N - j * 128 - col0 < 64;
+      float pr[64];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t sv[32], dv[32];
-          ptx::tmem_ld32(tmem + lane_off + L::tS + 64 * h + 32 * c, sv);
-          ptx::tmem_ld32(tmem + lane_off + L::tDP + 64 * h + 32 * c, dv);
-          ptx::tmem_wait_ld();
-          pin_after_wait<32>(sv);
-          pin_after_wait<32>(dv);
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float ge[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              float pv = ptx::ex2_approx(fmaf(__uint_as_float(sv[i + e]), sl, -lv));
-              if (64 * h + 32 * c + i + e >= lim) pv = 0.f;
-              ge[e] = pv * (__uint_as_float(dv[i + e]) - dval);
-            }
-            gk[16 * c + i / 2] = pack2<BF16>(ge[0], ge[1]);
-          }
-        }
-        ptx::tmem_st32(tmem + lane_off + L::tS + 64 * h, gk);  // dS into S columns (read)
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(L::kBarP + h));
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32];
+        ptx::tmem_ld32(tmem + lane_off + L::tS + col0 + 32 * c, sv);
+        ptx::tmem_wait_ld();
+        pin_after_wait<32>(sv);
+        if (masked)
+          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, nlv, 0, lim - 32 * c);
+        else
+          bwd_exp32<false>(pr + 32 * c, sv, sl, nullptr, nlv, 0, 32);
       }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(L::kBarP));  // S(j) read: S(j+1) may overwrite it
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + 1), j & 1, wc, 57));
+      if (!ok) break;
+      ptx::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dv[32];
+        ptx::tmem_ld32(tmem + lane_off + L::tDP + col0 + 32 * c, dv);
+        ptx::tmem_wait_ld();
+        pin_after_wait<32>(dv);
+        uint32_t gk[16];
+        bwd_ds32<BF16>(gk, pr + 32 * c, dv, nullptr, ndv);
+        ptx::tmem_st16(tmem + lane_off + L::tDS + 32 * g + 16 * c, gk);
+      }
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(L::kBarP + 1));  // dS(j) written
     }
     if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarG), 0, wc, 58));
-    if (ok) {
+    if (ok && g == 0) {
       ptx::tc_fence_after();
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       const size_t row = static_cast<size_t>(bh) * p.N + q_row;

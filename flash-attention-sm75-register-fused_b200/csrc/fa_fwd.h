@@ -95,8 +95,8 @@ __host__ __device__ inline int kv_tiles_for_tile(const FwdParams& p, int t) {
 }
 
 // Backward parameters (dK/dV and dQ kernels).  Q, K, V, dO as 3-D TMA maps
-// like the forward; l2 / dd hold per query row LSE*log2(e) (+inf past N) and
-// rowsum(dO * O) (0 past N), each [B*Hq][n_pad] with n_pad = 128 * n_tiles.
+// like the forward; l2 / dd hold per query row -LSE*log2(e) (-inf past N) and
+// -rowsum(dO * O) (0 past N), each [B*Hq][n_pad] with n_pad = 128 * n_tiles.
 struct alignas(64) BwdParams {
   CUtensorMap tm_q, tm_k, tm_v, tm_do;
   void* dq;          // [B, Hq, N, d]
@@ -106,6 +106,7 @@ struct alignas(64) BwdParams {
   const float* dd;
   int B, Hq, Hkv, N, n_pad, group, n_tiles, causal;
   float scale, scale_log2;
+  long long* trace;  // timeline samples, used only in FA_TRACE builds
   unsigned epoch;
   unsigned long long timeout_ns;
 };
