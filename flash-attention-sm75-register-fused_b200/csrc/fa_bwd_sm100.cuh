@@ -190,8 +190,9 @@ __device__ __forceinline__ void bwd_store_row(uint32_t t_acc, float mul, void* d
 constexpr int kBwdEmuEvery = FA_BWD_EMU_EVERY;
 
 // p[i] = 2^(s[i] * sl + nl[i]) for 32 scores of this thread's row, masked
-// (MASK) to 0 outside lo <= i < hi.  nl is per column (dK/dV kernel) or one
-// value (dQ kernel: nl_col == nullptr).
+// (MASK) to 0 outside lo <= i < hi.  nl holds the 32 per-column values
+// (dK/dV kernel: loaded from shared memory before the scores, see
+// bwd_load_vec32) or one value (dQ kernel: nl == nullptr).
 template <bool MASK>
 __device__ __forceinline__ void bwd_exp32(float* p, const uint32_t (&sv)[32], float sl,
                                           const float4* nl_col, float nl_row, int lo, int hi) {
@@ -217,6 +218,15 @@ __device__ __forceinline__ void bwd_exp32(float* p, const uint32_t (&sv)[32], fl
         if (i + e < lo || i + e >= hi) p[i + e] = 0.f;
     }
   }
+}
+
+// 32 per-column values from shared memory into registers, all loads issued
+// together: while the tensor pipe streams its operands from shared memory, a
+// load can wait hundreds of cycles, so they are started before the TMEM load
+// of the same columns rather than one by one inside the arithmetic.
+__device__ __forceinline__ void bwd_load_vec32(float4 (&v)[8], const float4* src) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = src[k];
 }
 
 // g = P * (dP + nd), 32 values packed to f16/bf16 pairs; nd per column
@@ -415,6 +425,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       float pr[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
+        float4 nl[8];
+        bwd_load_vec32(nl, l2v + 8 * c);
         uint32_t sv[32];
         ptx::tmem_ld32(tmem + lane_off + L::tS + col0 + 32 * c, sv);
         ptx::tmem_wait_ld();
@@ -422,9 +434,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
         if (threadIdx.x == 0) FA_TRACE_AT(s, c ? 15 : 13);
         // diagonal tile: query q = col0 + 32c + i is kept when q >= key r
         if (diag)
-          bwd_exp32<true>(pr + 32 * c, sv, sl, l2v + 8 * c, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
+          bwd_exp32<true>(pr + 32 * c, sv, sl, nl, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
         else
-          bwd_exp32<false>(pr + 32 * c, sv, sl, l2v + 8 * c, 0.f, 0, 32);
+          bwd_exp32<false>(pr + 32 * c, sv, sl, nl, 0.f, 0, 32);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(pr[32 * c + 2 * i], pr[32 * c + 2 * i + 1]);
@@ -443,12 +455,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       ptx::tc_fence_after();
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
+        float4 nd[8];
+        bwd_load_vec32(nd, ddv + 8 * c);
         uint32_t dv[32];
         ptx::tmem_ld32(tmem + lane_off + L::tDP + col0 + 32 * c, dv);
         ptx::tmem_wait_ld();
         pin_after_wait<32>(dv);
         uint32_t gk[16];
-        bwd_ds32<BF16>(gk, pr + 32 * c, dv, ddv + 8 * c, 0.f);
+        bwd_ds32<BF16>(gk, pr + 32 * c, dv, nd, 0.f);
         // dS^T into the group's dP columns col0 + 16c.. (already read)
         ptx::tmem_st16(tmem + lane_off + L::tDP + col0 + 16 * c, gk);
       }
