@@ -92,7 +92,10 @@ struct Layout {
   // persistent launches (several work items per CTA): the MMAs that read Q
   // buffer b for one item have completed, so the next Q may overwrite it
   static constexpr int kBarQFree = kBarDrain + 1;       // 2
-  static constexpr int kNumBars = kBarQFree + 2;
+  // first half of P_g (keys 0-63) written: the PV MMA starts on it while the
+  // softmax computes the second half (128 arrivals)
+  static constexpr int kBarPH = kBarQFree + 2;          // 2
+  static constexpr int kNumBars = kBarPH + 2;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynBytes = kBytes + 1024;  // slack for 1024-byte alignment
@@ -239,11 +242,12 @@ __device__ __forceinline__ float row_extreme(const float (&x)[N]) {
 }
 
 // exp2(x * sl - m) for the 128 scores of this thread's row; the packed
-// f16/bf16 values go to TMEM (P operand of the PV MMA) in two 32-column halves;
-// returns their fp32 sum.
+// f16/bf16 values go to TMEM (P operand of the PV MMA) in two 32-column halves,
+// the first announced on `half_bar` as soon as it is written; returns their
+// fp32 sum.
 template <bool BF16, bool kEmulate>
 __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, float neg_m,
-                                          uint32_t tP) {
+                                          uint32_t tP, uint32_t half_bar) {
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -266,6 +270,11 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
       pk[c] = pack2<BF16>(e0, e1);
     }
     ptx::tmem_st32(tP + 32 * h, pk);
+    if (h == 0) {
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(half_bar);
+    }
   }
   ptx::fadd2(a0, a1, a0, a1, b0, b1);
   return a0 + a1;
@@ -423,7 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     *abort_flag = ((st >> 32) == p.epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
     for (int i = 0; i < L::kNumBars; ++i) {
       // P completes on an arrival of every thread of a softmax group
-      const bool is_p = (i == L::kBarP || i == L::kBarP + 1);
+      const bool is_p = (i == L::kBarP || i == L::kBarP + 1 || i == L::kBarPH ||
+                         i == L::kBarPH + 1);
       ptx::mbar_init(bar(i), is_p ? 128u : 1u);
     }
     ptx::fence_barrier_init();
@@ -557,25 +567,39 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         }
         __syncwarp();
       };
-      // O_g (+)= P_g V with V in ring item `vi`; `first` starts the accumulator
-      auto issue_pv = [&](int g, int vi, bool first) {
-        const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(vi) * L::kTile) >> 4);
-        if (ptx::elect_one()) {
-#pragma unroll
-          for (int kk = 0; kk < kBlockN / 16; ++kk)
-            ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
-                        vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
-                        (!first || kk > 0) ? 1u : 0u);
-          ptx::mma_commit(bar(L::kBarO + g));
-        }
-        __syncwarp();
-      };
       auto commit = [&](uint32_t b) {
         if (ptx::elect_one()) ptx::mma_commit(b);
         __syncwarp();
       };
       auto wait = [&](uint32_t b, uint32_t ph, int site) {
         return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
+      };
+      // O_g (+)= P_g V with V in ring item `vi`; `first` starts the accumulator.
+      // Keys 0-63 (P columns 0-31) go out once the softmax has announced the
+      // first half of P (parity ph), keys 64-127 after the whole P.
+      auto issue_pv = [&](int g, int vi, bool first, uint32_t ph) -> bool {
+        const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(vi) * L::kTile) >> 4);
+        if (!wait(bar(L::kBarPH + g), ph, 13 + 3 * g)) return false;
+        ptx::tc_fence_after();
+        if (ptx::elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / 32; ++kk)
+            ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
+                        vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
+                        (!first || kk > 0) ? 1u : 0u);
+        }
+        __syncwarp();
+        if (!wait(bar(L::kBarP + g), ph, 13 + 3 * g)) return false;
+        ptx::tc_fence_after();
+        if (ptx::elect_one()) {
+#pragma unroll
+          for (int kk = kBlockN / 32; kk < kBlockN / 16; ++kk)
+            ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
+                        vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv, 1u);
+          ptx::mma_commit(bar(L::kBarO + g));
+        }
+        __syncwarp();
+        return true;
       };
 
 
@@ -629,10 +653,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               break;
             if (lane == 0) FA_TRACE_AT(j, 7);
             if (j < it.n_kv[0]) {
-              if (!(ok = wait(bar(L::kBarP), j & 1, 13))) break;
-              ptx::tc_fence_after();
               if (lane == 0) FA_TRACE_AT(j, 0);
-              issue_pv(0, item_v, j == 0);
+              if (!(ok = issue_pv(0, item_v, j == 0, j & 1))) break;
               if (lane == 0) FA_TRACE_AT(j, 4);
               if (next0) {
                 if (lane == 0) FA_TRACE_AT(j, 1);
@@ -642,10 +664,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               }
             }
             if (j < it.n_kv[1]) {
-              if (!(ok = wait(bar(L::kBarP + 1), j & 1, 16))) break;
-              ptx::tc_fence_after();
               if (lane == 0) FA_TRACE_AT(j, 2);
-              issue_pv(1, item_v, j == 0);
+              if (!(ok = issue_pv(1, item_v, j == 0, j & 1))) break;
             }
             commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
             if (next1) {
@@ -681,10 +701,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               const int ki = next ? ring + k_item_of(it, true, g, j + 1) : 0;
               if (!(ok = wait(bar(L::kBarFull + slot_of(vi)), phase_of(vi), 12))) break;
               if (next && !(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 14))) break;
-              if (!(ok = wait(bar(L::kBarP + g), (cnt[g] + j) & 1, 13 + 3 * g))) break;
-              ptx::tc_fence_after();
               if (lane == 0) FA_TRACE_AT(j, 2 * g);
-              issue_pv(g, vi, j == 0);
+              if (!(ok = issue_pv(g, vi, j == 0, (cnt[g] + j) & 1))) break;
               commit(bar(L::kBarEmpty + slot_of(vi)));
               if (next) {
                 if (lane == 0) FA_TRACE_AT(j, 1 + 2 * g);
@@ -851,8 +869,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 
       // P = exp2(x * sl_eff - m): packed FMA, then exp2 split between the MUFU
       // unit and a polynomial on the FMA pipe; written to TMEM in two halves.
-      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP)
-                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP);
+      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP, bar(L::kBarPH + g))
+                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP, bar(L::kBarPH + g));
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       if (lane == 0) FA_TRACE_AT(j, 8 + sw);
