@@ -425,7 +425,10 @@ int fa_fwd_kvcache(const void* Q, const void* K, const void* V, void* O, float* 
 size_t fa_bwd_workspace_bytes(int B, int Hq, int N) {
   if (B <= 0 || Hq <= 0 || N <= 0) return 0;
   const size_t n_pad = (static_cast<size_t>(N) + 127) / 128 * 128;
-  return 2 * static_cast<size_t>(B) * Hq * n_pad * sizeof(float);
+  // per query row: -LSE*log2(e) and -D (fp32); per 128-row query tile: two
+  // 4 KB operand tiles (BwdParams::vt)
+  return 2 * static_cast<size_t>(B) * Hq * n_pad * sizeof(float) +
+         static_cast<size_t>(B) * Hq * (n_pad / 128) * 8192;
 }
 
 int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
@@ -465,6 +468,7 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
   p.n_pad = p.n_tiles * 128;
   p.l2 = static_cast<const float*>(workspace);
   p.dd = static_cast<const float*>(workspace) + static_cast<size_t>(bhq) * p.n_pad;
+  p.vt = static_cast<const uint8_t*>(workspace) + 2 * static_cast<size_t>(bhq) * p.n_pad * sizeof(float);
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;

@@ -45,11 +45,13 @@ struct BwdLayout {
   static constexpr int kBlockBytes = 128 * 128;  // one 64-column block of a 128-row tile
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kSlots = (D == 128) ? 4 : 8;
-  static constexpr int kVec = 128 * 4;  // one tile's LSE*log2e or D values
+  // K-major 128x16 operand tile without swizzle (see BwdParams::vt)
+  static constexpr int kVec = 4096;
   static constexpr int kOffFix = 0;     // the CTA's two fixed tiles
   static constexpr int kOffRing = 2 * kTile;
-  static constexpr int kOffVec = kOffRing + kSlots * kTile;  // vector of ring slot s
-  static constexpr int kOffBar = kOffVec + kSlots * kVec;
+  static constexpr int kOffVec = kOffRing + kSlots * kTile;  // vector tile of ring slot s
+  static constexpr int kOffOnes = kOffVec + kSlots * kVec;   // A operand: ones in k = 0..2
+  static constexpr int kOffBar = kOffOnes + kVec;
   static constexpr int kBarFix = 0;
   static constexpr int kBarFull = 1;
   static constexpr int kBarEmpty = kBarFull + kSlots;
@@ -78,8 +80,10 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
                                                           const void* __restrict__ dout,
                                                           const float* __restrict__ lse,
                                                           float* __restrict__ l2,
-                                                          float* __restrict__ dd, int N, int n_pad,
-                                                          long long n_rows, int d) {
+                                                          float* __restrict__ dd,
+                                                          uint8_t* __restrict__ vt, float scale,
+                                                          int N, int n_pad, long long n_rows,
+                                                          int d) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= n_rows) return;
@@ -105,8 +109,34 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
   if (lane == 0) {
+    const float lse_r = (r < N) ? lse[bh * N + r] : 0.f;
     dd[row] = -acc;
-    l2[row] = (r < N) ? -lse[bh * N + r] * 1.4426950408889634f : -INFINITY;
+    l2[row] = (r < N) ? -lse_r * 1.4426950408889634f : -INFINITY;
+    // operand tiles of the dK/dV kernel: -LSE/scale (a large negative value
+    // for padded rows, whose P must vanish) and -D as three 16-bit terms
+    const float vals[2] = {(r < N) ? -lse_r / scale : -30000.f, -acc};
+    const int n = r & 127;
+    uint8_t* tile = vt + (static_cast<size_t>(row >> 7) * 2) * 4096 + (n >> 3) * 256 + (n & 7) * 16;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      uint32_t h[3];
+      float rest = vals[v];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        if constexpr (BF16) {
+          const __nv_bfloat16 t = __float2bfloat16_rn(rest);
+          rest -= __bfloat162float(t);
+          h[k] = *reinterpret_cast<const unsigned short*>(&t);
+        } else {
+          const __half t = __float2half_rn(rest);
+          rest -= __half2float(t);
+          h[k] = *reinterpret_cast<const unsigned short*>(&t);
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(tile + v * 4096);
+      dst[0] = make_uint4(h[0] | (h[1] << 16), h[2], 0u, 0u);  // k = 0..7
+      dst[8] = make_uint4(0u, 0u, 0u, 0u);                     // k = 8..15 (128 B further)
+    }
   }
 }
 
@@ -190,9 +220,8 @@ __device__ __forceinline__ void bwd_store_row(uint32_t t_acc, float mul, void* d
 constexpr int kBwdEmuEvery = FA_BWD_EMU_EVERY;
 
 // p[i] = 2^(s[i] * sl + nl[i]) for 32 scores of this thread's row, masked
-// (MASK) to 0 outside lo <= i < hi.  nl holds the 32 per-column values
-// (dK/dV kernel: loaded from shared memory before the scores, see
-// bwd_load_vec32) or one value (dQ kernel: nl == nullptr).
+// (MASK) to 0 outside lo <= i < hi.  nl holds 32 per-column values or, with
+// nl_col == nullptr, one value for the row.
 template <bool MASK>
 __device__ __forceinline__ void bwd_exp32(float* p, const uint32_t (&sv)[32], float sl,
                                           const float4* nl_col, float nl_row, int lo, int hi) {
@@ -220,29 +249,23 @@ __device__ __forceinline__ void bwd_exp32(float* p, const uint32_t (&sv)[32], fl
   }
 }
 
-// 32 per-column values from shared memory into registers, all loads issued
-// together: while the tensor pipe streams its operands from shared memory, a
-// load can wait hundreds of cycles, so they are started before the TMEM load
-// of the same columns rather than one by one inside the arithmetic.
-__device__ __forceinline__ void bwd_load_vec32(float4 (&v)[8], const float4* src) {
-#pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] = src[k];
-}
-
-// g = P * (dP + nd), 32 values packed to f16/bf16 pairs; nd per column
-// (nd_col) or one value (nd_col == nullptr).
-template <bool BF16>
+// g = P * (dP + nd) (ADD) or P * dP, 32 values packed to f16/bf16 pairs; nd
+// per column (nd_col) or one value (nd_col == nullptr).
+template <bool BF16, bool ADD>
 __device__ __forceinline__ void bwd_ds32(uint32_t (&gk)[16], const float* p,
                                          const uint32_t (&dv)[32], const float4* nd_col,
                                          float nd_row) {
 #pragma unroll
   for (int i = 0; i < 32; i += 4) {
-    float4 nd;
-    if (nd_col != nullptr) nd = nd_col[i / 4];
-    else nd = make_float4(nd_row, nd_row, nd_row, nd_row);
-    float a0, a1, a2, a3;
-    ptx::fadd2(a0, a1, __uint_as_float(dv[i]), __uint_as_float(dv[i + 1]), nd.x, nd.y);
-    ptx::fadd2(a2, a3, __uint_as_float(dv[i + 2]), __uint_as_float(dv[i + 3]), nd.z, nd.w);
+    float a0 = __uint_as_float(dv[i]), a1 = __uint_as_float(dv[i + 1]);
+    float a2 = __uint_as_float(dv[i + 2]), a3 = __uint_as_float(dv[i + 3]);
+    if (ADD) {
+      float4 nd;
+      if (nd_col != nullptr) nd = nd_col[i / 4];
+      else nd = make_float4(nd_row, nd_row, nd_row, nd_row);
+      ptx::fadd2(a0, a1, a0, a1, nd.x, nd.y);
+      ptx::fadd2(a2, a3, a2, a3, nd.z, nd.w);
+    }
     ptx::fmul2(a0, a1, a0, a1, p[i], p[i + 1]);
     ptx::fmul2(a2, a3, a2, a3, p[i + 2], p[i + 3]);
     gk[i / 2] = pack2<BF16>(a0, a1);
@@ -276,6 +299,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
   auto step_head = [&](int s) { return b * p.Hq + hk * p.group + s / n_q; };  // b*Hq + h
   auto step_tile = [&](int s) { return i0 + s % n_q; };
 
+  // A operand of the accumulator pre-load: ones in k = 0..2 of every row
+  // (f16 1.0 = 0x3C00, bf16 1.0 = 0x3F80), same core-matrix layout as the
+  // vector tiles; made visible to the tensor core's (async proxy) reads.
+  if (threadIdx.x < 256) {
+    const uint32_t one = BF16 ? 0x3F80u : 0x3C00u;
+    const int row = threadIdx.x >> 1, half = threadIdx.x & 1;
+    uint4* dst = reinterpret_cast<uint4*>(smem + L::kOffOnes + (row >> 3) * 256 + (row & 7) * 16 +
+                                          half * 128);
+    *dst = half ? make_uint4(0u, 0u, 0u, 0u) : make_uint4(one | (one << 16), one, 0u, 0u);
+  }
+  ptx::fence_proxy_async_smem();
+  __syncthreads();
+
   if (warp == kBwdWarpLoad) {
     if (lane == 0) {
       const uint64_t pol = ptx::policy_evict_last();
@@ -298,7 +334,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
         const int bhq = step_head(s);
         const int qt = step_tile(s);
         const void* map = (i & 1) ? static_cast<const void*>(&p.tm_do) : static_cast<const void*>(&p.tm_q);
-        const float* vec = ((i & 1) ? p.dd : p.l2) + static_cast<size_t>(bhq) * p.n_pad + qt * 128;
+        const uint8_t* vec = p.vt + ((static_cast<size_t>(bhq) * p.n_tiles + qt) * 2 + (i & 1)) * L::kVec;
         ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile + L::kVec);
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
@@ -332,14 +368,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     const uint64_t v_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);              // K-major
     const uint64_t ring_mn = ptx::smem_desc_sw128(sbase + L::kOffRing, L::kBlockBytes, 1024);  // MN-major
-    // D = A B^T with A the fixed K (V) tile and B ring item `item` (Q or dO), K = d
+    const uint64_t ones_desc = ptx::smem_desc_noswz(sbase + L::kOffOnes, 128, 256);
+    // D = ones x vec^T + A B^T with A the fixed K (V) tile, B ring item `item`
+    // (Q or dO, K = d) and vec the item's vector tile: the first product puts
+    // -LSE/scale (-D) of each query column into every row of the accumulator
     auto issue_score = [&](uint32_t d_col, uint64_t a_desc, int item, uint32_t done_bar) {
       const uint64_t b_off = static_cast<uint64_t>((slot_of(item) * L::kTile) >> 4);
+      const uint64_t vec_desc =
+          ptx::smem_desc_noswz(sbase + L::kOffVec + slot_of(item) * L::kVec, 128, 256);
       if (ptx::elect_one()) {
+        ptx::mma_ss(tmem + d_col, ones_desc, vec_desc, idesc_s, 0u);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + d_col, a_desc + off, ring_k + b_off + off, idesc_s, kk > 0 ? 1u : 0u);
+          ptx::mma_ss(tmem + d_col, a_desc + off, ring_k + b_off + off, idesc_s, 1u);
         }
         ptx::mma_commit(done_bar);
       }
@@ -414,8 +456,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     bool ok = true;
     for (int s = 0; ok && s < n_steps; ++s) {
       const int qt = step_tile(s);
-      const float4* l2v = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s) % L::kSlots) * L::kVec) + 16 * g;
-      const float4* ddv = reinterpret_cast<const float4*>(smem + L::kOffVec + ((2 * s + 1) % L::kSlots) * L::kVec) + 16 * g;
       const bool diag = p.causal && qt == t;  // query < key is masked
       if (threadIdx.x == 0) FA_TRACE_AT(s, 8);
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), s & 1, wc, 47));
@@ -425,18 +465,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       float pr[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        float4 nl[8];
-        bwd_load_vec32(nl, l2v + 8 * c);
         uint32_t sv[32];
         ptx::tmem_ld32(tmem + lane_off + L::tS + col0 + 32 * c, sv);
         ptx::tmem_wait_ld();
         pin_after_wait<32>(sv);
         if (threadIdx.x == 0) FA_TRACE_AT(s, c ? 15 : 13);
-        // diagonal tile: query q = col0 + 32c + i is kept when q >= key r
+        // S^T already holds s - LSE/scale.  Diagonal tile: query
+        // q = col0 + 32c + i is kept when q >= key r
         if (diag)
-          bwd_exp32<true>(pr + 32 * c, sv, sl, nl, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
+          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
         else
-          bwd_exp32<false>(pr + 32 * c, sv, sl, nl, 0.f, 0, 32);
+          bwd_exp32<false>(pr + 32 * c, sv, sl, nullptr, 0.f, 0, 32);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(pr[32 * c + 2 * i], pr[32 * c + 2 * i + 1]);
@@ -455,14 +494,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       ptx::tc_fence_after();
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        float4 nd[8];
-        bwd_load_vec32(nd, ddv + 8 * c);
         uint32_t dv[32];
         ptx::tmem_ld32(tmem + lane_off + L::tDP + col0 + 32 * c, dv);
         ptx::tmem_wait_ld();
         pin_after_wait<32>(dv);
         uint32_t gk[16];
-        bwd_ds32<BF16>(gk, pr + 32 * c, dv, nd, 0.f);
+        bwd_ds32<BF16, false>(gk, pr + 32 * c, dv, nullptr, 0.f);  // dP^T already holds dP - D
         // dS^T into the group's dP columns col0 + 16c.. (already read)
         ptx::tmem_st16(tmem + lane_off + L::tDP + col0 + 16 * c, gk);
       }
@@ -658,7 +695,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
         ptx::tmem_wait_ld();
         pin_after_wait<32>(dv);
         uint32_t gk[16];
-        bwd_ds32<BF16>(gk, pr + 32 * c, dv, nullptr, ndv);
+        bwd_ds32<BF16, true>(gk, pr + 32 * c, dv, nullptr, ndv);
         ptx::tmem_st16(tmem + lane_off + L::tDS + 32 * g + 16 * c, gk);
       }
       ptx::tmem_wait_st();
@@ -697,7 +734,8 @@ static cudaError_t launch_bwd_impl(const BwdParams& p, const void* o, const void
   }
   const long long rows = static_cast<long long>(p.B) * p.Hq * p.n_pad;
   fa_bwd_prep_kernel<BF16><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
-      o, dout, lse, const_cast<float*>(p.l2), const_cast<float*>(p.dd), p.N, p.n_pad, rows, D);
+      o, dout, lse, const_cast<float*>(p.l2), const_cast<float*>(p.dd), const_cast<uint8_t*>(p.vt),
+      p.scale, p.N, p.n_pad, rows, D);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   fa_bwd_dkdv_kernel<D, BF16><<<p.B * p.Hkv * p.n_tiles, kBwdThreads, BwdLayout<D>::kDynBytes, stream>>>(p);

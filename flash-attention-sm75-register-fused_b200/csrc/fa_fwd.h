@@ -104,6 +104,12 @@ struct alignas(64) BwdParams {
   void* dv;          // [B, Hkv, N, d]
   const float* l2;
   const float* dd;
+  // Per (batch*Hq, query tile): two 4 KB K-major operand tiles (128 query rows
+  // x 16 f16/bf16, no swizzle, 8x16-byte core matrices 128 B apart along K and
+  // 256 B apart along rows): row n holds -LSE/scale, then -D, each as three
+  // 16-bit terms (k = 0..2) summing to the fp32 value.  Multiplied by a tile
+  // of ones, they pre-load the S^T and dP^T accumulators of the dK/dV kernel.
+  const uint8_t* vt;
   int B, Hq, Hkv, N, n_pad, group, n_tiles, causal;
   float scale, scale_log2;
   long long* trace;  // timeline samples, used only in FA_TRACE builds

@@ -354,6 +354,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// Descriptor of a K-major tile without swizzling: 8-row x 16-byte core
+// matrices, `lbo_bytes` apart along K and `sbo_bytes` apart along M/N
+// (layout field 0).
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t saddr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 //   bits 4-5 D format (1 = f32); 7-9 A format, 10-12 B format (0 f16, 1 bf16);
 //   bit 15 A major (0 = K-major); bit 16 B major (1 = MN-major);

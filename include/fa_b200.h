@@ -150,7 +150,8 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
            int head_dim, float scale, int causal, int dtype, void* workspace,
            size_t workspace_bytes, void* stream);
 
-/* Workspace bytes of fa_bwd: two fp32 values per query row (from LSE and rowsum(dO*O)), padded to 128 rows. */
+/* Workspace bytes of fa_bwd: two fp32 values per query row (from LSE and rowsum(dO*O)) and two
+ * 4 KB operand tiles per 128-row query tile, rows padded to 128. */
 size_t fa_bwd_workspace_bytes(int B, int Hq, int N);
 
 /* ---- reference-compatible launchers (void, fp16, blocking) ----

@@ -125,4 +125,4 @@ def test_backward_argument_errors(sm100):
                     abi.ptr(q), abi.ptr(k), abi.ptr(v), 1, 2, 2, 64, 64, 0.125, 0, 0, abi.ptr(ws),
                     16, abi.stream_ptr())
     assert rc == 1  # FA_ERR_INVALID_ARG: workspace too small
-    assert lib.fa_bwd_workspace_bytes(1, 2, 64) == 2 * 2 * 128 * 4
+    assert lib.fa_bwd_workspace_bytes(1, 2, 64) == 2 * 2 * 128 * 4 + 2 * 8192
