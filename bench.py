@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config c5] [--dtype f16|bf16] [--no-extras] [--kvcache-only NAME|all]
+                    [--varlen-only NAME|all] [--backward-only NAME|all]
 
 Metric: attention-forward TFLOPS, FLOPs = 4*B*H*N^2*d (halved
 for causal, the reference's convention), whole-job aggregate over N GPUs.
@@ -63,6 +64,9 @@ def parse_args():
     ap.add_argument("--kvcache-only", default=None, metavar="NAME|all",
                     help="time only fa_fwd_kvcache workloads (decode / chunked prefill) and print "
                          "their table as one JSON line (profiling runs)")
+    ap.add_argument("--varlen-only", default=None, metavar="NAME|all",
+                    help="time only fa_fwd_varlen / fa_fwd_padded workloads and print their table "
+                         "as one JSON line (profiling runs)")
     ap.add_argument("--backward-only", default=None, metavar="NAME|all",
                     help="time only fa_bwd workloads (attention backward) and print their table "
                          "as one JSON line (profiling runs)")
@@ -301,6 +305,13 @@ def main():
             print(json.dumps({"kvcache": kvcache_configs(abi.load(), abi, dtype, dev, names)}),
                   flush=True)
         return
+    if args.varlen_only:
+        if rank == 0:
+            dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+            names = None if args.varlen_only == "all" else [args.varlen_only]
+            print(json.dumps({"varlen": varlen_configs(abi.load(), abi, dtype, dev, names)}),
+                  flush=True)
+        return
     if args.backward_only:
         if rank == 0:
             dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
@@ -386,6 +397,7 @@ def main():
             line["configs"] = other_configs(lib, abi, dtype, dev)
             line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
             line["backward"] = backward_configs(lib, abi, dtype, dev)
+            line["varlen"] = varlen_configs(lib, abi, dtype, dev)
     elif rank == 0:
         line["e2e"] = None
     if world > 1:
@@ -495,6 +507,78 @@ def kvcache_configs(lib, abi, dtype, dev, names=None):
                      "hbm_frac": round(byt / (ms * 1e-3) / 1e9 / hbm, 3),
                      "tflops": round(flops / ms / 1e9, 1), "splits_workspace_bytes": int(nbytes)}
         del q, k, v, o, lse, ws
+    return out
+
+
+# fa_fwd_varlen / fa_fwd_padded workloads: a batch of sequences of mixed length
+# (seeded, 512..8192 tokens) in the packed layout and the same batch padded to
+# the longest sequence; name -> (n_seq, Hq, Hkv, d, causal)
+VARLEN_CONFIGS = {
+    "varlen_16seq_gqa4_causal": (16, 32, 8, 128, True),
+    "varlen_16seq_mha_full": (16, 16, 16, 128, False),
+}
+
+
+def varlen_configs(lib, abi, dtype, dev, names=None):
+    """Kernel-only time of fa_fwd_varlen (packed) and fa_fwd_padded (padded
+    layout, valid ranges) on the same sequences; TFLOPS counts the attended
+    (query, key) pairs of every sequence (4*d FLOPs each)."""
+    import torch
+    out = {}
+    for name, (n_seq, Hq, Hkv, d, causal) in VARLEN_CONFIGS.items():
+        if names is not None and name not in names:
+            continue
+        g = torch.Generator().manual_seed(5)
+        lens = [int(x) for x in torch.randint(512, 8193, (n_seq,), generator=g)]
+        total, nmax = sum(lens), max(lens)
+        cu = [0]
+        for n in lens:
+            cu.append(cu[-1] + n)
+        gd = torch.Generator(device=dev).manual_seed(6)
+        mk = lambda *shape: torch.randn(*shape, device=dev, generator=gd).to(dtype)
+        q, k, v = mk(total, Hq, d), mk(total, Hkv, d), mk(total, Hkv, d)
+        o = torch.empty_like(q)
+        cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+        s = torch.cuda.current_stream(dev)
+        scale = 1.0 / math.sqrt(d)
+        dt = 1 if dtype == torch.bfloat16 else 0
+        mode = 1 if causal else 0
+        pairs = sum(n * (n + 1) / 2 if causal else float(n) * n for n in lens)
+        flops = 4.0 * d * Hq * pairs
+        fn = lambda: lib.fa_fwd_varlen(abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), None,
+                                       abi.ptr(cu_t), abi.ptr(cu_t), n_seq, Hq, Hkv, total, total,
+                                       nmax, nmax, d, scale, mode, dt, abi.stream_ptr(s))
+        assert fn() == 0
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        n_it = 20
+        ms = time_steps(fn, n_it, s) / n_it
+        res = {"seqs": n_seq, "tokens": total, "max_len": nmax, "varlen_us": round(ms * 1e3, 1),
+               "varlen_tflops": round(flops / ms / 1e9, 1)}
+        # the same batch padded to the longest sequence
+        qp = torch.zeros(n_seq, Hq, nmax, d, device=dev, dtype=dtype)
+        kp = torch.zeros(n_seq, Hkv, nmax, d, device=dev, dtype=dtype)
+        vp = torch.zeros_like(kp)
+        for i, n in enumerate(lens):
+            qp[i, :, :n] = q[cu[i]:cu[i + 1]].transpose(0, 1)
+            kp[i, :, :n] = k[cu[i]:cu[i + 1]].transpose(0, 1)
+            vp[i, :, :n] = v[cu[i]:cu[i + 1]].transpose(0, 1)
+        op = torch.empty_like(qp)
+        zeros = torch.zeros(n_seq, dtype=torch.int32, device=dev)
+        ends = torch.tensor(lens, dtype=torch.int32, device=dev)
+        fp = lambda: lib.fa_fwd_padded(abi.ptr(qp), abi.ptr(kp), abi.ptr(vp), abi.ptr(op), None,
+                                       abi.ptr(zeros), abi.ptr(ends), abi.ptr(zeros), abi.ptr(ends),
+                                       n_seq, Hq, Hkv, nmax, nmax, d, scale, mode, dt,
+                                       abi.stream_ptr(s))
+        assert fp() == 0
+        for _ in range(3):
+            fp()
+        torch.cuda.synchronize()
+        ms_p = time_steps(fp, n_it, s) / n_it
+        res.update({"padded_us": round(ms_p * 1e3, 1), "padded_tflops": round(flops / ms_p / 1e9, 1)})
+        out[name] = res
+        del q, k, v, o, qp, kp, vp, op
     return out
 
 
