@@ -74,7 +74,8 @@ struct BwdLayout {
 // Per padded row r < n_pad of every (batch, query head): nl2_r = -LSE_r*log2(e)
 // and nd_r = -D_r = -sum_c dO[r][c] O[r][c] (negated so that the main kernels
 // form s*scale*log2(e) - LSE*log2(e) and dP - D with one packed FMA / add);
-// rows >= N get nl2 = -inf, nd = 0, so their P is 0.  One warp per row.
+// rows >= N get nl2 = -inf, nd = 0, so their P is 0.  d/8 lanes per row, each
+// reading 16 bytes of O and of dO (the kernel streams O and dO once).
 template <bool BF16>
 __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict__ o,
                                                           const void* __restrict__ dout,
@@ -84,30 +85,37 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
                                                           uint8_t* __restrict__ vt, float scale,
                                                           int N, int n_pad, long long n_rows,
                                                           int d) {
-  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= n_rows) return;
-  const int lane = threadIdx.x & 31;
-  const long long bh = row / n_pad;
-  const int r = static_cast<int>(row % n_pad);
+  const int lpr = d >> 3;  // lanes per row: 16 (d = 128) or 8 (d = 64)
+  const int rows_per_block = 256 / lpr;
+  const long long row = static_cast<long long>(blockIdx.x) * rows_per_block + threadIdx.x / lpr;
+  const int sub = threadIdx.x % lpr;
+  const bool live = row < n_rows;
+  const long long bh = live ? row / n_pad : 0;
+  const int r = live ? static_cast<int>(row % n_pad) : N;
   float acc = 0.f;
   if (r < N) {
-    const T* op = reinterpret_cast<const T*>(o) + (bh * N + r) * d;
-    const T* gp = reinterpret_cast<const T*>(dout) + (bh * N + r) * d;
-    for (int c = lane * 2; c < d; c += 64) {
-      float2 a, g;
+    const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(o) +
+                                                    ((bh * N + r) * d + sub * 8) * 2);
+    const uint4 g = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(dout) +
+                                                    ((bh * N + r) * d + sub * 8) * 2);
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 fa, fg;
       if constexpr (BF16) {
-        a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(op + c));
-        g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gp + c));
+        fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&av[i]));
+        fg = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gv[i]));
       } else {
-        a = __half22float2(*reinterpret_cast<const __half2*>(op + c));
-        g = __half22float2(*reinterpret_cast<const __half2*>(gp + c));
+        fa = __half22float2(*reinterpret_cast<const __half2*>(&av[i]));
+        fg = __half22float2(*reinterpret_cast<const __half2*>(&gv[i]));
       }
-      acc = fmaf(a.x, g.x, fmaf(a.y, g.y, acc));
+      acc = fmaf(fa.x, fg.x, fmaf(fa.y, fg.y, acc));
     }
   }
-#pragma unroll
-  for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+  // sum over the row's lanes (aligned groups of lpr lanes within the warp)
+  for (int m = lpr >> 1; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  if (!live) return;
+  const int lane = sub;
   if (lane == 0) {
     const float lse_r = (r < N) ? lse[bh * N + r] : 0.f;
     dd[row] = -acc;
@@ -733,7 +741,8 @@ static cudaError_t launch_bwd_impl(const BwdParams& p, const void* o, const void
     if (dev >= 0 && dev < 64) attr_done[dev] = 1;
   }
   const long long rows = static_cast<long long>(p.B) * p.Hq * p.n_pad;
-  fa_bwd_prep_kernel<BF16><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+  const long long rows_per_block = 256 / (D / 8);
+  fa_bwd_prep_kernel<BF16><<<static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block), 256, 0, stream>>>(
       o, dout, lse, const_cast<float*>(p.l2), const_cast<float*>(p.dd), const_cast<uint8_t*>(p.vt),
       p.scale, p.N, p.n_pad, rows, D);
   cudaError_t e = cudaGetLastError();

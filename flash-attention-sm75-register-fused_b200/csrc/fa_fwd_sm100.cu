@@ -186,6 +186,10 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 //   28-29 group 0 / 1 tile max computed (row 0)
 //   30-31 producer issued the loads of V_j / K_{j+1}
 //   (tile kTraceTiles-1, events 30 / 31: CTA set up / CTA done)
+// Dual (decode) launches index rows by each group's running tile count
+// (mod 64) and record: 2g MMA warp saw V_j, K_{j+1} of group g land; 4+g
+// P_g(j) seen and PV issued; 1+2g S_g(j+1) issued; 24+g / 26+g producer
+// issued K / V of the tile; 8-23, 28-29 as above.
 constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
 #ifdef FA_TRACE
 #define FA_TRACE_AT(tile, ev)                                                          \
@@ -470,6 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // have completed.  Shared mode uses both Q buffers for its two tiles and
       // is never launched with more than one item per CTA.
       int ring = 0, k = 0, q_loads[2] = {0, 0};
+#ifdef FA_TRACE
+      int pc[2] = {0, 0};  // dual mode: tiles of group g in earlier work items (trace rows)
+#endif
       bool ok = true;
       for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x, ++k) {
         WorkItem it;
@@ -518,6 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
                                     : static_cast<const void*>(&p.tm_k);
           if ((i & 1) && !dual) FA_TRACE_AT(i >> 1, 30);                // V_j issued
           if (!(i & 1) && !dual && i > 0) FA_TRACE_AT((i >> 1) - 1, 31);  // K_{j+1} issued
+#ifdef FA_TRACE
+          if (dual) FA_TRACE_AT((pc[g] + tile - (g ? it.jb[1] : it.jb[0])) & 63, (i & 1) ? 26 + g : 24 + g);
+#endif
           ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
           const int row = it.ky + tile * kBlockN;
 #pragma unroll
@@ -530,6 +540,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
                                row, it.kz, pol_kv);
           }
         }
+#ifdef FA_TRACE
+        pc[0] += it.n_kv[0];
+        pc[1] += it.n_kv[1];
+#endif
       }
       // Drain: every copy this thread started must land before the CTA exits.
       for (int r = max(0, ring - L::kSlots); r < ring; ++r)
@@ -701,11 +715,12 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               const int ki = next ? ring + k_item_of(it, true, g, j + 1) : 0;
               if (!(ok = wait(bar(L::kBarFull + slot_of(vi)), phase_of(vi), 12))) break;
               if (next && !(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 14))) break;
-              if (lane == 0) FA_TRACE_AT(j, 2 * g);
+              if (lane == 0) FA_TRACE_AT((cnt[g] + j) & 63, 2 * g);  // V_j and K_{j+1} landed
               if (!(ok = issue_pv(g, vi, j == 0, (cnt[g] + j) & 1))) break;
+              if (lane == 0) FA_TRACE_AT((cnt[g] + j) & 63, 4 + g);  // P(j) seen, PV issued
               commit(bar(L::kBarEmpty + slot_of(vi)));
               if (next) {
-                if (lane == 0) FA_TRACE_AT(j, 1 + 2 * g);
+                if (lane == 0) FA_TRACE_AT((cnt[g] + j) & 63, 1 + 2 * g);
                 issue_s(g, ki, qd);
                 commit(bar(L::kBarEmpty + slot_of(ki)));
               }
@@ -789,7 +804,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     for (int j = 0; ok && j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + g), (cnt + j) & 1, wc, 20 + g));
       if (!ok) break;
-      if (lane == 0) FA_TRACE_AT(j, 16 + sw);
+      if (lane == 0) FA_TRACE_AT(dual ? ((cnt + j) & 63) : j, 16 + sw);
       ptx::tc_fence_after();
 
       float x[kBlockN];
@@ -835,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         m_tile = row_extreme<kBlockN, true>(x) * sl;
       }
 
-      if (r == 0) FA_TRACE_AT(j, 28 + g);
+      if (r == 0) FA_TRACE_AT(dual ? ((cnt + j) & 63) : j, 28 + g);
       const float m_new = fmaxf(m, m_tile);
       const bool grow = m_new > m + kRescaleThreshold;
       if (j == 0) {
@@ -873,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
                                     : exp_tile<BF16, true>(x, sl_eff, neg_m, tP, bar(L::kBarPH + g));
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      if (lane == 0) FA_TRACE_AT(j, 8 + sw);
+      if (lane == 0) FA_TRACE_AT(dual ? ((cnt + j) & 63) : j, 8 + sw);
       ptx::mbar_arrive(bar(L::kBarP + g));
       l += tile_sum;
     }
