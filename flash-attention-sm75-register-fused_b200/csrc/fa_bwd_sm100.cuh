@@ -21,7 +21,8 @@
 //
 // Development builds (-DFA_TRACE) record clock64 timelines of the first
 // CTAs into BwdParams::trace (dK/dV kernel: per step s, MMA warp events 1-5,
-// elementwise warp 0 events 8-15, 17-18, producer event 16).
+// elementwise warp 0 events 8-15, 17-18, producer event 16; dQ kernel: per
+// K/V tile j, MMA warp events 19-23, elementwise warp 0 events 24-28).
 //
 // Warps (384 threads): 0-7 elementwise in two groups g (warps 4g..4g+3, one
 // TMEM lane = one row per thread, columns [64g, 64g+64) of the 128), 8 TMA
@@ -61,13 +62,16 @@ struct BwdLayout {
   // written.  dQ kernel: kBarP = S read, kBarP + 1 = dS written.
   static constexpr int kBarP = kBarS + 2;
   static constexpr int kBarG = kBarP + 2;            // all gradient MMAs completed
-  static constexpr int kNumBars = kBarG + 1;
+  static constexpr int kBarQT = kBarG + 1;           // dQ kernel: Q copied into TMEM (128 arrivals)
+  static constexpr int kNumBars = kBarQT + 1;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynBytes = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t tS = 0, tDP = 128, tAcc0 = 256, tAcc1 = 256 + D;
-  static constexpr uint32_t tDS = 256 + D;  // dQ kernel: packed dS (64 columns)
+  static constexpr uint32_t tDS = 256 + D;       // dQ kernel: packed dS (64 columns)
+  static constexpr uint32_t tQ = 256 + D + 64;   // dQ kernel: Q as the A operand (d/2 columns)
+  static_assert(tQ + D / 2 <= kTmemCols, "tensor memory budget");
   static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -169,7 +173,9 @@ __device__ __forceinline__ bool bwd_setup(uint8_t* smem_raw, uint8_t*& smem, uin
     *abort_flag = ((st >> 32) == epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
     for (int i = 0; i < L::kNumBars; ++i)
       ptx::mbar_init(sbase + L::kOffBar + 8u * i,
-                     (i == L::kBarP || i == L::kBarP + 1) ? static_cast<uint32_t>(kBwdElemThreads) : 1u);
+                     (i == L::kBarP || i == L::kBarP + 1) ? static_cast<uint32_t>(kBwdElemThreads)
+                     : i == L::kBarQT                     ? 128u
+                                                          : 1u);
     ptx::fence_barrier_init();
   }
   __syncthreads();
@@ -600,43 +606,52 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     auto wait = [&](uint32_t bb, uint32_t ph, int site) {
       return __all_sync(0xffffffffu, bar_wait(bb, ph, wc, site));
     };
-    const uint64_t q_desc = ptx::smem_desc_sw128(sbase + L::kOffFix, 16, 1024);
     const uint64_t do_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);
     const uint64_t ring_mn = ptx::smem_desc_sw128(sbase + L::kOffRing, L::kBlockBytes, 1024);
-    // D = A B^T with A the fixed Q (dO) tile and B ring item `item` (K or V), K = d
-    auto issue_score = [&](uint32_t d_col, uint64_t a_desc, int item, uint32_t done_bar) {
+    // D = A B^T with B ring item `item` (K or V), K = d, and A the fixed tile:
+    // Q from TMEM (copied there by the elementwise warps; halves the product's
+    // shared-memory reads) or dO from shared memory
+    auto issue_score = [&](uint32_t d_col, bool a_in_tmem, int item, uint32_t done_bar) {
       const uint64_t b_off = static_cast<uint64_t>((slot_of(item) * L::kTile) >> 4);
       if (ptx::elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-          ptx::mma_ss(tmem + d_col, a_desc + off, ring_k + b_off + off, idesc_s, kk > 0 ? 1u : 0u);
+          if (a_in_tmem)
+            ptx::mma_ts(tmem + d_col, tmem + L::tQ + 8 * kk, ring_k + b_off + off, idesc_s,
+                        kk > 0 ? 1u : 0u);
+          else
+            ptx::mma_ss(tmem + d_col, do_desc + off, ring_k + b_off + off, idesc_s, kk > 0 ? 1u : 0u);
         }
         ptx::mma_commit(done_bar);
       }
       __syncwarp();
     };
-    bool ok = wait(bar(L::kBarFix), 0, 53);
+    bool ok = wait(bar(L::kBarFix), 0, 53) && wait(bar(L::kBarQT), 0, 53);
     if (ok && n_kv > 0) {
       ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 54);
       if (ok) {
         ptx::tc_fence_after();
-        issue_score(L::tS, q_desc, 0, bar(L::kBarS));
+        issue_score(L::tS, true, 0, bar(L::kBarS));
         ok = wait(bar(L::kBarFull + slot_of(1)), phase_of(1), 54);
       }
-      if (ok) issue_score(L::tDP, do_desc, 1, bar(L::kBarS + 1));
+      if (ok) issue_score(L::tDP, false, 1, bar(L::kBarS + 1));
     }
     for (int j = 0; ok && j < n_kv; ++j) {
       const bool next = j + 1 < n_kv;
       const int ik = 2 * j, iv = 2 * j + 1;
+      if (lane == 0) FA_TRACE_AT(j, 19);
       if (!(ok = wait(bar(L::kBarP), j & 1, 55))) break;
+      if (lane == 0) FA_TRACE_AT(j, 20);
       if (next) {
         if (!(ok = wait(bar(L::kBarFull + slot_of(ik + 2)), phase_of(ik + 2), 54))) break;
         ptx::tc_fence_after();
-        issue_score(L::tS, q_desc, ik + 2, bar(L::kBarS));  // S(j+1)
+        issue_score(L::tS, true, ik + 2, bar(L::kBarS));  // S(j+1)
       }
+      if (lane == 0) FA_TRACE_AT(j, 21);
       if (!(ok = wait(bar(L::kBarP + 1), j & 1, 55))) break;
+      if (lane == 0) FA_TRACE_AT(j, 22);
       ptx::tc_fence_after();
       // dQ += dS K_j (A = dS from TMEM, B = K_j MN-major: K = keys)
       const uint64_t k_off = static_cast<uint64_t>((slot_of(ik) * L::kTile) >> 4);
@@ -652,8 +667,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       __syncwarp();
       if (next) {
         if (!(ok = wait(bar(L::kBarFull + slot_of(iv + 2)), phase_of(iv + 2), 54))) break;
-        issue_score(L::tDP, do_desc, iv + 2, bar(L::kBarS + 1));  // dP(j+1)
+        issue_score(L::tDP, false, iv + 2, bar(L::kBarS + 1));  // dP(j+1)
       }
+      if (lane == 0) FA_TRACE_AT(j, 23);
     }
     if (ptx::elect_one()) ptx::mma_commit(bar(L::kBarG));
     __syncwarp();
@@ -670,15 +686,42 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     const float nlv = p.l2[static_cast<size_t>(bh) * p.n_pad + q_row];  // -LSE*log2(e)
     const float ndv = p.dd[static_cast<size_t>(bh) * p.n_pad + q_row];  // -D
     bool ok = true;
+    if (g == 0) {
+      // row r of the Q tile (TMA 128-byte swizzle: 16-byte chunk c of a row
+      // at position c ^ (r % 8)) into TMEM lane r, element pairs packed per
+      // column: the A operand layout of the TS product S = Q K^T
+      ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarFix), 0, wc, 59));
+      if (ok) {
+#pragma unroll
+        for (int blk = 0; blk < L::kColBlocks; ++blk) {
+          uint32_t w[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(
+                smem + L::kOffFix + blk * L::kBlockBytes + r * 128 + ((c ^ (r & 7)) * 16));
+            w[4 * c] = v.x;
+            w[4 * c + 1] = v.y;
+            w[4 * c + 2] = v.z;
+            w[4 * c + 3] = v.w;
+          }
+          ptx::tmem_st32(tmem + lane_off + L::tQ + 32 * blk, w);
+        }
+        ptx::tmem_wait_st();
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(L::kBarQT));
+    }
     for (int j = 0; ok && j < n_kv; ++j) {
       // keys >= N and (causal) keys > this query get P = 0
       int lim = p.N - j * 128 - col0;
       if (p.causal && j == t) lim = min(lim, r + 1 - col0);
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), j & 1, wc, 57));
       if (!ok) break;
+      if (threadIdx.x == 0) FA_TRACE_AT(j, 25);
       ptx::tc_fence_after();
       // keys of the group past N or (causal) past this query: masked tiles only
       const bool masked = (p.causal && j == t) || p.N - j * 128 - col0 < 64;
+      if (threadIdx.x == 0) FA_TRACE_AT(j, 24);
       float pr[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -693,8 +736,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(L::kBarP));  // S(j) read: S(j+1) may overwrite it
+      if (threadIdx.x == 0) FA_TRACE_AT(j, 26);
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + 1), j & 1, wc, 57));
       if (!ok) break;
+      if (threadIdx.x == 0) FA_TRACE_AT(j, 27);
       ptx::tc_fence_after();
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -709,6 +754,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(L::kBarP + 1));  // dS(j) written
+      if (threadIdx.x == 0) FA_TRACE_AT(j, 28);
     }
     if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarG), 0, wc, 58));
     if (ok && g == 0) {

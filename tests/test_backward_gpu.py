@@ -76,6 +76,20 @@ def test_backward_bf16(sm100):
         _check(got, ref, torch.bfloat16)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_backward_large_logits(sm100, d):
+    """Scores of several tens (LSE/scale in the hundreds) and a few keys x8, as
+    in the C5 inputs: the per-query LSE and D values the dK/dV kernel adds to
+    its accumulators keep their precision."""
+    q, k, v, do = _inputs(1, 4, 2, 300, d, seed=d)
+    q, k = q * 3, k * 3
+    k[:, :, ::37] *= 8
+    dq, dk, dv = _run_bwd(q, k, v, do, True)
+    rq, rk, rv = orc.attention_grads_fp32(q, k, v, do, causal=True)
+    for got, ref in ((dq, rq), (dk, rk), (dv, rv)):
+        _check(got, ref, torch.float16)
+
+
 def test_autograd_path(sm100):
     """flash_attention(...).backward() gives the C-ABI gradients; the
     reference-compatible flash_attention_forward still refuses backward."""
