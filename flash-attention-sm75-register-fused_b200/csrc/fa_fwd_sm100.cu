@@ -92,8 +92,8 @@ struct Layout {
   // persistent launches (several work items per CTA): the MMAs that read Q
   // buffer b for one item have completed, so the next Q may overwrite it
   static constexpr int kBarQFree = kBarDrain + 1;       // 2
-  // first half of P_g (keys 0-63) written: the PV MMA starts on it while the
-  // softmax computes the second half (128 arrivals)
+  // early part of P_g written (kPEarlyQuarters x 32 keys): the PV MMA starts
+  // on it while the softmax computes the rest (128 arrivals)
   static constexpr int kBarPH = kBarQFree + 2;          // 2
   static constexpr int kNumBars = kBarPH + 2;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
@@ -245,20 +245,29 @@ __device__ __forceinline__ float row_extreme(const float (&x)[N]) {
   return op3(a, b, kMin ? fminf(c, d) : fmaxf(c, d));
 }
 
+// The first kPEarlyQuarters quarters of P (32 keys each) are announced to the
+// MMA warp before the rest is computed, so the PV steps on them overlap the
+// softmax's tail.
+#ifndef FA_P_EARLY_QUARTERS
+#define FA_P_EARLY_QUARTERS 2
+#endif
+constexpr int kPEarlyQuarters = FA_P_EARLY_QUARTERS;
+static_assert(kPEarlyQuarters >= 1 && kPEarlyQuarters <= 3, "early part of P: 1-3 quarters");
+
 // exp2(x * sl - m) for the 128 scores of this thread's row; the packed
-// f16/bf16 values go to TMEM (P operand of the PV MMA) in two 32-column halves,
-// the first announced on `half_bar` as soon as it is written; returns their
-// fp32 sum.
+// f16/bf16 values go to TMEM (P operand of the PV MMA) in four 16-column
+// quarters, the first kPEarlyQuarters announced on `half_bar` as soon as they
+// are written; returns their fp32 sum.
 template <bool BF16, bool kEmulate>
 __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, float neg_m,
                                           uint32_t tP, uint32_t half_bar) {
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t pk[32];
+  for (int h = 0; h < 4; ++h) {
+    uint32_t pk[16];
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const int i = 64 * h + 2 * c;
+    for (int c = 0; c < 16; ++c) {
+      const int i = 32 * h + 2 * c;
       float t0, t1, e0, e1;
       ptx::ffma2(t0, t1, x[i], x[i + 1], sl, sl, neg_m, neg_m);
       if (kEmulate && (c % kEmuPeriod) >= kEmuPeriod - kEmuCount) {
@@ -273,8 +282,8 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
         ptx::fadd2(a0, a1, a0, a1, e0, e1);
       pk[c] = pack2<BF16>(e0, e1);
     }
-    ptx::tmem_st32(tP + 32 * h, pk);
-    if (h == 0) {
+    ptx::tmem_st16(tP + 16 * h, pk);
+    if (h == kPEarlyQuarters - 1) {
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(half_bar);
@@ -589,15 +598,16 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
       };
       // O_g (+)= P_g V with V in ring item `vi`; `first` starts the accumulator.
-      // Keys 0-63 (P columns 0-31) go out once the softmax has announced the
-      // first half of P (parity ph), keys 64-127 after the whole P.
+      // The PV steps on the announced early part of P (2 K-steps per quarter)
+      // go out once the softmax has announced it (parity ph), the rest after
+      // the whole P.
       auto issue_pv = [&](int g, int vi, bool first, uint32_t ph) -> bool {
         const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(vi) * L::kTile) >> 4);
         if (!wait(bar(L::kBarPH + g), ph, 13 + 3 * g)) return false;
         ptx::tc_fence_after();
         if (ptx::elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < kBlockN / 32; ++kk)
+          for (int kk = 0; kk < 2 * kPEarlyQuarters; ++kk)
             ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
                         vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
                         (!first || kk > 0) ? 1u : 0u);
@@ -607,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         ptx::tc_fence_after();
         if (ptx::elect_one()) {
 #pragma unroll
-          for (int kk = kBlockN / 32; kk < kBlockN / 16; ++kk)
+          for (int kk = 2 * kPEarlyQuarters; kk < kBlockN / 16; ++kk)
             ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
                         vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv, 1u);
           ptx::mma_commit(bar(L::kBarO + g));
