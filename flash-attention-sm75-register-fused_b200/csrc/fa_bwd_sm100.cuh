@@ -9,13 +9,17 @@
 // autograd Function raises (src/flash_attention_sm75/ops.py:47-52).
 //
 // Three kernels:
-//   fa_bwd_prep_kernel  D and LSE*log2(e) per query row, padded to whole tiles
+//   fa_bwd_prep_kernel  per query row -LSE*log2(e) and -D (padded to whole
+//                       tiles), and per 128-row query tile two K-major operand
+//                       tiles holding -LSE/scale and -D as 16-bit terms
 //   fa_bwd_dkdv_kernel  one CTA per (batch, KV head, 128-key tile): loops over
-//                       the group's query heads and query tiles, S^T = K Q^T and
-//                       dP^T = V dO^T on tcgen05, P^T and dS^T in registers,
-//                       dV += P^T dO and dK += dS^T Q accumulated in TMEM
-//   fa_bwd_dq_kernel    one CTA per (batch, query head, 128-query tile):
-//                       S = Q K^T, dP = dO V^T, dS, dQ += dS K in TMEM
+//                       the group's query heads and query tiles; issue order
+//                       dV += P^T(s) dO(s), S^T(s+1), dK += dS^T(s) Q(s),
+//                       dP^T(s+1), the score products starting from a
+//                       ones x vector product that pre-loads -LSE/scale (-D)
+//   fa_bwd_dq_kernel    one CTA per (batch, query head, 128-query tile), Q in
+//                       TMEM: S(j+1) = Q K^T as soon as S(j) is read, then
+//                       dQ += dS(j) K_j and dP(j+1)
 // S and dP are recomputed by both main kernels, so no atomics are needed (GQA
 // groups accumulate dK / dV inside one CTA).
 //
@@ -30,7 +34,8 @@
 // TMEM (512 columns), dK/dV kernel: S^T 0..127, dP^T 128..255, dV and dK
 // accumulators at 256 and 256+d; group g packs its P^T / dS^T (f16 pairs)
 // into the first 32 of its own 64 S / dP columns.  dQ kernel: S, dP, the dQ
-// accumulator at 256 and packed dS at 256+d (group g: columns 32g..).
+// accumulator at 256, packed dS at 256+d (group g: columns 32g..) and Q (the
+// A operand of S) at 320+d.
 
 namespace fa {
 namespace {
