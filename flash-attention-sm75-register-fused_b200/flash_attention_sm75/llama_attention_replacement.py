@@ -27,11 +27,16 @@ masks, holes) keeps the reference's ``has_attn_mask`` fallback, as does
 ``apply_patch(masks=False)``.  Query rows whose mask row is empty (padding
 queries) come back as zeros, as from SDPA's CPU path; SDPA's CUDA kernels
 leave implementation-defined values there, which callers discard.
+
+Training: when autograd needs gradients of the inputs, unmasked square calls
+go to ``flash_attention`` (forward and backward kernels; the reference's
+patch raised in backward), and masked or Nq != Nk calls fall back to SDPA with
+reason ``requires_grad`` (those kernels have no backward).
 """
 import torch
 import torch.nn.functional as F
 
-from .ops import (flash_attention_forward, flash_attention_forward_kvcache,
+from .ops import (flash_attention, flash_attention_forward, flash_attention_forward_kvcache,
                   flash_attention_forward_padded)
 
 _original_sdpa = F.scaled_dot_product_attention
@@ -44,6 +49,7 @@ _stats = {
     "flash": 0,
     "flash_kvcache": 0,
     "flash_masked": 0,
+    "flash_autograd": 0,
     "fallback": 0,
     "fallback_reasons": {},
 }
@@ -151,7 +157,13 @@ def _ineligible_reason(query, key, value, dropout_p, attn_mask, is_causal=False)
             attn_mask.device == query.device and
             _padded_for(attn_mask, query.size(0), query.size(2), key.size(2)) is not None):
         return "has_attn_mask"
+    if _needs_grad(query, key, value) and (attn_mask is not None or query.size(2) != key.size(2)):
+        return "requires_grad"  # the padded and KV-cache kernels have no backward
     return None
+
+
+def _needs_grad(*ts):
+    return torch.is_grad_enabled() and any(getattr(t, "requires_grad", False) for t in ts)
 
 
 def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None,
@@ -173,6 +185,9 @@ def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=Fa
         _stats["flash_kvcache"] += 1
         return flash_attention_forward_kvcache(query, key, value, causal=is_causal, scale=scale,
                                                causal_alignment="top_left")
+    if _needs_grad(query, key, value):
+        _stats["flash_autograd"] += 1  # training: forward + backward kernels
+        return flash_attention(query, key, value, causal=is_causal, scale=scale)
     return flash_attention_forward(query, key, value, causal=is_causal, scale=scale)
 
 
@@ -209,6 +224,7 @@ def reset_stats():
     _stats["flash"] = 0
     _stats["flash_kvcache"] = 0
     _stats["flash_masked"] = 0
+    _stats["flash_autograd"] = 0
     _stats["fallback"] = 0
     _stats["fallback_reasons"].clear()
 

@@ -5,7 +5,8 @@ llama_attention_replacement example runs it with a downloaded model.
 A left-padded batch exercises the padded-mask route, a prompt without padding
 the plain causal route, and one KV-cache decode step the Nq != Nk route; the
 logits must match the unpatched model's on every real (non-padding) token
-within fp16 tolerance.
+within fp16 tolerance.  A training step checks the autograd route (loss and
+attention-weight gradients against the unpatched model).
 """
 import pytest
 import torch
@@ -81,3 +82,33 @@ def test_llama_decode_step(sm100):
     assert (pre - ref_pre).abs().max().item() < 5e-2
     assert (dec - ref_dec).abs().max().item() < 5e-2
     assert s["flash_kvcache"] >= 2 and s["fallback"] == 0, s
+
+
+def test_llama_training_step(sm100):
+    """A training step through the patch: the causal GQA attention calls run the
+    forward and backward kernels (the reference's patch raised in backward);
+    loss and gradients match the unpatched model's."""
+    model = _tiny_llama(seed=4)
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 512, (2, 160), generator=g).cuda()
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        loss = model(input_ids=ids, labels=ids).loss
+        loss.backward()
+        return loss.item(), {n: p.grad.float().clone() for n, p in model.named_parameters()
+                             if p.grad is not None and "self_attn" in n}
+
+    ref_loss, ref_g = step()
+    patch.reset_stats()
+    patch.apply_patch()
+    try:
+        loss, grads = step()
+    finally:
+        patch.remove_patch()
+    s = patch.patch_stats()
+    assert s["flash_autograd"] == 2 and s["fallback"] == 0, s
+    assert abs(loss - ref_loss) < 1e-2 * abs(ref_loss)
+    for n, gr in ref_g.items():
+        err = (grads[n] - gr).abs().max().item()
+        assert err <= 3e-2 * gr.abs().max().item() + 1e-5, (n, err, gr.abs().max().item())

@@ -89,3 +89,27 @@ def test_padded_mask_structure_cpu():
     bias = torch.randn(1, 1, N, N)
     assert patch.padded_structure(bias, 1, N, N) is None
     assert patch.padded_structure(torch.ones(1, 2, N, N, dtype=torch.bool), 1, N, N) is None
+
+
+def test_requires_grad_routing_cpu():
+    """Calls that need gradients: masked / Nq != Nk ones fall back with reason
+    requires_grad (checked on fake CUDA tensors; the routing of unmasked
+    square calls to the autograd kernels is tested on the GPU)."""
+    class Fake:
+        def __init__(self, shape=(1, 2, 8, 64), grad=True):
+            self.is_cuda, self.dtype, self._s = True, torch.float16, shape
+            self.shape = torch.Size(shape)
+            self.requires_grad = grad
+
+        def dim(self):
+            return len(self._s)
+
+        def size(self, i):
+            return self._s[i]
+
+    r = patch._ineligible_reason
+    q, kv = Fake((1, 2, 1, 64)), Fake((1, 2, 8, 64))
+    assert r(q, kv, kv, 0.0, None) == "requires_grad"
+    with torch.no_grad():
+        assert r(q, kv, kv, 0.0, None) is None
+    assert r(Fake(), Fake(), Fake(), 0.0, None) is None  # square, unmasked: autograd kernels
