@@ -431,10 +431,16 @@ size_t fa_bwd_workspace_bytes(int B, int Hq, int N) {
          static_cast<size_t>(B) * Hq * (n_pad / 128) * 8192;
 }
 
-int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
-           const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
-           int head_dim, float scale, int causal, int dtype, void* workspace,
-           size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// fa_bwd and fa_bwd_padded: ranges (q_lo, q_hi, k_lo, k_hi) all null or all set.
+int launch_backward(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                    const float* lse, void* dQ, void* dK, void* dV, const int* q_lo,
+                    const int* q_hi, const int* k_lo, const int* k_hi, int B, int Hq, int Hkv,
+                    int N, int head_dim, float scale, int causal, int dtype, void* workspace,
+                    size_t workspace_bytes, void* stream) {
   if (B < 0 || Hq < 0 || Hkv < 0 || N < 0) return FA_ERR_INVALID_ARG;
   if (head_dim != 64 && head_dim != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_DTYPE;
@@ -464,6 +470,10 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
   p.dq = dQ;
   p.dk = dK;
   p.dv = dV;
+  p.q_lo = q_lo;
+  p.q_hi = q_hi;
+  p.k_lo = k_lo;
+  p.k_hi = k_hi;
   p.n_tiles = static_cast<int>(n_tiles);
   p.n_pad = p.n_tiles * 128;
   p.l2 = static_cast<const float*>(workspace);
@@ -482,6 +492,31 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaError_t e = fa::launch_bwd(p, O, dO, lse, head_dim, bf16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+           const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
+           int head_dim, float scale, int causal, int dtype, void* workspace,
+           size_t workspace_bytes, void* stream) {
+  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, nullptr, nullptr, nullptr, nullptr, B,
+                         Hq, Hkv, N, head_dim, scale, causal, dtype, workspace, workspace_bytes,
+                         stream);
+}
+
+int fa_bwd_padded(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                  const float* lse, const int* q_start, const int* q_end, const int* k_start,
+                  const int* k_end, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
+                  int head_dim, float scale, int causal, int dtype, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (B > 0 && Hq > 0 && N > 0 && (!q_start || !q_end || !k_start || !k_end))
+    return FA_ERR_INVALID_ARG;
+  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, q_start, q_end, k_start, k_end, B, Hq,
+                         Hkv, N, head_dim, scale, causal, dtype, workspace, workspace_bytes,
+                         stream);
 }
 
 int fa_fwd_varlen(const void* Q, const void* K, const void* V, void* O, float* lse,

@@ -93,7 +93,9 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
                                                           float* __restrict__ dd,
                                                           uint8_t* __restrict__ vt, float scale,
                                                           int N, int n_pad, long long n_rows,
-                                                          int d) {
+                                                          int d, int heads,
+                                                          const int* __restrict__ q_lo,
+                                                          const int* __restrict__ q_hi) {
   const int lpr = d >> 3;  // lanes per row: 16 (d = 128) or 8 (d = 64)
   const int rows_per_block = 256 / lpr;
   const long long row = static_cast<long long>(blockIdx.x) * rows_per_block + threadIdx.x / lpr;
@@ -101,8 +103,17 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
   const bool live = row < n_rows;
   const long long bh = live ? row / n_pad : 0;
   const int r = live ? static_cast<int>(row % n_pad) : N;
+  // a row outside its batch entry's query range, or one that saw no key
+  // (LSE = -inf), is treated like a padded row: P = 0
+  bool valid = r < N;
+  if (valid && q_lo != nullptr) {
+    const int b = static_cast<int>(bh / heads);
+    valid = r >= __ldg(q_lo + b) && r < __ldg(q_hi + b);
+  }
+  const float lse_r = valid ? lse[bh * N + r] : 0.f;
+  if (valid && lse_r == -INFINITY) valid = false;
   float acc = 0.f;
-  if (r < N) {
+  if (valid) {
     const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(o) +
                                                     ((bh * N + r) * d + sub * 8) * 2);
     const uint4 g = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(dout) +
@@ -126,12 +137,11 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
   if (!live) return;
   const int lane = sub;
   if (lane == 0) {
-    const float lse_r = (r < N) ? lse[bh * N + r] : 0.f;
     dd[row] = -acc;
-    l2[row] = (r < N) ? -lse_r * 1.4426950408889634f : -INFINITY;
+    l2[row] = valid ? -lse_r * 1.4426950408889634f : -INFINITY;
     // operand tiles of the dK/dV kernel: -LSE/scale (a large negative value
     // for padded rows, whose P must vanish) and -D as three 16-bit terms
-    const float vals[2] = {(r < N) ? -lse_r / scale : -30000.f, -acc};
+    const float vals[2] = {valid ? -lse_r / scale : -30000.f, -acc};
     const int n = r & 127;
     uint8_t* tile = vt + (static_cast<size_t>(row >> 7) * 2) * 4096 + (n >> 3) * 256 + (n & 7) * 16;
 #pragma unroll
@@ -472,6 +482,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t col0 = 64u * g;
     const float sl = p.scale_log2;
+    // padded batch: a key outside its entry's valid range gets P^T = 0
+    const bool key_ok =
+        p.k_lo == nullptr || (key >= __ldg(p.k_lo + b) && key < __ldg(p.k_hi + b));
     bool ok = true;
     for (int s = 0; ok && s < n_steps; ++s) {
       const int qt = step_tile(s);
@@ -491,7 +504,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
         if (threadIdx.x == 0) FA_TRACE_AT(s, c ? 15 : 13);
         // S^T already holds s - LSE/scale.  Diagonal tile: query
         // q = col0 + 32c + i is kept when q >= key r
-        if (diag)
+        if (!key_ok)
+          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, 0.f, 32, 32);  // all masked
+        else if (diag)
           bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
         else
           bwd_exp32<false>(pr + 32 * c, sv, sl, nullptr, 0.f, 0, 32);
@@ -690,6 +705,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     const float sl = p.scale_log2;
     const float nlv = p.l2[static_cast<size_t>(bh) * p.n_pad + q_row];  // -LSE*log2(e)
     const float ndv = p.dd[static_cast<size_t>(bh) * p.n_pad + q_row];  // -D
+    const int k_begin = p.k_lo == nullptr ? 0 : __ldg(p.k_lo + b);
+    const int k_end = p.k_lo == nullptr ? p.N : __ldg(p.k_hi + b);
     bool ok = true;
     if (g == 0) {
       // row r of the Q tile (TMA 128-byte swizzle: 16-byte chunk c of a row
@@ -717,15 +734,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       ptx::mbar_arrive(bar(L::kBarQT));
     }
     for (int j = 0; ok && j < n_kv; ++j) {
-      // keys >= N and (causal) keys > this query get P = 0
-      int lim = p.N - j * 128 - col0;
+      // keys >= N, (causal) keys > this query and (padded batch) keys outside
+      // the entry's range get P = 0; [klo, lim) relative to the group's first key
+      const int key0 = j * 128 + col0;
+      int lim = p.N - key0;
       if (p.causal && j == t) lim = min(lim, r + 1 - col0);
+      int klo = 0;
+      if (p.k_lo != nullptr) {
+        klo = k_begin - key0;
+        lim = min(lim, k_end - key0);
+      }
       ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS), j & 1, wc, 57));
       if (!ok) break;
       if (threadIdx.x == 0) FA_TRACE_AT(j, 25);
       ptx::tc_fence_after();
-      // keys of the group past N or (causal) past this query: masked tiles only
-      const bool masked = (p.causal && j == t) || p.N - j * 128 - col0 < 64;
+      // masked tiles only: the group's keys reach N, the diagonal or a range end
+      const bool masked = (p.causal && j == t) || p.N - key0 < 64 || klo > 0 ||
+                          (p.k_lo != nullptr && k_end - key0 < 64);
       if (threadIdx.x == 0) FA_TRACE_AT(j, 24);
       float pr[64];
 #pragma unroll
@@ -735,7 +760,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
         ptx::tmem_wait_ld();
         pin_after_wait<32>(sv);
         if (masked)
-          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, nlv, 0, lim - 32 * c);
+          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, nlv, klo - 32 * c, lim - 32 * c);
         else
           bwd_exp32<false>(pr + 32 * c, sv, sl, nullptr, nlv, 0, 32);
       }
@@ -766,8 +791,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       ptx::tc_fence_after();
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       const size_t row = static_cast<size_t>(bh) * p.N + q_row;
-      bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc0, p.scale, reinterpret_cast<T*>(p.dq) + row * D,
-                             q_row < p.N);
+      // rows that take no part (padding, or no visible key: -LSE = -inf) get dQ = 0
+      bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc0, nlv == -INFINITY ? 0.f : p.scale,
+                             reinterpret_cast<T*>(p.dq) + row * D, q_row < p.N);
     }
   }
   bwd_teardown<L>(tmem, warp);
@@ -795,7 +821,7 @@ static cudaError_t launch_bwd_impl(const BwdParams& p, const void* o, const void
   const long long rows_per_block = 256 / (D / 8);
   fa_bwd_prep_kernel<BF16><<<static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block), 256, 0, stream>>>(
       o, dout, lse, const_cast<float*>(p.l2), const_cast<float*>(p.dd), const_cast<uint8_t*>(p.vt),
-      p.scale, p.N, p.n_pad, rows, D);
+      p.scale, p.N, p.n_pad, rows, D, p.Hq, p.q_lo, p.q_hi);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   fa_bwd_dkdv_kernel<D, BF16><<<p.B * p.Hkv * p.n_tiles, kBwdThreads, BwdLayout<D>::kDynBytes, stream>>>(p);

@@ -110,6 +110,14 @@ struct alignas(64) BwdParams {
   // 16-bit terms (k = 0..2) summing to the fp32 value.  Multiplied by a tile
   // of ones, they pre-load the S^T and dP^T accumulators of the dK/dV kernel.
   const uint8_t* vt;
+  // Padded batch (all non-null) or nullptr: batch entry b's valid query rows
+  // are [q_lo[b], q_hi[b]) and valid keys [k_lo[b], k_hi[b]) (int32 device
+  // arrays, clamped to [0, N]); outside them P = 0, so invalid keys get
+  // dK = dV = 0 and invalid query rows dQ = 0.
+  const int* q_lo;
+  const int* q_hi;
+  const int* k_lo;
+  const int* k_hi;
   int B, Hq, Hkv, N, n_pad, group, n_tiles, causal;
   float scale, scale_log2;
   long long* trace;  // timeline samples, used only in FA_TRACE builds

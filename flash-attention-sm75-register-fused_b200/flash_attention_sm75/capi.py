@@ -22,6 +22,9 @@ SIGNATURES = {
     "fa_bwd": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                        c_int, c_int, c_float, c_int, c_int, c_vp, ctypes.c_size_t, c_vp]),
     "fa_bwd_workspace_bytes": (ctypes.c_size_t, [c_int, c_int, c_int]),
+    "fa_bwd_padded": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                              c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int,
+                              c_vp, ctypes.c_size_t, c_vp]),
     "fa_fwd_varlen": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
                               c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_vp]),
     "fa_fwd_padded": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
@@ -165,3 +168,23 @@ def fa_fwd_padded(q, k, v, o, lse, q_start, q_end, k_start, k_end, causal=CAUSAL
     return load().fa_fwd_padded(ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), ptr(q_start),
                                 ptr(q_end), ptr(k_start), ptr(k_end), B, Hq, Hkv, Nq, Nk, d,
                                 float(scale), int(causal), dtype, stream_ptr(stream))
+
+
+def fa_bwd_padded(q, k, v, o, do, lse, q_start, q_end, k_start, k_end, dq, dk, dv, causal=False,
+                  scale=None, stream=None):
+    """Call fa_bwd_padded on torch CUDA tensors ([B, H, N, d]; lse [B, Hq, N]
+    fp32; row ranges int32 [B]); allocates the workspace.  Returns the status."""
+    import math
+    import torch
+    B, Hq, N, d = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    lib = load()
+    nbytes = lib.fa_bwd_workspace_bytes(B, Hq, N)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    return lib.fa_bwd_padded(ptr(q), ptr(k), ptr(v), ptr(o), ptr(do), ptr(lse), ptr(q_start),
+                             ptr(q_end), ptr(k_start), ptr(k_end), ptr(dq), ptr(dk), ptr(dv), B, Hq,
+                             Hkv, N, d, float(scale), int(bool(causal)), dtype, ptr(ws), nbytes,
+                             stream_ptr(stream))

@@ -28,16 +28,16 @@ masks, holes) keeps the reference's ``has_attn_mask`` fallback, as does
 queries) come back as zeros, as from SDPA's CPU path; SDPA's CUDA kernels
 leave implementation-defined values there, which callers discard.
 
-Training: when autograd needs gradients of the inputs, unmasked square calls
-go to ``flash_attention`` (forward and backward kernels; the reference's
-patch raised in backward), and masked or Nq != Nk calls fall back to SDPA with
-reason ``requires_grad`` (those kernels have no backward).
+Training: when autograd needs gradients of the inputs, square calls go to
+``flash_attention`` / ``flash_attention_padded`` (forward and backward kernels;
+the reference's patch raised in backward), and Nq != Nk calls fall back to
+SDPA with reason ``requires_grad`` (the KV-cache kernel has no backward).
 """
 import torch
 import torch.nn.functional as F
 
 from .ops import (flash_attention, flash_attention_forward, flash_attention_forward_kvcache,
-                  flash_attention_forward_padded)
+                  flash_attention_forward_padded, flash_attention_padded)
 
 _original_sdpa = F.scaled_dot_product_attention
 _patch_active = False
@@ -157,8 +157,8 @@ def _ineligible_reason(query, key, value, dropout_p, attn_mask, is_causal=False)
             attn_mask.device == query.device and
             _padded_for(attn_mask, query.size(0), query.size(2), key.size(2)) is not None):
         return "has_attn_mask"
-    if _needs_grad(query, key, value) and (attn_mask is not None or query.size(2) != key.size(2)):
-        return "requires_grad"  # the padded and KV-cache kernels have no backward
+    if _needs_grad(query, key, value) and query.size(2) != key.size(2):
+        return "requires_grad"  # the KV-cache kernel has no backward
     return None
 
 
@@ -178,6 +178,10 @@ def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=Fa
     if attn_mask is not None:
         _stats["flash_masked"] += 1
         mode, qs, qe, ks, ke = _padded_for(attn_mask, query.size(0), query.size(2), key.size(2))
+        if _needs_grad(query, key, value):  # square here (Nq != Nk fell back above)
+            _stats["flash_autograd"] += 1
+            return flash_attention_padded(query, key, value, qs, qe, ks, ke, causal=mode != 0,
+                                          scale=scale)
         return flash_attention_forward_padded(
             query, key, value, qs, qe, ks, ke, causal=mode != 0, scale=scale,
             causal_alignment="top_left" if mode == 2 else "bottom_right")

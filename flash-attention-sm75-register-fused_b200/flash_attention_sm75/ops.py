@@ -240,6 +240,48 @@ def flash_attention_forward_padded(Q, K, V, q_start, q_end, k_start, k_end, caus
     return (out, lse) if return_lse else out
 
 
+class FlashAttentionPaddedFunction(torch.autograd.Function):
+    """Padded-batch attention with forward and backward (square N)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, q_start, q_end, k_start, k_end, causal, scale):
+        _check_gqa(Q.size(1), K.size(1))
+        Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+        out, lse = _C.flash_attention_forward_padded(Q, K, V, q_start, q_end, k_start, k_end,
+                                                     1 if causal else 0, float(scale))
+        ctx.save_for_backward(Q, K, V, out, lse, q_start, q_end, k_start, k_end)
+        ctx.causal, ctx.scale = bool(causal), float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, out, lse, qs, qe, ks, ke = ctx.saved_tensors
+        dQ, dK, dV = _C.flash_attention_backward_padded(dO.contiguous(), Q, K, V, out, lse, qs, qe,
+                                                        ks, ke, ctx.causal, ctx.scale)
+        return dQ, dK, dV, None, None, None, None, None, None
+
+
+def flash_attention_padded(Q, K, V, q_start, q_end, k_start, k_end, causal=False, scale=None):
+    """``flash_attention_forward_padded`` with autograd support for square
+    padded batches (Q, K, V all [B, H, N, D]): padding keys get zero dK / dV,
+    query rows outside the ranges zero dQ."""
+    if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
+        raise ValueError("Q, K, V must be 4D [B, H, N, D]")
+    if Q.size(2) != K.size(2):
+        raise ValueError("flash_attention_padded needs Nq == Nk")
+    head_dim = Q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    B = Q.size(0)
+    ranges = [_rows_tensor(x, B, Q.device, name) for x, name in
+              ((q_start, "q_start"), (q_end, "q_end"), (k_start, "k_start"), (k_end, "k_end"))]
+    return FlashAttentionPaddedFunction.apply(Q, K, V, *ranges, causal, scale)
+
+
 _pipeline = {}
 
 

@@ -154,6 +154,23 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
  * 4 KB operand tiles per 128-row query tile, rows padded to 128. */
 size_t fa_bwd_workspace_bytes(int B, int Hq, int N);
 
+/*
+ * fa_bwd_padded — gradients of fa_fwd_padded for square padded batches
+ * (Nq = Nk = N): batch entry b's valid query rows are [q_start[b], q_end[b]) and
+ * valid keys [k_start[b], k_end[b]) (int32 device arrays of B entries); O and
+ * LSE come from fa_fwd_padded (rows outside a query range: O = 0, LSE = -inf, as
+ * the Python API returns them).  Padding keys get dK = dV = 0 and query rows
+ * outside the ranges dQ = 0.  `causal` 0/1 (bottom-right = top-left for square
+ * inputs).  Workspace, errors and stream as fa_bwd.
+ *
+ * No reference counterpart (reference llama_attention_replacement.py:61-62).
+ */
+int fa_bwd_padded(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                  const float* lse, const int* q_start, const int* q_end, const int* k_start,
+                  const int* k_end, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
+                  int head_dim, float scale, int causal, int dtype, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* ---- reference-compatible launchers (void, fp16, blocking) ----
  * Same signatures and conventions as the reference: errors are printed to
  * stderr, the work runs on the legacy default stream and the call ends with

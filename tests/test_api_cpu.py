@@ -11,7 +11,8 @@ def test_public_surface():
     # the reference's surface (src/flash_attention_sm75/__init__.py:1-4) plus additions
     assert fa.__all__ == ["flash_attention_forward", "flash_attention_forward_kvcache",
                           "flash_attention_forward_host", "flash_attention_varlen_forward",
-                          "flash_attention_forward_padded", "flash_attention"]
+                          "flash_attention_forward_padded", "flash_attention",
+                          "flash_attention_padded"]
     assert isinstance(fa.__version__, str)
 
 

@@ -140,3 +140,52 @@ def test_backward_argument_errors(sm100):
                     16, abi.stream_ptr())
     assert rc == 1  # FA_ERR_INVALID_ARG: workspace too small
     assert lib.fa_bwd_workspace_bytes(1, 2, 64) == 2 * 2 * 128 * 4 + 2 * 8192
+
+
+def _padded_grads_ref(q, k, v, do, ranges, causal):
+    """fp32 autograd reference of a square padded batch: key j visible to query
+    i of entry b iff both lie in the entry's ranges (and j <= i when causal);
+    rows without a visible key have output 0."""
+    B, Hq, N, d = q.shape
+    G = Hq // k.size(1)
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    kx, vx = kf.repeat_interleave(G, 1), vf.repeat_interleave(G, 1)
+    i = torch.arange(N)[:, None]
+    j = torch.arange(N)[None, :]
+    mask = torch.zeros(B, 1, N, N, dtype=torch.bool)
+    for b, ((q0, q1), (k0, k1)) in enumerate(ranges):
+        m = (i >= q0) & (i < q1) & (j >= k0) & (j < k1)
+        if causal:
+            m &= j <= i
+        mask[b, 0] = m
+    s = (qf @ kx.transpose(-2, -1)) / math.sqrt(d)
+    s = s.masked_fill(~mask, float("-inf"))
+    p = torch.softmax(s, -1).nan_to_num(0.0)
+    (p @ vx).backward(do.float())
+    return qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_padded_backward_matches_reference(sm100, d, causal):
+    B, Hq, Hkv, N = 3, 4, 2, 200
+    q, k, v, do = _inputs(B, Hq, Hkv, N, d, seed=d + causal)
+    ranges = [((0, N), (0, N)), ((37, N), (37, N)), ((0, 150), (0, 150))]
+    qc, kc, vc, doc = (t.cuda() for t in (q, k, v, do))
+    rng = [torch.tensor([r[i][j] for r in ranges], dtype=torch.int32, device="cuda")
+           for i in (0, 1) for j in (0, 1)]
+    qg, kg, vg = (t.clone().requires_grad_(True) for t in (qc, kc, vc))
+    out = fa.flash_attention_padded(qg, kg, vg, *rng, causal=causal)
+    out.backward(doc)
+    rq, rk, rv = _padded_grads_ref(q, k, v, do, ranges, causal)
+    for got, ref in ((qg.grad, rq), (kg.grad, rk), (vg.grad, rv)):
+        _check(got, ref, torch.float16)
+    # padding: exact zeros
+    assert (qg.grad[1, :, :37] == 0).all() and (qg.grad[2, :, 150:] == 0).all()
+    assert (kg.grad[1, :, :37] == 0).all() and (vg.grad[2, :, 150:] == 0).all()
+    # the C ABI entry point gives the same bits
+    o, lse = fa.flash_attention_forward_padded(qc, kc, vc, *rng, causal=causal, return_lse=True)
+    dq, dk, dv = torch.empty_like(qc), torch.empty_like(kc), torch.empty_like(vc)
+    assert abi.fa_bwd_padded(qc, kc, vc, o, doc, lse, *rng, dq, dk, dv, causal=causal) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dq, qg.grad) and torch.equal(dk, kg.grad) and torch.equal(dv, vg.grad)

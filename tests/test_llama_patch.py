@@ -92,9 +92,9 @@ def test_padded_mask_structure_cpu():
 
 
 def test_requires_grad_routing_cpu():
-    """Calls that need gradients: masked / Nq != Nk ones fall back with reason
-    requires_grad (checked on fake CUDA tensors; the routing of unmasked
-    square calls to the autograd kernels is tested on the GPU)."""
+    """Calls that need gradients: Nq != Nk ones fall back with reason
+    requires_grad (checked on fake CUDA tensors; the routing of square calls
+    to the autograd kernels is tested on the GPU)."""
     class Fake:
         def __init__(self, shape=(1, 2, 8, 64), grad=True):
             self.is_cuda, self.dtype, self._s = True, torch.float16, shape
@@ -109,7 +109,7 @@ def test_requires_grad_routing_cpu():
 
     r = patch._ineligible_reason
     q, kv = Fake((1, 2, 1, 64)), Fake((1, 2, 8, 64))
-    assert r(q, kv, kv, 0.0, None) == "requires_grad"
+    assert r(q, kv, kv, 0.0, None) == "requires_grad"  # Nq != Nk
     with torch.no_grad():
         assert r(q, kv, kv, 0.0, None) is None
     assert r(Fake(), Fake(), Fake(), 0.0, None) is None  # square, unmasked: autograd kernels
