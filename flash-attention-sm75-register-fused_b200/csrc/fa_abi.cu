@@ -435,12 +435,14 @@ size_t fa_bwd_workspace_bytes(int B, int Hq, int N) {
 
 namespace {
 
-// fa_bwd and fa_bwd_padded: ranges (q_lo, q_hi, k_lo, k_hi) all null or all set.
+// fa_bwd, fa_bwd_padded and fa_bwd_varlen: ranges (q_lo, q_hi, k_lo, k_hi)
+// all null or all set; cu (cu_seqlens of a packed batch, `total` rows, N the
+// longest sequence) or null.
 int launch_backward(const void* Q, const void* K, const void* V, const void* O, const void* dO,
                     const float* lse, void* dQ, void* dK, void* dV, const int* q_lo,
-                    const int* q_hi, const int* k_lo, const int* k_hi, int B, int Hq, int Hkv,
-                    int N, int head_dim, float scale, int causal, int dtype, void* workspace,
-                    size_t workspace_bytes, void* stream) {
+                    const int* q_hi, const int* k_lo, const int* k_hi, const int* cu, int total,
+                    int B, int Hq, int Hkv, int N, int head_dim, float scale, int causal,
+                    int dtype, void* workspace, size_t workspace_bytes, void* stream) {
   if (B < 0 || Hq < 0 || Hkv < 0 || N < 0) return FA_ERR_INVALID_ARG;
   if (head_dim != 64 && head_dim != 128) return FA_ERR_UNSUPPORTED_HEAD_DIM;
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return FA_ERR_DTYPE;
@@ -464,9 +466,16 @@ int launch_backward(const void* Q, const void* K, const void* V, const void* O, 
   fa::BwdParams p;
   const bool bf16 = dtype == FA_DTYPE_BF16;
   const long long bhq = static_cast<long long>(B) * Hq, bhk = static_cast<long long>(B) * Hkv;
-  if (!make_map(&p.tm_q, Q, head_dim, N, bhq, bf16) || !make_map(&p.tm_do, dO, head_dim, N, bhq, bf16) ||
-      !make_map(&p.tm_k, K, head_dim, N, bhk, bf16) || !make_map(&p.tm_v, V, head_dim, N, bhk, bf16))
-    return FA_ERR_TENSOR_MAP;
+  const bool maps_ok =
+      cu ? (make_map_packed(&p.tm_q, Q, head_dim, Hq, total, bf16) &&
+            make_map_packed(&p.tm_do, dO, head_dim, Hq, total, bf16) &&
+            make_map_packed(&p.tm_k, K, head_dim, Hkv, total, bf16) &&
+            make_map_packed(&p.tm_v, V, head_dim, Hkv, total, bf16))
+         : (make_map(&p.tm_q, Q, head_dim, N, bhq, bf16) &&
+            make_map(&p.tm_do, dO, head_dim, N, bhq, bf16) &&
+            make_map(&p.tm_k, K, head_dim, N, bhk, bf16) &&
+            make_map(&p.tm_v, V, head_dim, N, bhk, bf16));
+  if (!maps_ok) return FA_ERR_TENSOR_MAP;
   p.dq = dQ;
   p.dk = dK;
   p.dv = dV;
@@ -474,6 +483,8 @@ int launch_backward(const void* Q, const void* K, const void* V, const void* O, 
   p.q_hi = q_hi;
   p.k_lo = k_lo;
   p.k_hi = k_hi;
+  p.cu = cu;
+  p.total = total;
   p.n_tiles = static_cast<int>(n_tiles);
   p.n_pad = p.n_tiles * 128;
   p.l2 = static_cast<const float*>(workspace);
@@ -502,9 +513,9 @@ int fa_bwd(const void* Q, const void* K, const void* V, const void* O, const voi
            const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int N,
            int head_dim, float scale, int causal, int dtype, void* workspace,
            size_t workspace_bytes, void* stream) {
-  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, nullptr, nullptr, nullptr, nullptr, B,
-                         Hq, Hkv, N, head_dim, scale, causal, dtype, workspace, workspace_bytes,
-                         stream);
+  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, nullptr, nullptr, nullptr, nullptr,
+                         nullptr, 0, B, Hq, Hkv, N, head_dim, scale, causal, dtype, workspace,
+                         workspace_bytes, stream);
 }
 
 int fa_bwd_padded(const void* Q, const void* K, const void* V, const void* O, const void* dO,
@@ -514,9 +525,24 @@ int fa_bwd_padded(const void* Q, const void* K, const void* V, const void* O, co
                   size_t workspace_bytes, void* stream) {
   if (B > 0 && Hq > 0 && N > 0 && (!q_start || !q_end || !k_start || !k_end))
     return FA_ERR_INVALID_ARG;
-  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, q_start, q_end, k_start, k_end, B, Hq,
-                         Hkv, N, head_dim, scale, causal, dtype, workspace, workspace_bytes,
-                         stream);
+  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, q_start, q_end, k_start, k_end,
+                         nullptr, 0, B, Hq, Hkv, N, head_dim, scale, causal, dtype, workspace,
+                         workspace_bytes, stream);
+}
+
+int fa_bwd_varlen(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                  const float* lse, const int* cu_seqlens, void* dQ, void* dK, void* dV, int B,
+                  int Hq, int Hkv, int total, int max_seqlen, int head_dim, float scale,
+                  int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (total < 0 || max_seqlen < 0) return FA_ERR_INVALID_ARG;
+  if (B > 0 && Hq > 0 && total > 0 && max_seqlen > 0 && !cu_seqlens) return FA_ERR_INVALID_ARG;
+  if (static_cast<long long>(total) * Hq * head_dim > (1LL << 40) ||
+      static_cast<long long>(total) * Hkv * head_dim > (1LL << 40))
+    return FA_ERR_TOO_LARGE;
+  if (total == 0) return (B < 0 || Hq < 0 || Hkv < 0) ? FA_ERR_INVALID_ARG : FA_OK;
+  return launch_backward(Q, K, V, O, dO, lse, dQ, dK, dV, nullptr, nullptr, nullptr, nullptr,
+                         cu_seqlens, total, B, Hq, Hkv, max_seqlen, head_dim, scale, causal, dtype,
+                         workspace, workspace_bytes, stream);
 }
 
 int fa_fwd_varlen(const void* Q, const void* K, const void* V, void* O, float* lse,

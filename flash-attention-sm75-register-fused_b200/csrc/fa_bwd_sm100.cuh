@@ -80,6 +80,20 @@ struct BwdLayout {
   static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
 };
 
+// First row and length of batch entry b's sequence: the packed varlen layout
+// reads them from cu_seqlens (clamped to the tensors), the fixed layout has
+// every sequence at rows [0, N).
+__device__ __forceinline__ void bwd_seq(const int* cu, int total, int N, int b, int& start,
+                                        int& n) {
+  if (cu == nullptr) {
+    start = 0;
+    n = N;
+    return;
+  }
+  start = min(max(__ldg(cu + b), 0), total);
+  n = min(min(max(__ldg(cu + b + 1), start), total) - start, N);
+}
+
 // Per padded row r < n_pad of every (batch, query head): nl2_r = -LSE_r*log2(e)
 // and nd_r = -D_r = -sum_c dO[r][c] O[r][c] (negated so that the main kernels
 // form s*scale*log2(e) - LSE*log2(e) and dP - D with one packed FMA / add);
@@ -95,7 +109,8 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
                                                           int N, int n_pad, long long n_rows,
                                                           int d, int heads,
                                                           const int* __restrict__ q_lo,
-                                                          const int* __restrict__ q_hi) {
+                                                          const int* __restrict__ q_hi,
+                                                          const int* __restrict__ cu, int total) {
   const int lpr = d >> 3;  // lanes per row: 16 (d = 128) or 8 (d = 64)
   const int rows_per_block = 256 / lpr;
   const long long row = static_cast<long long>(blockIdx.x) * rows_per_block + threadIdx.x / lpr;
@@ -103,21 +118,23 @@ __global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const void* __restrict
   const bool live = row < n_rows;
   const long long bh = live ? row / n_pad : 0;
   const int r = live ? static_cast<int>(row % n_pad) : N;
-  // a row outside its batch entry's query range, or one that saw no key
-  // (LSE = -inf), is treated like a padded row: P = 0
-  bool valid = r < N;
-  if (valid && q_lo != nullptr) {
-    const int b = static_cast<int>(bh / heads);
-    valid = r >= __ldg(q_lo + b) && r < __ldg(q_hi + b);
-  }
-  const float lse_r = valid ? lse[bh * N + r] : 0.f;
+  // a row outside its batch entry's query range or sequence, or one that saw
+  // no key (LSE = -inf), is treated like a padded row: P = 0
+  const int b = static_cast<int>(bh / heads), h = static_cast<int>(bh % heads);
+  int start, n;
+  bwd_seq(cu, total, N, b, start, n);
+  bool valid = live && r < n;
+  if (valid && q_lo != nullptr) valid = r >= __ldg(q_lo + b) && r < __ldg(q_hi + b);
+  // element offset of the row in O / dO and its LSE index (packed: [total, H, d], [H, total])
+  const long long orow = cu ? (static_cast<long long>(start + r) * heads + h) * d : (bh * N + r) * d;
+  const float lse_r = valid ? lse[cu ? static_cast<long long>(h) * total + start + r : bh * N + r] : 0.f;
   if (valid && lse_r == -INFINITY) valid = false;
   float acc = 0.f;
   if (valid) {
     const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(o) +
-                                                    ((bh * N + r) * d + sub * 8) * 2);
+                                                    (orow + sub * 8) * 2);
     const uint4 g = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(dout) +
-                                                    ((bh * N + r) * d + sub * 8) * 2);
+                                                    (orow + sub * 8) * 2);
     const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -309,21 +326,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  uint8_t* smem;
-  uint32_t sbase, tmem;
-  volatile int* abort_flag;
-  if (!bwd_setup<L>(smem_raw, smem, sbase, p.epoch, abort_flag, tmem, warp)) return;
-  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
-  const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
-
   // work: key tile t of KV head (b, hk); steps over the group's query heads
   // and the query tiles that see the key tile (causal: i >= t, heaviest first)
   const int t = blockIdx.x % p.n_tiles;
   const int bhk = blockIdx.x / p.n_tiles;
   const int b = bhk / p.Hkv;
   const int hk = bhk % p.Hkv;
+  int start, n;  // sequence of batch entry b (packed varlen: its rows)
+  bwd_seq(p.cu, p.total, p.N, b, start, n);
+  if (t * 128 >= n) return;  // past the end of a shorter sequence: nothing to do
+  const int n_tiles_b = (n + 127) / 128;
   const int i0 = p.causal ? t : 0;
-  const int n_q = p.n_tiles - i0;
+  const int n_q = n_tiles_b - i0;
+
+  uint8_t* smem;
+  uint32_t sbase, tmem;
+  volatile int* abort_flag;
+  if (!bwd_setup<L>(smem_raw, smem, sbase, p.epoch, abort_flag, tmem, warp)) return;
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
+  const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
   const int n_steps = p.group * n_q;
   auto step_head = [&](int s) { return b * p.Hq + hk * p.group + s / n_q; };  // b*Hq + h
   auto step_tile = [&](int s) { return i0 + s % n_q; };
@@ -347,10 +368,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
       ptx::mbar_arrive_expect_tx(bar(L::kBarFix), 2 * L::kTile);
 #pragma unroll
       for (int c = 0; c < L::kColBlocks; ++c) {
+        // fixed layout: (column, row, batch*head); packed: (column, head, row)
+        const int c1 = p.cu ? hk : t * 128, c2 = p.cu ? start + t * 128 : bhk;
         ptx::tma_load_3d(sbase + L::kOffFix + c * L::kBlockBytes, &p.tm_k, bar(L::kBarFix), c * 64,
-                         t * 128, bhk, pol);
+                         c1, c2, pol);
         ptx::tma_load_3d(sbase + L::kOffFix + L::kTile + c * L::kBlockBytes, &p.tm_v,
-                         bar(L::kBarFix), c * 64, t * 128, bhk, pol);
+                         bar(L::kBarFix), c * 64, c1, c2, pol);
       }
       // ring item 2s: Q tile (+ its L2 vector), 2s+1: dO tile (+ its D vector)
       int issued = 0;
@@ -365,10 +388,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
         const void* map = (i & 1) ? static_cast<const void*>(&p.tm_do) : static_cast<const void*>(&p.tm_q);
         const uint8_t* vec = p.vt + ((static_cast<size_t>(bhq) * p.n_tiles + qt) * 2 + (i & 1)) * L::kVec;
         ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile + L::kVec);
+        const int c1 = p.cu ? bhq % p.Hq : qt * 128, c2 = p.cu ? start + qt * 128 : bhq;
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
           ptx::tma_load_3d(sbase + L::kOffRing + slot * L::kTile + c * L::kBlockBytes, map,
-                           bar(L::kBarFull + slot), c * 64, qt * 128, bhq, pol);
+                           bar(L::kBarFull + slot), c * 64, c1, c2, pol);
         ptx::bulk_load(sbase + L::kOffVec + slot * L::kVec, vec, L::kVec, bar(L::kBarFull + slot));
         issued = i + 1;
       }
@@ -482,9 +506,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t col0 = 64u * g;
     const float sl = p.scale_log2;
-    // padded batch: a key outside its entry's valid range gets P^T = 0
-    const bool key_ok =
-        p.k_lo == nullptr || (key >= __ldg(p.k_lo + b) && key < __ldg(p.k_hi + b));
+    // padded batch: a key outside its entry's valid range gets P^T = 0;
+    // packed: a row past the sequence's end (the next sequence's) too
+    const bool key_ok = key < n && (p.k_lo == nullptr ||
+                                    (key >= __ldg(p.k_lo + b) && key < __ldg(p.k_hi + b)));
     bool ok = true;
     for (int s = 0; ok && s < n_steps; ++s) {
       const int qt = step_tile(s);
@@ -504,10 +529,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
         if (threadIdx.x == 0) FA_TRACE_AT(s, c ? 15 : 13);
         // S^T already holds s - LSE/scale.  Diagonal tile: query
         // q = col0 + 32c + i is kept when q >= key r
-        if (!key_ok)
-          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, 0.f, 32, 32);  // all masked
-        else if (diag)
-          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, 0.f, r - static_cast<int>(col0) - 32 * c, 32);
+        // (a key outside its range masks every column)
+        if (diag || !key_ok)
+          bwd_exp32<true>(pr + 32 * c, sv, sl, nullptr, 0.f,
+                          key_ok ? r - static_cast<int>(col0) - 32 * c : 32, 32);
         else
           bwd_exp32<false>(pr + 32 * c, sv, sl, nullptr, 0.f, 0, 32);
         uint32_t pk[16];
@@ -546,9 +571,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     if (ok) {
       // group 0 writes the dV rows, group 1 the dK rows
       ptx::tc_fence_after();
-      const bool store = key < p.N;
+      const bool store = key < n;
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      const size_t row = static_cast<size_t>(bhk) * p.N + key;
+      // row index in units of d elements (packed: token-major [total, Hkv, d])
+      const size_t row = p.cu ? static_cast<size_t>(start + key) * p.Hkv + hk
+                              : static_cast<size_t>(bhk) * p.N + key;
       if (g == 0)
         bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc0, 1.0f, reinterpret_cast<T*>(p.dv) + row * D, store);
       else
@@ -565,6 +592,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // work: query tile t of (b, hq); key tiles 0..n_kv-1 (causal: j <= t,
+  // heaviest tiles first)
+  int t = blockIdx.x % p.n_tiles;
+  if (p.causal) t = p.n_tiles - 1 - t;
+  const int bh = blockIdx.x / p.n_tiles;
+  const int b = bh / p.Hq;
+  const int h = bh % p.Hq;
+  const int bh_kv = b * p.Hkv + h / p.group;
+  int start, n;  // sequence of batch entry b (packed varlen: its rows)
+  bwd_seq(p.cu, p.total, p.N, b, start, n);
+  if (t * 128 >= n) return;  // past the end of a shorter sequence: nothing to do
+  const int n_kv = p.causal ? t + 1 : (n + 127) / 128;
+
   uint8_t* smem;
   uint32_t sbase, tmem;
   volatile int* abort_flag;
@@ -572,25 +612,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
   auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
 
-  // work: query tile t of (b, hq); key tiles 0..n_kv-1 (causal: j <= t,
-  // heaviest tiles first)
-  int t = blockIdx.x % p.n_tiles;
-  if (p.causal) t = p.n_tiles - 1 - t;
-  const int bh = blockIdx.x / p.n_tiles;
-  const int b = bh / p.Hq;
-  const int bh_kv = b * p.Hkv + (bh % p.Hq) / p.group;
-  const int n_kv = p.causal ? t + 1 : p.n_tiles;
-
   if (warp == kBwdWarpLoad) {
     if (lane == 0) {
       const uint64_t pol = ptx::policy_evict_last();
       ptx::mbar_arrive_expect_tx(bar(L::kBarFix), 2 * L::kTile);
 #pragma unroll
       for (int c = 0; c < L::kColBlocks; ++c) {
+        // fixed layout: (column, row, batch*head); packed: (column, head, row)
+        const int c1 = p.cu ? h : t * 128, c2 = p.cu ? start + t * 128 : bh;
         ptx::tma_load_3d(sbase + L::kOffFix + c * L::kBlockBytes, &p.tm_q, bar(L::kBarFix), c * 64,
-                         t * 128, bh, pol);
+                         c1, c2, pol);
         ptx::tma_load_3d(sbase + L::kOffFix + L::kTile + c * L::kBlockBytes, &p.tm_do,
-                         bar(L::kBarFix), c * 64, t * 128, bh, pol);
+                         bar(L::kBarFix), c * 64, c1, c2, pol);
       }
       // ring item 2j: K_j, 2j+1: V_j
       int issued = 0;
@@ -600,10 +633,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
           break;
         const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v) : static_cast<const void*>(&p.tm_k);
         ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
+        const int row = (i >> 1) * 128;
+        const int c1 = p.cu ? h / p.group : row, c2 = p.cu ? start + row : bh_kv;
 #pragma unroll
         for (int c = 0; c < L::kColBlocks; ++c)
           ptx::tma_load_3d(sbase + L::kOffRing + slot * L::kTile + c * L::kBlockBytes, map,
-                           bar(L::kBarFull + slot), c * 64, (i >> 1) * 128, bh_kv, pol);
+                           bar(L::kBarFull + slot), c * 64, c1, c2, pol);
         issued = i + 1;
       }
       for (int i = max(0, issued - L::kSlots); i < issued; ++i)
@@ -737,7 +772,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       // keys >= N, (causal) keys > this query and (padded batch) keys outside
       // the entry's range get P = 0; [klo, lim) relative to the group's first key
       const int key0 = j * 128 + col0;
-      int lim = p.N - key0;
+      int lim = n - key0;
       if (p.causal && j == t) lim = min(lim, r + 1 - col0);
       int klo = 0;
       if (p.k_lo != nullptr) {
@@ -749,7 +784,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
       if (threadIdx.x == 0) FA_TRACE_AT(j, 25);
       ptx::tc_fence_after();
       // masked tiles only: the group's keys reach N, the diagonal or a range end
-      const bool masked = (p.causal && j == t) || p.N - key0 < 64 || klo > 0 ||
+      const bool masked = (p.causal && j == t) || n - key0 < 64 || klo > 0 ||
                           (p.k_lo != nullptr && k_end - key0 < 64);
       if (threadIdx.x == 0) FA_TRACE_AT(j, 24);
       float pr[64];
@@ -790,10 +825,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     if (ok && g == 0) {
       ptx::tc_fence_after();
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      const size_t row = static_cast<size_t>(bh) * p.N + q_row;
+      // row index in units of d elements (packed: token-major [total, Hq, d])
+      const size_t row = p.cu ? static_cast<size_t>(start + q_row) * p.Hq + h
+                              : static_cast<size_t>(bh) * p.N + q_row;
       // rows that take no part (padding, or no visible key: -LSE = -inf) get dQ = 0
       bwd_store_row<D, BF16>(tmem + lane_off + L::tAcc0, nlv == -INFINITY ? 0.f : p.scale,
-                             reinterpret_cast<T*>(p.dq) + row * D, q_row < p.N);
+                             reinterpret_cast<T*>(p.dq) + row * D, q_row < n);
     }
   }
   bwd_teardown<L>(tmem, warp);
@@ -821,7 +858,7 @@ static cudaError_t launch_bwd_impl(const BwdParams& p, const void* o, const void
   const long long rows_per_block = 256 / (D / 8);
   fa_bwd_prep_kernel<BF16><<<static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block), 256, 0, stream>>>(
       o, dout, lse, const_cast<float*>(p.l2), const_cast<float*>(p.dd), const_cast<uint8_t*>(p.vt),
-      p.scale, p.N, p.n_pad, rows, D, p.Hq, p.q_lo, p.q_hi);
+      p.scale, p.N, p.n_pad, rows, D, p.Hq, p.q_lo, p.q_hi, p.cu, p.total);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   fa_bwd_dkdv_kernel<D, BF16><<<p.B * p.Hkv * p.n_tiles, kBwdThreads, BwdLayout<D>::kDynBytes, stream>>>(p);

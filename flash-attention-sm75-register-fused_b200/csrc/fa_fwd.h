@@ -118,6 +118,12 @@ struct alignas(64) BwdParams {
   const int* q_hi;
   const int* k_lo;
   const int* k_hi;
+  // Packed variable-length batch (self-attention): cu_seqlens [B + 1] or
+  // nullptr.  Sequence b owns rows [cu[b], cu[b+1]) of Q, K, V, O, dO, dQ, dK,
+  // dV ([total, H, d]; maps (d, H, T)) and LSE [Hq, total]; N is the longest
+  // sequence (it sizes the grid and the per-tile workspace).
+  const int* cu;
+  int total;
   int B, Hq, Hkv, N, n_pad, group, n_tiles, causal;
   float scale, scale_log2;
   long long* trace;  // timeline samples, used only in FA_TRACE builds

@@ -405,6 +405,53 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> flash_attention_backward
   return {dQ, dK, dV};
 }
 
+// Gradients of flash_attention_forward_varlen for packed self-attention batches.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> flash_attention_backward_varlen(
+    torch::Tensor dO, torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor O,
+    torch::Tensor lse, torch::Tensor cu_seqlens, int64_t max_seqlen, bool causal, float scale) {
+  check_packed(Q, "Q");
+  check_packed(K, "K");
+  check_packed(V, "V");
+  check_packed(O, "O");
+  check_packed(dO, "dO");
+  TORCH_CHECK(Q.dtype() == K.dtype() && Q.dtype() == V.dtype() && Q.dtype() == O.dtype() &&
+                  Q.dtype() == dO.dtype(),
+              "Q, K, V, O, dO must share a dtype");
+  TORCH_CHECK(O.sizes() == Q.sizes() && dO.sizes() == Q.sizes(), "O and dO must have Q's shape");
+  TORCH_CHECK(K.sizes() == V.sizes() && K.size(0) == Q.size(0) && K.size(2) == Q.size(2),
+              "K, V must be [total, Hkv, d] over the same rows as Q (self-attention)");
+  TORCH_CHECK(lse.is_cuda() && lse.dtype() == torch::kFloat32 && lse.is_contiguous() &&
+                  lse.dim() == 2 && lse.size(0) == Q.size(1) && lse.size(1) == Q.size(0),
+              "lse must be a contiguous fp32 CUDA tensor [Hq, total]");
+  const auto head_dim = Q.size(2);
+  TORCH_CHECK(head_dim == 64 || head_dim == 128,
+              "flash_attention_forward supports head_dim=64 or 128, got ", head_dim);
+  TORCH_CHECK(K.size(1) > 0 && Q.size(1) % K.size(1) == 0, "GQA: Q heads (", Q.size(1),
+              ") not divisible by K/V heads (", K.size(1), ")");
+  TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.size(0) >= 1, "cu_seqlens must be [B + 1]");
+  const int64_t B = cu_seqlens.size(0) - 1;
+  check_rows(cu_seqlens, "cu_seqlens", B + 1, Q);
+  TORCH_CHECK(Q.size(0) <= INT32_MAX && max_seqlen >= 0 && max_seqlen <= INT32_MAX,
+              "size exceeds int32");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  const int Hq = static_cast<int>(Q.size(1));
+  auto dQ = torch::empty_like(Q);
+  auto dK = torch::empty_like(K);
+  auto dV = torch::empty_like(V);
+  const size_t ws_bytes = fa_bwd_workspace_bytes(static_cast<int>(B), Hq, static_cast<int>(max_seqlen));
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes > 0 ? ws_bytes : 16)},
+                         Q.options().dtype(torch::kUInt8));
+  const int rc = fa_bwd_varlen(
+      Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), dO.data_ptr(), lse.data_ptr<float>(),
+      cu_seqlens.data_ptr<int>(), dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), static_cast<int>(B),
+      Hq, static_cast<int>(K.size(1)), static_cast<int>(Q.size(0)), static_cast<int>(max_seqlen),
+      static_cast<int>(head_dim), scale, causal ? 1 : 0,
+      Q.dtype() == torch::kBFloat16 ? FA_DTYPE_BF16 : FA_DTYPE_F16, ws.data_ptr(), ws_bytes,
+      stream_of(Q));
+  TORCH_CHECK(rc == FA_OK, "flash_attention_backward_varlen: ", fa_error_string(rc));
+  return {dQ, dK, dV};
+}
+
 int device_status(bool reset) { return fa_device_status(reset ? 1 : 0); }
 
 }  // namespace
@@ -429,6 +476,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "(O, LSE) of a padded batch with per-entry valid query / key row ranges");
   m.def("flash_attention_backward_padded", &flash_attention_backward_padded,
         "(dQ, dK, dV) of flash_attention_forward_padded for square padded batches");
+  m.def("flash_attention_backward_varlen", &flash_attention_backward_varlen,
+        "(dQ, dK, dV) of flash_attention_forward_varlen for packed self-attention batches");
   m.def("device_status", &device_status, pybind11::arg("reset") = false,
         "Error code recorded by the in-kernel watchdog (0 = none)");
   m.def("set_watchdog_ns", &fa_set_watchdog_ns);

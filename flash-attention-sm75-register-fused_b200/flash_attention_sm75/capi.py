@@ -25,6 +25,9 @@ SIGNATURES = {
     "fa_bwd_padded": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                               c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int,
                               c_vp, ctypes.c_size_t, c_vp]),
+    "fa_bwd_varlen": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int,
+                              c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_vp,
+                              ctypes.c_size_t, c_vp]),
     "fa_fwd_varlen": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int,
                               c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_vp]),
     "fa_fwd_padded": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
@@ -188,3 +191,24 @@ def fa_bwd_padded(q, k, v, o, do, lse, q_start, q_end, k_start, k_end, dq, dk, d
                              ptr(q_end), ptr(k_start), ptr(k_end), ptr(dq), ptr(dk), ptr(dv), B, Hq,
                              Hkv, N, d, float(scale), int(bool(causal)), dtype, ptr(ws), nbytes,
                              stream_ptr(stream))
+
+
+def fa_bwd_varlen(q, k, v, o, do, lse, cu, max_seqlen, dq, dk, dv, causal=False, scale=None,
+                  stream=None):
+    """Call fa_bwd_varlen on packed torch CUDA tensors ([total, H, d]; lse
+    [Hq, total] fp32; cu int32 [B + 1]); allocates the workspace.  Returns the
+    status."""
+    import math
+    import torch
+    T, Hq, d = q.shape
+    Hkv = k.shape[1]
+    B = cu.numel() - 1
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    dtype = 1 if q.dtype == torch.bfloat16 else 0
+    lib = load()
+    nbytes = lib.fa_bwd_workspace_bytes(B, Hq, int(max_seqlen))
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    return lib.fa_bwd_varlen(ptr(q), ptr(k), ptr(v), ptr(o), ptr(do), ptr(lse), ptr(cu), ptr(dq),
+                             ptr(dk), ptr(dv), B, Hq, Hkv, T, int(max_seqlen), d, float(scale),
+                             int(bool(causal)), dtype, ptr(ws), nbytes, stream_ptr(stream))

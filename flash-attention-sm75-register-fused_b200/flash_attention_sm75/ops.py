@@ -282,6 +282,47 @@ def flash_attention_padded(Q, K, V, q_start, q_end, k_start, k_end, causal=False
     return FlashAttentionPaddedFunction.apply(Q, K, V, *ranges, causal, scale)
 
 
+class FlashAttentionVarlenFunction(torch.autograd.Function):
+    """Packed variable-length self-attention with forward and backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cu, max_seqlen, causal, scale):
+        _check_gqa(q.size(1), k.size(1))
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        out, lse = _C.flash_attention_forward_varlen(q, k, v, cu, cu, int(max_seqlen),
+                                                     int(max_seqlen), 1 if causal else 0,
+                                                     float(scale))
+        ctx.save_for_backward(q, k, v, out, lse, cu)
+        ctx.max_seqlen, ctx.causal, ctx.scale = int(max_seqlen), bool(causal), float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dO):
+        q, k, v, out, lse, cu = ctx.saved_tensors
+        dq, dk, dv = _C.flash_attention_backward_varlen(dO.contiguous(), q, k, v, out, lse, cu,
+                                                        ctx.max_seqlen, ctx.causal, ctx.scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, causal=False, scale=None):
+    """``flash_attention_varlen_forward`` with autograd support for packed
+    self-attention batches (one ``cu_seqlens`` for queries and keys): q
+    [total, H_q, D], k / v [total, H_kv, D]."""
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("q, k, v must be 3D [total, H, D]")
+    if q.size(0) != k.size(0):
+        raise ValueError("flash_attention_varlen is self-attention: q and k share their rows")
+    head_dim = q.size(-1)
+    if head_dim not in (64, 128):
+        raise RuntimeError(
+            f"flash_attention_sm75 supports head_dim=64 or 128, got {head_dim}"
+        )
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    cu = torch.as_tensor(cu_seqlens, dtype=torch.int32, device=q.device).contiguous()
+    return FlashAttentionVarlenFunction.apply(q, k, v, cu, max_seqlen, causal, scale)
+
+
 _pipeline = {}
 
 

@@ -171,6 +171,21 @@ int fa_bwd_padded(const void* Q, const void* K, const void* V, const void* O, co
                   int head_dim, float scale, int causal, int dtype, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/*
+ * fa_bwd_varlen — gradients of fa_fwd_varlen for packed self-attention batches
+ * (the same cu_seqlens for queries and keys): Q, K, V, O, dO, dQ, dK, dV in the
+ * packed layout ([total, H, d]), LSE fp32 [Hq, total] from fa_fwd_varlen,
+ * cu_seqlens int32 device array of B + 1 offsets, max_seqlen >= every length.
+ * `causal` 0/1.  Workspace: fa_bwd_workspace_bytes(B, Hq, max_seqlen).
+ * Errors and stream as fa_bwd.
+ *
+ * No reference counterpart (reference llama_attention_replacement.py:61-62).
+ */
+int fa_bwd_varlen(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                  const float* lse, const int* cu_seqlens, void* dQ, void* dK, void* dV, int B,
+                  int Hq, int Hkv, int total, int max_seqlen, int head_dim, float scale,
+                  int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- reference-compatible launchers (void, fp16, blocking) ----
  * Same signatures and conventions as the reference: errors are printed to
  * stderr, the work runs on the legacy default stream and the call ends with

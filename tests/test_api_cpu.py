@@ -12,7 +12,7 @@ def test_public_surface():
     assert fa.__all__ == ["flash_attention_forward", "flash_attention_forward_kvcache",
                           "flash_attention_forward_host", "flash_attention_varlen_forward",
                           "flash_attention_forward_padded", "flash_attention",
-                          "flash_attention_padded"]
+                          "flash_attention_padded", "flash_attention_varlen"]
     assert isinstance(fa.__version__, str)
 
 
