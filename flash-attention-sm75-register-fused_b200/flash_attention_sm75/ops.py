@@ -333,7 +333,7 @@ def _pipeline_streams(index):
 
 
 def flash_attention_forward_host(Q, K, V, causal=False, scale=None, out=None, device=None,
-                                 chunks=16):
+                                 chunks=32):
     """Attention forward of host-resident Q, K, V into host-resident O.
 
     The work is cut into about ``chunks`` (batch entry, KV-head group) slices.
