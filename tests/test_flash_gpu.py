@@ -182,3 +182,61 @@ def test_lse_null_and_stream(sm100):
     o2, _ = run(q, k, v, False)
     assert torch.equal(o, o2)
     assert abi.load().fa_device_status(0) == 0
+
+
+def _spiked_inputs(B, Hq, Hkv, Nq, Nk, d, spikes, dtype=torch.float16, seed=5):
+    """Queries in [0.5, 1] and small random keys, except keys at the positions
+    `spikes` (ascending), which are constant vectors of growing size: each
+    spike lifts a row's running score maximum by ~18 log2 units (above the
+    kernel's lazy-rescale threshold of 15), wherever it falls in a K/V tile."""
+    g = torch.Generator().manual_seed(seed)
+    q = 0.5 + 0.5 * torch.rand(B, Hq, Nq, d, generator=g)
+    k = 0.3 * torch.randn(B, Hkv, Nk, d, generator=g)
+    v = torch.randn(B, Hkv, Nk, d, generator=g)
+    step = 18.0 / (0.75 * math.sqrt(d) * 1.4426950408889634)
+    for t, pos in enumerate(spikes):
+        k[:, :, pos] = step * (t + 1)
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+# spike positions (128-key tiles, the first 64 keys of a tile form its early
+# part): tile 1 early, tile 2 late, tile 3 early then late, tile 5 last key,
+# tile 7 first late key, tile 8 early
+SPIKES = [133, 356, 404, 474, 767, 960, 1030]
+
+
+@pytest.mark.parametrize("d,causal,dtype", [(64, False, torch.float16), (128, False, torch.float16),
+                                             (128, True, torch.float16), (64, True, torch.bfloat16)])
+def test_parity_late_max_growth(sm100, d, causal, dtype):
+    """The running maximum grows by more than the rescale threshold in later
+    K/V tiles, in either part of a tile and twice within one: O and l must be
+    rescaled consistently whichever part of P was already consumed."""
+    q, k, v = _spiked_inputs(1, 4, 2, 1100, 1100, d, SPIKES, dtype)
+    o, lse = run(q.cuda(), k.cuda(), v.cuda(), causal)
+    ref_o, ref_lse = orc.attention_fp32(q, k, v, causal=causal)
+    if dtype == torch.bfloat16:
+        r = orc.check(o.cpu(), ref_o, atol=BF16_ATOL, rtol=BF16_RTOL)
+    else:
+        r = orc.check(o.cpu(), ref_o)
+    assert r["ok"], r
+    lerr = (lse.cpu() - ref_lse).abs()
+    assert (lerr <= orc.LSE_ATOL + 2e-6 * ref_lse.abs()).all(), lerr.max().item()
+
+
+@pytest.mark.parametrize("Nq,Nk", [(1, 4096), (3, 2500)])
+def test_parity_late_max_growth_kvcache(sm100, Nq, Nk):
+    """Late max growth in the split-KV (decode) path, where each split and
+    each half of a dual split rescales on its own before the combine."""
+    spikes = [133, 356, 404, 474, 1279, 2050, 2333]
+    q, k, v = _spiked_inputs(2, 8, 2, Nq, Nk, 128, spikes)
+    o = torch.empty_like(q).cuda()
+    lse = torch.empty(q.shape[:3], dtype=torch.float32, device="cuda")
+    rc = abi.fa_fwd_kvcache(q.cuda(), k.cuda(), v.cuda(), o, lse, causal=1, workspace=True)
+    assert rc == 0, abi.load().fa_error_string(rc)
+    torch.cuda.synchronize()
+    ref_o, ref_lse = orc.attention_fp32(q, k, v, causal=True,
+                                        causal_offset=orc.kvcache_offset(Nq, Nk, 1))
+    r = orc.check(o.cpu(), ref_o)
+    assert r["ok"], r
+    lerr = (lse.cpu() - ref_lse).abs()
+    assert (lerr <= orc.LSE_ATOL + 2e-6 * ref_lse.abs()).all(), lerr.max().item()
