@@ -37,16 +37,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [rows = B*H*N, d] tensor viewed as 3-D (d, N, B*H) so that a 128-row box
-// never crosses into the next head: rows >= N read as zeros.
-bool make_map(CUtensorMap* map, const void* base, int d, int n, long long bh, bool bf16) {
+// [rows = B*H*N, d] tensor viewed as 3-D (d, N, B*H) so that a box of
+// `box_rows` rows never crosses into the next head: rows >= N read as zeros.
+bool make_map(CUtensorMap* map, const void* base, int d, int n, long long bh, bool bf16,
+              unsigned box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n),
                               static_cast<cuuint64_t>(bh)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
                                  static_cast<cuuint64_t>(n) * static_cast<cuuint64_t>(d) * 2};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t box[3] = {64, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r =
       fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -170,12 +171,15 @@ int sm_count() {
 // CTAs per SM run; a combine kernel merges the splits.
 struct Plan {
   bool pack = false;
+  bool decode = false;  // at most 16 query rows: the decode kernel
   bool dual = false;  // one Q tile: the two softmax groups split the key tiles
   int n_ctas = 0;     // persistent CTAs (dual mode), 0 = one per work item
   int heads = 0, rows = 0, group = 1, pos_mod = 1, n_qpairs = 0, n_kv_tiles = 0;
   int n_splits = 1, tiles_per_split = 0;
   size_t ws_o_bytes = 0, ws_bytes = 0;
 };
+
+constexpr int kDecodeRows = 16;  // query rows of the decode kernel's blocks
 
 Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) {
   Plan k;
@@ -223,6 +227,33 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
     if (tps > k.n_kv_tiles) tps = k.n_kv_tiles;
     k.tiles_per_split = static_cast<int>(tps);
     k.n_splits = (k.n_kv_tiles + k.tiles_per_split - 1) / k.tiles_per_split;
+    const long long n_work = units * k.n_splits;
+    k.n_ctas = static_cast<int>(n_work < sms ? n_work : sms);
+  }
+  // At most 16 query rows per (batch, head) -- decode -- run the decode
+  // kernel (keys on the MMA's M dimension, persistent CTAs walking (head, key
+  // split) items).  The split is chosen for balance: fewest waves of items
+  // over the SMs, each item costing its tiles plus about half a tile of
+  // hand-off; at most 64 splits per row keep the combine short.
+  k.decode = k.rows <= kDecodeRows;
+  if (k.decode) {
+    k.dual = false;
+    const long long n = k.n_kv_tiles;
+    long long best_tps = n, best_cost = -1;
+    if (allow_split) {
+      for (long long tps = 1; tps <= n; ++tps) {
+        const long long ns = (n + tps - 1) / tps;
+        if (ns > 64 || (n + ns - 1) / ns != tps) continue;  // balanced splits only
+        const long long waves = (units * ns + sms - 1) / sms;
+        const long long cost = waves * (2 * tps + 1);
+        if (best_cost < 0 || cost < best_cost) {
+          best_cost = cost;
+          best_tps = tps;
+        }
+      }
+    }
+    k.tiles_per_split = static_cast<int>(best_tps);
+    k.n_splits = static_cast<int>((n + best_tps - 1) / best_tps);
     const long long n_work = units * k.n_splits;
     k.n_ctas = static_cast<int>(n_work < sms ? n_work : sms);
   }
@@ -276,7 +307,7 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
 
   fa::FwdParams p;
   const long long bh = static_cast<long long>(B) * k.heads;
-  if (!make_map(&p.tm_q, Q, head_dim, k.rows, bh, bf16) ||
+  if (!make_map(&p.tm_q, Q, head_dim, k.rows, bh, bf16, k.decode ? kDecodeRows : 128) ||
       !make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16) ||
       !make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16))
     return FA_ERR_TENSOR_MAP;
@@ -312,7 +343,9 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (fa::launch_fwd(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
+  const cudaError_t e = k.decode ? fa::launch_decode(p, head_dim, bf16, s)
+                                 : fa::launch_fwd(p, head_dim, bf16, s);
+  if (e != cudaSuccess) return FA_ERR_LAUNCH;
   if (use_ws && fa::launch_combine(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
   return FA_OK;
 }

@@ -1,0 +1,607 @@
+// Decode attention for B200 (sm_100a): query blocks of at most 16 rows per
+// (batch, KV head) -- one token per query head of a GQA group, or a few
+// tokens of a short chunk -- against a long K/V cache.  Included by
+// fa_fwd_sm100.cu, whose helpers (bounded mbarrier waits, the device status
+// word, pack2, kv_tiles_core) it uses.
+//
+// The same online softmax as the attention kernel (running max m, sum l, O
+// rescaled when m grows; flash-attention-sm75-fused/include/online_step.cuh:
+// 36-126), arranged for few query rows: keys lie on the MMA's M dimension.
+//
+//   S^T = K_j Q^T        M = 128 keys (one TMEM lane each), N = 16 query rows
+//   P   = exp2(S - m)    written by the key's thread into shared memory as
+//                        the K-major A operand [128 rows x 128 keys], double-
+//                        buffered; only the first 16 rows are written, and the
+//                        rows past them overlap the other buffers: they only
+//                        reach O rows past the query block, which are never
+//                        read (so four 16 KB operand blocks fit in 22 KB)
+//   O  += P V_j          M = 128 (the first rows are the queries), N = d
+//
+// so each thread computes R <= 16 exponentials per 128-key tile (R = the
+// block's rows rounded up to 4, 8 or 16) instead of 128, and S^T is
+// double-buffered in TMEM: the scores of tile j+1 are computed while the
+// softmax of tile j runs.  The rows' maxima are combined across the four
+// softmax warps once per tile (named barrier with an AND of the warps' status,
+// so a failed wait makes all four leave together).
+//
+// Work items are (batch*head, key split) pairs walked by persistent CTAs; the
+// K/V ring and the Q double buffer carry over from one item to the next.  A
+// split writes a normalised partial O and its LSE for fa_combine_kernel
+// (n_splits > 1), otherwise the final O / LSE.
+//
+// Warps (192 threads): 0-3 softmax (thread t = key t of the tile; warp 0 also
+// rescales O and writes the epilogue, whose rows live in TMEM lanes 0-15),
+// 4 TMA producer, 5 MMA issuer + TMEM owner.
+namespace fa {
+namespace {
+
+constexpr int kDecThreads = 192;
+constexpr int kDecRows = 16;  // query rows per item: the S^T MMA's N
+constexpr int kDecWarpLoad = 4;
+constexpr int kDecWarpMma = 5;
+
+template <int D>
+struct DecLayout {
+  static constexpr int kTile = kBlockN * D * 2;          // one K or V tile
+  static constexpr int kBlockBytes = kBlockN * 128;      // 64-column block of a tile
+  static constexpr int kSlots = (D == 128) ? 6 : 12;     // K/V ring (192 KB)
+  static constexpr int kQBytes = kDecRows * D * 2;       // 16-row Q block
+  static constexpr int kQBlock = kDecRows * 128;         // 64-column block of it
+  static constexpr int kPBlock = kBlockM * 128;          // 64 keys x 128 rows of P (16 KB)
+  // Operand block i = 2 * buffer + (key / 64) starts at kOffP + i * kPRows:
+  // its 16 written rows are rows 16 i.. of block 0, the rows past them are
+  // the next blocks' written rows (or never written)
+  static constexpr int kPRows = kDecRows * 128;          // 2 KB
+  // shared memory (offsets from a 1024-aligned base)
+  static constexpr int kOffP = 0;
+  static constexpr int kOffKV = kOffP + kPBlock + 3 * kPRows;
+  static constexpr int kOffQ = kOffKV + kSlots * kTile;  // Q double buffer
+  static constexpr int kOffRed = kOffQ + 2 * kQBytes;    // [2][4 warps][16] row maxima
+  static constexpr int kOffSum = kOffRed + 2 * 4 * kDecRows * 4;  // [4 warps][16] row sums
+  static constexpr int kOffBar = kOffSum + 4 * kDecRows * 4;
+  // named barrier of the four softmax warps
+  static constexpr uint32_t kNamedBar = 1;
+  // barriers
+  static constexpr int kBarQ = 0;                        // 2 (TMA)
+  static constexpr int kBarQFree = 2;                    // 2 (MMA commit)
+  static constexpr int kBarFull = 4;                     // kSlots (TMA)
+  static constexpr int kBarEmpty = kBarFull + kSlots;    // kSlots (MMA commit)
+  static constexpr int kBarS = kBarEmpty + kSlots;       // 2 (MMA commit): S^T buffer written
+  static constexpr int kBarSFree = kBarS + 2;            // 2 (128 arrivals): S^T buffer read
+  static constexpr int kBarP = kBarSFree + 2;            // 2 (128 arrivals): P buffer written
+  static constexpr int kBarPV = kBarP + 2;               // 2 (MMA commit): PV from P buffer done
+  static constexpr int kBarOFree = kBarPV + 2;           // 1 (1 arrival): epilogue read O
+  static constexpr int kBarDrain = kBarOFree + 1;        // 1 (MMA commit)
+  static constexpr int kNumBars = kBarDrain + 1;
+  static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
+  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kDynBytes = kBytes + 1024;
+  // tensor memory: S^T buffers at columns 0 / 16, O at 128
+  static constexpr uint32_t kTmemCols = 256;
+  __host__ __device__ static constexpr uint32_t tS(int b) { return b ? 16u : 0u; }
+  static constexpr uint32_t tO = 128;
+  static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kOffKV % 1024 == 0 && kOffQ % 1024 == 0 && kTile % 1024 == 0 &&
+                    kQBytes % 1024 == 0,
+                "128-byte-swizzled operands need 1024-byte alignment");
+};
+
+struct DecItem {
+  int bh, sp, bh_kv;
+  int jb, n;  // first K/V tile and tile count of the split
+};
+
+__device__ __forceinline__ void dec_item(const FwdParams& p, int w, DecItem& it) {
+  it.sp = w % p.n_splits;
+  it.bh = w / p.n_splits;
+  const int b = it.bh / p.heads;
+  it.bh_kv = b * p.Hkv + (it.bh % p.heads) / p.group;
+  // all rows are in query tile 0
+  const int total = kv_tiles_for_tile(p, 0);
+  it.jb = it.sp * p.tiles_per_split;
+  it.n = max(0, min(total, it.jb + p.tiles_per_split) - it.jb);
+}
+
+// Transposed butterfly over the warp: v[R] per lane in; out, the reduction
+// over all 32 lanes of row dec_row<R>(lane) (lanes with the low lane bits
+// dec_low<R>() clear hold it).  log2(R) halving steps on lane bits 16, 8, ..
+// then a plain butterfly over the remaining bits.
+template <int R>
+__device__ __forceinline__ constexpr int dec_low() {
+  return (16 >> (R == 4 ? 2 : R == 8 ? 3 : 4)) * 2 - 1;
+}
+template <int R, bool kMax>
+__device__ __forceinline__ float dec_reduce(float (&v)[R], int lane) {
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+  constexpr int kSteps = R == 4 ? 2 : R == 8 ? 3 : 4;
+#pragma unroll
+  for (int step = 0; step < kSteps; ++step) {
+    // rows [0, 2*half) -> [0, half): lanes with lane bit `bit` set keep the
+    // upper half of the rows, their partners the lower half
+    const int half = (R / 2) >> step;
+    const int bit = 16 >> step;
+    const bool hi = (lane & bit) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = hi ? v[i] : v[i + half];
+      const float keep = hi ? v[i + half] : v[i];
+      v[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, bit));
+    }
+  }
+  float r = v[0];
+#pragma unroll
+  for (int bit = 16 >> kSteps; bit >= 1; bit >>= 1) r = op(r, __shfl_xor_sync(0xffffffffu, r, bit));
+  return r;
+}
+
+template <int R>
+__device__ __forceinline__ int dec_row(int lane) {
+  constexpr int kSteps = R == 4 ? 2 : R == 8 ? 3 : 4;
+  int row = 0;
+#pragma unroll
+  for (int step = 0; step < kSteps; ++step)
+    if (lane & (16 >> step)) row += (R / 2) >> step;
+  return row;
+}
+
+template <int D, bool BF16, int R>
+__global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_constant__ FwdParams p) {
+  static_assert(R == 4 || R == 8 || R == 16, "rows per block");
+  using L = DecLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
+  const int n_work = p.B * p.heads * p.n_splits;
+
+  // ---- set-up
+  if (threadIdx.x == 0) {
+    const unsigned long long st = *reinterpret_cast<volatile unsigned long long*>(&g_fa_status);
+    *abort_flag = ((st >> 32) == p.epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
+    for (int i = 0; i < L::kNumBars; ++i) {
+      const bool all = (i == L::kBarSFree || i == L::kBarSFree + 1 || i == L::kBarP ||
+                        i == L::kBarP + 1);
+      ptx::mbar_init(bar(i), all ? 128u : 1u);
+    }
+    ptx::fence_barrier_init();
+  }
+  // P rows past the query block are not written by the softmax: start them
+  // at zero (their products only reach O rows that are never read)
+  if (warp < 4) {
+    uint4* pz = reinterpret_cast<uint4*>(smem + L::kOffP);
+    for (int i = threadIdx.x; i < (L::kOffKV - L::kOffP) / 16; i += 128)
+      pz[i] = make_uint4(0u, 0u, 0u, 0u);
+    ptx::fence_proxy_async_smem();
+  }
+  __syncthreads();
+  if (*abort_flag) return;
+  if (warp == kDecWarpMma) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), L::kTmemCols);
+    ptx::tmem_relinquish();
+    ptx::tc_fence_before();
+  }
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
+
+  if (warp == kDecWarpLoad) {
+    // ===================================================== TMA producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&p.tm_q);
+      ptx::prefetch_tmap(&p.tm_k);
+      ptx::prefetch_tmap(&p.tm_v);
+      const uint64_t pol_q = ptx::policy_evict_first();
+      const uint64_t pol_kv = ptx::policy_evict_first();  // each K/V tile is read once
+      int ring = 0, k = 0, q_loads[2] = {0, 0};
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x) {
+        DecItem it;
+        dec_item(p, w, it);
+        if (it.n == 0) continue;
+        const int qb = k & 1;
+        // item k's Q overwrites the buffer of item k-2, once its S MMAs completed
+        if (k >= 2 && !(ok = bar_wait(bar(L::kBarQFree + qb), ((k - 2) >> 1) & 1, wc, 40))) break;
+        ptx::mbar_arrive_expect_tx(bar(L::kBarQ + qb), L::kQBytes);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          ptx::tma_load_3d(sbase + L::kOffQ + qb * L::kQBytes + c * L::kQBlock, &p.tm_q,
+                           bar(L::kBarQ + qb), c * 64, 0, it.bh, pol_q);
+        ++q_loads[qb];
+        for (int i = 0; i < 2 * it.n; ++i, ++ring) {  // K_j, V_j, K_j+1, ...
+          const int slot = ring % L::kSlots;
+          if (ring >= L::kSlots &&
+              !(ok = bar_wait(bar(L::kBarEmpty + slot), ((ring / L::kSlots) - 1) & 1, wc, 41)))
+            break;
+          const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
+                                    : static_cast<const void*>(&p.tm_k);
+          const uint32_t dst = sbase + L::kOffKV + slot * L::kTile;
+          ptx::mbar_arrive_expect_tx(bar(L::kBarFull + slot), L::kTile);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
+                             (it.jb + (i >> 1)) * kBlockN, it.bh_kv, pol_kv);
+        }
+        ++k;
+      }
+      // every copy this thread started lands before the CTA exits
+      for (int r = max(0, ring - L::kSlots); r < ring; ++r)
+        bar_wait(bar(L::kBarFull + r % L::kSlots), (r / L::kSlots) & 1, wc, 42, false);
+      for (int b = 0; b < 2; ++b)
+        if (q_loads[b] > 0) bar_wait(bar(L::kBarQ + b), (q_loads[b] - 1) & 1, wc, 42, false);
+    }
+  } else if (warp == kDecWarpMma) {
+    // ===================================================== MMA issuer
+    constexpr uint32_t fmt = BF16 ? 1u : 0u;
+    constexpr uint32_t idesc_s = ptx::make_idesc_f16(kBlockN, kDecRows, fmt, 0, 0);
+    constexpr uint32_t idesc_pv = ptx::make_idesc_f16(kBlockM, D, fmt, 0, 1);
+    const uint64_t k_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16, 1024);
+    const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
+    const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
+    const uint64_t p_desc = ptx::smem_desc_sw128(sbase + L::kOffP, 16, 1024);
+    auto slot_of = [](int item) { return item % L::kSlots; };
+    auto phase_of = [](int item) { return static_cast<uint32_t>((item / L::kSlots) & 1); };
+    auto wait = [&](uint32_t b, uint32_t ph, int site) {
+      return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
+    };
+    // S^T(c) = K_c Q^T into buffer c & 1 (K = ring item 2c, Q buffer qb)
+    auto issue_s = [&](int c, int qb, bool last_of_item) -> bool {
+      if (!wait(bar(L::kBarFull + slot_of(2 * c)), phase_of(2 * c), 43)) return false;
+      if (c >= 2 && !wait(bar(L::kBarSFree + (c & 1)), ((c >> 1) - 1) & 1, 44)) return false;
+      ptx::tc_fence_after();
+      const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(2 * c) * L::kTile) >> 4);
+      const uint64_t qd = q_desc0 + static_cast<uint64_t>((qb * L::kQBytes) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          ptx::mma_ss(tmem + L::tS(c & 1),
+                      kd + static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4),
+                      qd + static_cast<uint64_t>(((kk / 4) * L::kQBlock + (kk % 4) * 32) >> 4),
+                      idesc_s, kk > 0 ? 1u : 0u);
+        ptx::mma_commit(bar(L::kBarS + (c & 1)));
+        ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * c)));
+        if (last_of_item) ptx::mma_commit(bar(L::kBarQFree + qb));
+      }
+      __syncwarp();
+      return true;
+    };
+    // O (+)= P V_c (P buffer c & 1, V = ring item 2c+1); the first tile of
+    // item k starts the accumulator once the epilogue of item k-1 has read it
+    auto issue_pv = [&](int c, bool first, int k) -> bool {
+      if (!wait(bar(L::kBarP + (c & 1)), (c >> 1) & 1, 45)) return false;
+      if (!wait(bar(L::kBarFull + slot_of(2 * c + 1)), phase_of(2 * c + 1), 46)) return false;
+      if (first && k > 0 && !wait(bar(L::kBarOFree), (k - 1) & 1, 47)) return false;
+      ptx::tc_fence_after();
+      const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(2 * c + 1) * L::kTile) >> 4);
+      const uint64_t pd = p_desc + static_cast<uint64_t>((2 * (c & 1) * L::kPRows) >> 4);
+      if (ptx::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk)
+          ptx::mma_ss(tmem + L::tO,
+                      pd + static_cast<uint64_t>(((kk / 4) * L::kPRows + (kk % 4) * 32) >> 4),
+                      vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
+                      (first && kk == 0) ? 0u : 1u);
+        ptx::mma_commit(bar(L::kBarPV + (c & 1)));
+        ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * c + 1)));
+      }
+      __syncwarp();
+      return true;
+    };
+    // Issue order: S^T(c) and PV(c-1), the PV first when K_c has not landed
+    // yet (the softmax of tile c cannot start before it anyway).
+    bool ok = true;
+    int c = 0, k = 0;
+    bool pending = false;
+    int pend_c = 0, pend_k = 0;
+    bool pend_first = false;
+    for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x) {
+      DecItem it;
+      dec_item(p, w, it);
+      if (it.n == 0) continue;
+      const int qb = k & 1;
+      for (int j = 0; ok && j < it.n; ++j, ++c) {
+        if (pending && !ptx::mbar_test_wait(bar(L::kBarFull + slot_of(2 * c)), phase_of(2 * c))) {
+          if (!(ok = issue_pv(pend_c, pend_first, pend_k))) break;
+          pending = false;
+        }
+        if (j == 0 && !(ok = wait(bar(L::kBarQ + qb), (k >> 1) & 1, 48))) break;
+        if (!(ok = issue_s(c, qb, j == it.n - 1))) break;
+        if (pending && !(ok = issue_pv(pend_c, pend_first, pend_k))) break;
+        pending = true;
+        pend_c = c;
+        pend_k = k;
+        pend_first = j == 0;
+      }
+      ++k;
+    }
+    if (ok && pending) issue_pv(pend_c, pend_first, pend_k);
+    // all MMAs complete before TMEM is released
+    if (ptx::elect_one()) ptx::mma_commit(bar(L::kBarDrain));
+    __syncwarp();
+    bar_wait(bar(L::kBarDrain), 0, wc, 49, false);
+  } else {
+    // ===================================================== softmax (warps 0-3)
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    const int t = threadIdx.x;  // key of the tile, TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int nrows = p.Nq;
+    float* red = reinterpret_cast<float*>(smem + L::kOffRed);
+    float* sums = reinterpret_cast<float*>(smem + L::kOffSum);
+    // this thread's P column in operand block (key / 64) of a buffer: row r at
+    // r/8 * 1024 + (r%8) * 128, 16-byte chunk (key%64)/8 XOR r%8
+    const int kc = t & 63;
+    uint8_t* pcol = smem + L::kOffP + (t >> 6) * L::kPRows + (kc & 7) * 2;
+    const int chunk = kc >> 3;
+    const long long n_rows = static_cast<long long>(p.B) * p.heads * p.Nq;
+    // PV of tile c (from P buffer c & 1) has completed
+    auto wait_pv = [&](int c, int site) {
+      return __all_sync(0xffffffffu,
+                        bar_wait(bar(L::kBarPV + (c & 1)), (c >> 1) & 1, wc, site));
+    };
+    // Epilogue of an item (warp 0, lane = query row): O / l from TMEM to the
+    // output (one split) or the split workspace.  Deferred to the next item's
+    // first tile, whose softmax waits for the item's last PV anyway.
+    auto epilogue = [&](int bh, int sp, float mq, float lq) {
+      ptx::tc_fence_after();
+      const int q = lane;
+      const bool row_ok = q < nrows;
+      const float inv_l = (lq > 0.f) ? 1.0f / lq : 0.f;
+      const float m_use = (mq == -INFINITY) ? 0.f : mq;
+      const float lse_row = (lq > 0.f) ? (m_use + __log2f(lq)) * 0.69314718055994530942f : -INFINITY;
+      const long long row = static_cast<long long>(bh) * p.Nq + q;
+      if (p.n_splits == 1) {
+        T* orow = reinterpret_cast<T*>(p.o) + row * D;
+#pragma unroll 1
+        for (int ch = 0; ch < D / 32; ++ch) {
+          uint32_t o[32];
+          ptx::tmem_ld32(tmem + L::tO + ch * 32, o);
+          ptx::tmem_wait_ld();
+          pin_after_wait<32>(o);
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 v4;
+              v4.x = pack2<BF16>(__uint_as_float(o[8 * i]) * inv_l, __uint_as_float(o[8 * i + 1]) * inv_l);
+              v4.y = pack2<BF16>(__uint_as_float(o[8 * i + 2]) * inv_l, __uint_as_float(o[8 * i + 3]) * inv_l);
+              v4.z = pack2<BF16>(__uint_as_float(o[8 * i + 4]) * inv_l, __uint_as_float(o[8 * i + 5]) * inv_l);
+              v4.w = pack2<BF16>(__uint_as_float(o[8 * i + 6]) * inv_l, __uint_as_float(o[8 * i + 7]) * inv_l);
+              dst[i] = v4;
+            }
+          }
+        }
+        if (row_ok && p.lse != nullptr) p.lse[row] = lse_row;
+      } else {
+        const size_t ws_row = static_cast<size_t>(sp) * n_rows + row;
+        float* wrow = p.ws_o + ws_row * D;
+#pragma unroll 1
+        for (int ch = 0; ch < D / 32; ++ch) {
+          uint32_t o[32];
+          ptx::tmem_ld32(tmem + L::tO + ch * 32, o);
+          ptx::tmem_wait_ld();
+          pin_after_wait<32>(o);
+          if (row_ok) {
+            float4* dst = reinterpret_cast<float4*>(wrow + ch * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                                   __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
+          }
+        }
+        if (row_ok) p.ws_lse[ws_row] = lse_row;
+      }
+      ptx::tc_fence_before();
+    };
+    // `ok` is this thread's status since the last named barrier; every
+    // barrier ANDs it over the four warps, so they stop at the same barrier
+    // (a thread whose wait failed skips its work but still reaches it).
+    bool ok = true;
+    int c = 0;
+    // the item whose epilogue is pending (warp 0): its head, split, and this
+    // lane's row max and row sum
+    bool pend = false;
+    int pend_bh = 0, pend_sp = 0;
+    float pend_m = -INFINITY, pend_l = 0.f;
+    bool run = true;
+    for (int w = blockIdx.x; run && w < n_work; w += gridDim.x) {
+      DecItem it;
+      dec_item(p, w, it);
+      if (it.n == 0) {
+        // a lone split without visible keys: O = 0, LSE = -inf
+        if (p.n_splits == 1 && warp == 0 && lane < nrows) {
+          T* orow = reinterpret_cast<T*>(p.o) + (static_cast<long long>(it.bh) * p.Nq + lane) * D;
+          for (int i = 0; i < D; ++i) orow[i] = T(0.f);
+          if (p.lse != nullptr) p.lse[static_cast<long long>(it.bh) * p.Nq + lane] = -INFINITY;
+        }
+        continue;
+      }
+      float m[R], l[R];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        m[q] = -INFINITY;
+        l[q] = 0.f;
+      }
+      for (int j = 0; j < it.n; ++j, ++c) {
+        const int b = c & 1;
+        float x[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) x[q] = -INFINITY;
+        if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + b), (c >> 1) & 1, wc, 50));
+        if (ok) {
+          ptx::tc_fence_after();
+          uint32_t u[16];
+          ptx::tmem_ld16(tmem + lane_base + L::tS(b), u);
+          ptx::tmem_wait_ld();
+          pin_after_wait<16>(u);
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(L::kBarSFree + b));
+          // scaled scores; -inf for rows past the block and keys a row does not see
+          const int key = (it.jb + j) * kBlockN + t;
+#pragma unroll
+          for (int q = 0; q < R; ++q) {
+            bool vis = q < nrows && key < p.Nk;
+            if (p.causal) vis = vis && key <= q % p.pos_mod + p.causal_off;
+            x[q] = vis ? __uint_as_float(u[q]) * p.scale_log2 : -INFINITY;
+          }
+          // tile maxima of the rows over the warp's 32 keys
+          float v[R];
+#pragma unroll
+          for (int q = 0; q < R; ++q) v[q] = x[q];
+          const float wmax = dec_reduce<R, true>(v, lane);
+          if (!(lane & dec_low<R>())) red[(b * 4 + warp) * R + dec_row<R>(lane)] = wmax;
+        }
+        if (!(ok = ptx::bar_and(L::kNamedBar, 128, ok))) {
+          run = false;
+          break;
+        }
+        float mt[R];
+        {
+          const float4* r4 = reinterpret_cast<const float4*>(red + b * 4 * R);
+#pragma unroll
+          for (int i = 0; i < R / 4; ++i) {
+            const float4 a = r4[i], e = r4[R / 4 + i], f = r4[2 * (R / 4) + i], g = r4[3 * (R / 4) + i];
+            mt[4 * i] = fmaxf(fmaxf(a.x, e.x), fmaxf(f.x, g.x));
+            mt[4 * i + 1] = fmaxf(fmaxf(a.y, e.y), fmaxf(f.y, g.y));
+            mt[4 * i + 2] = fmaxf(fmaxf(a.z, e.z), fmaxf(f.z, g.z));
+            mt[4 * i + 3] = fmaxf(fmaxf(a.w, e.w), fmaxf(f.w, g.w));
+          }
+        }
+        // lazy rescale (the same threshold as the attention kernel); every
+        // thread holds the same m, so the branch is uniform
+        bool any = false;
+        float alpha[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+          const float mn = fmaxf(m[q], mt[q]);
+          const bool grow = mn > m[q] + kRescaleThreshold;
+          alpha[q] = (grow && j > 0) ? ptx::ex2_approx(m[q] - mn) : 1.0f;
+          any |= grow && j > 0;
+          if (grow) m[q] = mn;
+        }
+        if (any) {
+#pragma unroll
+          for (int q = 0; q < R; ++q) l[q] *= alpha[q];
+          // O holds PV of tiles < j once PV(c-1) completed; PV(c) waits for P(c)
+          if (warp == 0 && (ok = wait_pv(c - 1, 52))) {
+            ptx::tc_fence_after();
+            float a = 1.0f;
+#pragma unroll
+            for (int q = 0; q < R; ++q)
+              if (lane == q) a = alpha[q];
+#pragma unroll 1
+            for (int ch = 0; ch < D / 32; ++ch) {
+              uint32_t o[32];
+              ptx::tmem_ld32(tmem + L::tO + ch * 32, o);
+              ptx::tmem_wait_ld();
+              pin_after_wait<32>(o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+              ptx::tmem_st32(tmem + L::tO + ch * 32, o);
+            }
+            ptx::tmem_wait_st();
+            ptx::tc_fence_before();
+          }
+        }
+        if (ok && pend && warp == 0) {
+          // the previous item's last PV (tile c-1) completed: read its O, then
+          // let this item's first PV overwrite the accumulator
+          if ((ok = wait_pv(c - 1, 53))) {
+            epilogue(pend_bh, pend_sp, pend_m, pend_l);
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(bar(L::kBarOFree));
+          }
+          pend = false;
+        }
+        // P buffer b was last read by PV(c-2)
+        if (ok && c >= 2) ok = wait_pv(c - 2, 54);
+        if (ok) {
+#pragma unroll
+          for (int q = 0; q < R; ++q) {
+            const float e = ptx::ex2_approx(x[q] - (m[q] == -INFINITY ? 0.f : m[q]));
+            l[q] += e;
+            *reinterpret_cast<T*>(pcol + 2 * b * L::kPRows + (q >> 3) * 1024 + (q & 7) * 128 +
+                                  ((chunk ^ (q & 7)) << 4)) = T(e);
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive(bar(L::kBarP + b));
+        }
+      }
+      if (!run) break;
+
+      // ---- end of the item: row sums over the 128 keys (the O readout is
+      // deferred to the next item's first tile)
+      const float wsum = dec_reduce<R, false>(l, lane);
+      if (!(lane & dec_low<R>())) sums[warp * R + dec_row<R>(lane)] = wsum;
+      if (!(ok = ptx::bar_and(L::kNamedBar, 128, ok))) break;
+      // warp 0 reads the sums before the next item's first barrier, after
+      // which the other warps may overwrite them
+      if (warp == 0) {
+        pend_l = 0.f;
+        pend_m = -INFINITY;
+        if (lane < R) {
+          pend_l = sums[lane] + sums[R + lane] + sums[2 * R + lane] + sums[3 * R + lane];
+#pragma unroll
+          for (int i = 0; i < R; ++i)
+            if (lane == i) pend_m = m[i];
+        }
+        pend_bh = it.bh;
+        pend_sp = it.sp;
+        pend = true;
+      }
+    }
+    if (ok && pend && warp == 0 && wait_pv(c - 1, 53)) epilogue(pend_bh, pend_sp, pend_m, pend_l);
+  }
+
+  // ---- teardown
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kDecWarpMma) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+template <int D, bool BF16, int R>
+cudaError_t launch_decode_impl(const FwdParams& p, int grid, cudaStream_t stream) {
+  auto kern = fa_decode_kernel<D, BF16, R>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               DecLayout<D>::kDynBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
+  }
+  kern<<<grid, kDecThreads, DecLayout<D>::kDynBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// the smallest row count (4, 8, 16) that holds the block
+template <int D, bool BF16>
+cudaError_t launch_decode_rows(const FwdParams& p, int grid, cudaStream_t stream) {
+  if (p.Nq <= 4) return launch_decode_impl<D, BF16, 4>(p, grid, stream);
+  if (p.Nq <= 8) return launch_decode_impl<D, BF16, 8>(p, grid, stream);
+  return launch_decode_impl<D, BF16, 16>(p, grid, stream);
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
+  if (p.Nq > kDecRows) return cudaErrorInvalidValue;
+  const int n_work = p.B * p.heads * p.n_splits;
+  const int grid = (p.n_ctas > 0 && p.n_ctas < n_work) ? p.n_ctas : n_work;
+  if (head_dim == 64)
+    return bf16 ? launch_decode_rows<64, true>(p, grid, stream)
+                : launch_decode_rows<64, false>(p, grid, stream);
+  return bf16 ? launch_decode_rows<128, true>(p, grid, stream)
+              : launch_decode_rows<128, false>(p, grid, stream);
+}
+
+}  // namespace fa

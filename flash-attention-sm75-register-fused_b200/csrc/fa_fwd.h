@@ -132,6 +132,10 @@ struct alignas(64) BwdParams {
 };
 
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream);
+// Decode kernel (at most 16 query rows per batch*head, dual = 0): one pass
+// over the (batch*head, key split) items; partial results for the combine
+// when n_splits > 1.
+cudaError_t launch_decode(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream);
 // dD / L2 preprocessing (reads O, dO, LSE) and the two backward kernels.
 cudaError_t launch_bwd(const BwdParams& p, const void* o, const void* dout, const float* lse,
                        int head_dim, bool bf16, cudaStream_t stream);

@@ -1007,34 +1007,64 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
   const int q_row = static_cast<int>(row % p.Nq);
   const int total = kv_tiles_for_tile(p, q_row / kBlockM);
   // slots holding data: one per split with tiles (two in dual mode, where an
-  // empty half stores LSE = -inf)
+  // empty half stores LSE = -inf and no O)
   const int ns = min(p.n_splits, (total + p.tiles_per_split - 1) / p.tiles_per_split) *
                  (p.dual ? 2 : 1);
+  // The slots' loads are independent: LSEs one per lane, then the O rows
+  // eight at a time, so a row costs a few memory round trips, not one per slot.
   float mx = -INFINITY;
-  for (int s = 0; s < ns; ++s) mx = fmaxf(mx, p.ws_lse[static_cast<size_t>(s) * n_rows + row]);
+  // first 32 slots' LSEs stay in registers for the weights
+  const float ls0 = lane < ns ? p.ws_lse[static_cast<size_t>(lane) * n_rows + row] : -INFINITY;
+  mx = ls0;
+  for (int s = lane + 32; s < ns; s += 32) mx = fmaxf(mx, p.ws_lse[static_cast<size_t>(s) * n_rows + row]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
   float wsum = 0.f;
   if (mx != -INFINITY) {
-    for (int s = 0; s < ns; ++s) {
-      const float ls = p.ws_lse[static_cast<size_t>(s) * n_rows + row];
-      if (ls == -INFINITY) continue;
-      const float w = expf(ls - mx);
+    for (int s0 = 0; s0 < ns; s0 += 32) {
+      const int cnt = min(32, ns - s0);
+      float w = 0.f;
+      if (lane < cnt) {
+        const float ls = s0 == 0 ? ls0 : p.ws_lse[static_cast<size_t>(s0 + lane) * n_rows + row];
+        w = (ls == -INFINITY) ? 0.f : expf(ls - mx);
+      }
       wsum += w;
-      const float* src = p.ws_o + (static_cast<size_t>(s) * n_rows + row) * D + lane * E;
-      if constexpr (E == 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src);
-        acc[0] = fmaf(w, v.x, acc[0]);
-        acc[1] = fmaf(w, v.y, acc[1]);
-        acc[2] = fmaf(w, v.z, acc[2]);
-        acc[3] = fmaf(w, v.w, acc[3]);
-      } else {
-        const float2 v = *reinterpret_cast<const float2*>(src);
-        acc[0] = fmaf(w, v.x, acc[0]);
-        acc[1] = fmaf(w, v.y, acc[1]);
+      for (int i = 0; i < cnt; i += 8) {
+        float ww[8], v[8][E];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          ww[u] = __shfl_sync(0xffffffffu, w, (i + u) & 31);
+          if (i + u >= cnt) ww[u] = 0.f;
+          const float* src =
+              p.ws_o + (static_cast<size_t>(s0 + i + u) * n_rows + row) * D + lane * E;
+          if (ww[u] != 0.f) {
+            if constexpr (E == 4) {
+              const float4 t = *reinterpret_cast<const float4*>(src);
+              v[u][0] = t.x;
+              v[u][1] = t.y;
+              v[u][2] = t.z;
+              v[u][3] = t.w;
+            } else {
+              const float2 t = *reinterpret_cast<const float2*>(src);
+              v[u][0] = t.x;
+              v[u][1] = t.y;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) v[u][e] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = fmaf(ww[u], v[u][e], acc[e]);
       }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   }
   const float inv = wsum > 0.f ? 1.0f / wsum : 0.f;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -1111,5 +1141,7 @@ cudaError_t read_status(unsigned long long* out, bool reset) {
 
 }  // namespace fa
 
-// Backward kernels (same translation unit: they share the device helpers above).
+// Decode and backward kernels (same translation unit: they share the device
+// helpers above).
+#include "fa_decode_sm100.cuh"
 #include "fa_bwd_sm100.cuh"

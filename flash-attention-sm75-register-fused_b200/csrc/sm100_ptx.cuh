@@ -122,6 +122,22 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Named barrier over `n` threads (warp multiples) with an AND reduction of
+// `v`: every participant gets the same result, so a failure seen by one
+// thread makes all of them leave a loop together.
+__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}\n"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

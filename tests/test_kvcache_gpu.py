@@ -124,3 +124,42 @@ def test_small_workspace_runs_unsplit(sm100):
     o1, l1 = run(q, k, v, 0, workspace=tiny)
     o2, l2 = run(q, k, v, 0, workspace=None)
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
+
+
+# Query blocks of at most 16 rows per (batch, KV head) run the decode kernel
+# (keys on the MMA's M dimension); 17 rows and more the attention kernel.
+DECODE_BLOCKS = [
+    # B, Hq, Hkv, Nq, Nk, d
+    (2, 16, 2, 2, 3000, 128),   # GQA 8 x 2 tokens = 16 rows
+    (1, 12, 4, 4, 900, 64),     # GQA 3 x 4 tokens = 12 rows
+    (3, 4, 4, 16, 2000, 128),   # MHA, 16 tokens
+    (1, 6, 2, 5, 128, 128),     # 15 rows, exactly one K/V tile
+    (2, 8, 8, 3, 50, 64),       # Nk below one tile
+    (1, 17, 1, 1, 500, 64),     # 17 rows: the attention kernel
+]
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("case", DECODE_BLOCKS, ids=[str(c) for c in DECODE_BLOCKS])
+@pytest.mark.parametrize("workspace", [True, None], ids=["split", "unsplit"])
+def test_decode_blocks(sm100, case, mode, workspace):
+    parity(*case, mode=mode, seed=sum(case) + mode, workspace=workspace)
+
+
+def test_decode_blocks_bf16(sm100):
+    parity(2, 16, 2, 2, 3000, 128, mode=1, seed=3, dtype=torch.bfloat16)
+    parity(1, 12, 4, 4, 900, 64, mode=2, seed=4, dtype=torch.bfloat16)
+
+
+def test_decode_many_items_per_cta(sm100):
+    """Enough (head, split) items that every persistent CTA walks several,
+    carrying the K/V ring, the Q double buffer and the deferred epilogue over
+    item boundaries; split and unsplit results agree to rounding."""
+    q, k, v = (t.cuda() for t in _inputs(16, 32, 8, 1, 4096, 128, seed=12))
+    o1, l1 = run(q, k, v, 0, workspace=True)
+    o2, l2 = run(q, k, v, 0, workspace=None)
+    ref_o, ref_lse = orc.attention_fp32(q.cpu()[:2], k.cpu()[:2], v.cpu()[:2])
+    assert orc.check(o1.cpu()[:2], ref_o)["ok"]
+    assert orc.check_lse(l1.cpu()[:2], ref_lse)["ok"]
+    assert (o1.float() - o2.float()).abs().max().item() <= 2e-3
+    assert (l1 - l2).abs().max().item() <= 1e-4
