@@ -10,32 +10,48 @@
 //
 //   S^T = K_j Q^T        M = 128 keys (one TMEM lane each), N = 16 query rows
 //   P   = exp2(S - m)    written by the key's thread into shared memory as
-//                        the K-major A operand [128 rows x 128 keys], double-
-//                        buffered; only the first 16 rows are written, and the
-//                        rows past them overlap the other buffers: they only
-//                        reach O rows past the query block, which are never
-//                        read (so four 16 KB operand blocks fit in 22 KB)
-//   O  += P V_j          M = 128 (the first rows are the queries), N = d
+//                        the K-major B operand [16 rows x 128 keys] (4 KB,
+//                        double-buffered)
+//   O^T += V_j^T P^T     M = d (one TMEM lane per column of O; d = 64 pads M
+//                        to 128 with rows that are never read), N = 16
 //
 // so each thread computes R <= 16 exponentials per 128-key tile (R = the
-// block's rows rounded up to 4, 8 or 16) instead of 128, and S^T is
-// double-buffered in TMEM: the scores of tile j+1 are computed while the
-// softmax of tile j runs.  The rows' maxima are combined across the four
-// softmax warps once per tile (named barrier with an AND of the warps' status,
-// so a failed wait makes all four leave together).
+// block's rows rounded up to 4, 8 or 16) instead of 128, S^T is
+// double-buffered in TMEM (the scores of tile j+1 are computed while the
+// softmax of tile j runs), and the tensor core reads only K, V and the small
+// Q and P operands from shared memory.  The rows' maxima are combined across
+// the four softmax warps once per tile (named barrier with an AND of the
+// warps' status, so a failed wait makes all four leave together).
 //
 // Work items are (batch*head, key split) pairs walked by persistent CTAs; the
 // K/V ring and the Q double buffer carry over from one item to the next.  A
 // split writes a normalised partial O and its LSE for fa_combine_kernel
 // (n_splits > 1), otherwise the final O / LSE.
 //
-// Warps (192 threads): 0-3 softmax (thread t = key t of the tile; warp 0 also
-// rescales O and writes the epilogue, whose rows live in TMEM lanes 0-15),
-// 4 TMA producer, 5 MMA issuer + TMEM owner.
+// Warps (192 threads): 0-3 softmax (thread t = key t of the tile, and column
+// t of O^T for its rescale and the epilogue), 4 TMA producer, 5 MMA issuer +
+// TMEM owner.
+//
+// Development builds (-DFA_TRACE) record per tile c of the CTA (c < 63):
+// producer issued K_c / V_c (0, 1); MMA warp issued S^T(c) / PV(c) (2, 3),
+// saw K_c / V_c land (8, 9) and P(c) (10); softmax warp 0 saw S^T(c) (4),
+// passed the tile's barrier (5), arrived on P(c) (6), saw PV(c-2) done (7);
+// row 63: CTA set up / done (30, 31).
 namespace fa {
 namespace {
 
 constexpr int kDecThreads = 192;
+// critical-path waits poll (bar_wait_spin) instead of suspending
+#ifndef FA_DEC_SPIN
+#define FA_DEC_SPIN 1
+#endif
+__device__ __forceinline__ bool dec_wait(uint32_t bar, uint32_t parity, const WaitCtl& c, int site) {
+#if FA_DEC_SPIN
+  return bar_wait_spin(bar, parity, c, site);
+#else
+  return bar_wait(bar, parity, c, site);
+#endif
+}
 constexpr int kDecRows = 16;  // query rows per item: the S^T MMA's N
 constexpr int kDecWarpLoad = 4;
 constexpr int kDecWarpMma = 5;
@@ -47,15 +63,16 @@ struct DecLayout {
   static constexpr int kSlots = (D == 128) ? 6 : 12;     // K/V ring (192 KB)
   static constexpr int kQBytes = kDecRows * D * 2;       // 16-row Q block
   static constexpr int kQBlock = kDecRows * 128;         // 64-column block of it
-  static constexpr int kPBlock = kBlockM * 128;          // 64 keys x 128 rows of P (16 KB)
-  // Operand block i = 2 * buffer + (key / 64) starts at kOffP + i * kPRows:
-  // its 16 written rows are rows 16 i.. of block 0, the rows past them are
-  // the next blocks' written rows (or never written)
+  // P buffer b: two 64-key blocks of [16 rows x 128 B] at kOffP + b * kPBuf
   static constexpr int kPRows = kDecRows * 128;          // 2 KB
+  static constexpr int kPBuf = 2 * kPRows;
   // shared memory (offsets from a 1024-aligned base)
   static constexpr int kOffP = 0;
-  static constexpr int kOffKV = kOffP + kPBlock + 3 * kPRows;
-  static constexpr int kOffQ = kOffKV + kSlots * kTile;  // Q double buffer
+  static constexpr int kOffKV = kOffP + 2 * kPBuf;
+  // d = 64: the V^T operand's second 64-row block (M = 128) starts one block
+  // past the V tile; for the last slot that is this pad
+  static constexpr int kOffPad = kOffKV + kSlots * kTile;
+  static constexpr int kOffQ = kOffPad + (D == 64 ? kBlockBytes : 0);  // Q double buffer
   static constexpr int kOffRed = kOffQ + 2 * kQBytes;    // [2][4 warps][16] row maxima
   static constexpr int kOffSum = kOffRed + 2 * 4 * kDecRows * 4;  // [4 warps][16] row sums
   static constexpr int kOffBar = kOffSum + 4 * kDecRows * 4;
@@ -70,16 +87,16 @@ struct DecLayout {
   static constexpr int kBarSFree = kBarS + 2;            // 2 (128 arrivals): S^T buffer read
   static constexpr int kBarP = kBarSFree + 2;            // 2 (128 arrivals): P buffer written
   static constexpr int kBarPV = kBarP + 2;               // 2 (MMA commit): PV from P buffer done
-  static constexpr int kBarOFree = kBarPV + 2;           // 1 (1 arrival): epilogue read O
+  static constexpr int kBarOFree = kBarPV + 2;           // 1 (128 arrivals): epilogue read O
   static constexpr int kBarDrain = kBarOFree + 1;        // 1 (MMA commit)
   static constexpr int kNumBars = kBarDrain + 1;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynBytes = kBytes + 1024;
-  // tensor memory: S^T buffers at columns 0 / 16, O at 128
-  static constexpr uint32_t kTmemCols = 256;
+  // tensor memory: S^T buffers at columns 0 / 16, O^T at 32
+  static constexpr uint32_t kTmemCols = 64;
   __host__ __device__ static constexpr uint32_t tS(int b) { return b ? 16u : 0u; }
-  static constexpr uint32_t tO = 128;
+  static constexpr uint32_t tO = 32;
   static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
   static_assert(kOffKV % 1024 == 0 && kOffQ % 1024 == 0 && kTile % 1024 == 0 &&
                     kQBytes % 1024 == 0,
@@ -165,13 +182,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     *abort_flag = ((st >> 32) == p.epoch && (st & 0xffffffffull) != 0ull) ? 1 : 0;
     for (int i = 0; i < L::kNumBars; ++i) {
       const bool all = (i == L::kBarSFree || i == L::kBarSFree + 1 || i == L::kBarP ||
-                        i == L::kBarP + 1);
+                        i == L::kBarP + 1 || i == L::kBarOFree);
       ptx::mbar_init(bar(i), all ? 128u : 1u);
     }
     ptx::fence_barrier_init();
   }
-  // P rows past the query block are not written by the softmax: start them
-  // at zero (their products only reach O rows that are never read)
+  // P rows past the block (R..15) are never written: zero them once
   if (warp < 4) {
     uint4* pz = reinterpret_cast<uint4*>(smem + L::kOffP);
     for (int i = threadIdx.x; i < (L::kOffKV - L::kOffP) / 16; i += 128)
@@ -189,6 +205,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
+  if (threadIdx.x == 0) FA_TRACE_AT(kTraceTiles - 1, 30);
 
   if (warp == kDecWarpLoad) {
     // ===================================================== TMA producer
@@ -216,7 +233,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         for (int i = 0; i < 2 * it.n; ++i, ++ring) {  // K_j, V_j, K_j+1, ...
           const int slot = ring % L::kSlots;
           if (ring >= L::kSlots &&
-              !(ok = bar_wait(bar(L::kBarEmpty + slot), ((ring / L::kSlots) - 1) & 1, wc, 41)))
+              !(ok = dec_wait(bar(L::kBarEmpty + slot), ((ring / L::kSlots) - 1) & 1, wc, 41)))
             break;
           const void* map = (i & 1) ? static_cast<const void*>(&p.tm_v)
                                     : static_cast<const void*>(&p.tm_k);
@@ -226,6 +243,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
           for (int c = 0; c < D / 64; ++c)
             ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
                              (it.jb + (i >> 1)) * kBlockN, it.bh_kv, pol_kv);
+          FA_TRACE_AT(ring >> 1, ring & 1);
         }
         ++k;
       }
@@ -239,21 +257,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     // ===================================================== MMA issuer
     constexpr uint32_t fmt = BF16 ? 1u : 0u;
     constexpr uint32_t idesc_s = ptx::make_idesc_f16(kBlockN, kDecRows, fmt, 0, 0);
-    constexpr uint32_t idesc_pv = ptx::make_idesc_f16(kBlockM, D, fmt, 0, 1);
+    constexpr uint32_t idesc_pv = ptx::make_idesc_f16(128, kDecRows, fmt, 1, 0);
     const uint64_t k_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16, 1024);
     const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
     const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
     const uint64_t p_desc = ptx::smem_desc_sw128(sbase + L::kOffP, 16, 1024);
+    // V as the MN-major A operand of O^T (M = d in 64-row blocks kBlockBytes
+    // apart): the same descriptor as V in the attention kernel's PV
     auto slot_of = [](int item) { return item % L::kSlots; };
     auto phase_of = [](int item) { return static_cast<uint32_t>((item / L::kSlots) & 1); };
     auto wait = [&](uint32_t b, uint32_t ph, int site) {
-      return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
+      return __all_sync(0xffffffffu, dec_wait(b, ph, wc, site));
     };
     // S^T(c) = K_c Q^T into buffer c & 1 (K = ring item 2c, Q buffer qb)
     auto issue_s = [&](int c, int qb, bool last_of_item) -> bool {
       if (!wait(bar(L::kBarFull + slot_of(2 * c)), phase_of(2 * c), 43)) return false;
+      if (lane == 0) FA_TRACE_AT(c, 8);
       if (c >= 2 && !wait(bar(L::kBarSFree + (c & 1)), ((c >> 1) - 1) & 1, 44)) return false;
       ptx::tc_fence_after();
+      if (lane == 0) FA_TRACE_AT(c, 2);
       const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(2 * c) * L::kTile) >> 4);
       const uint64_t qd = q_desc0 + static_cast<uint64_t>((qb * L::kQBytes) >> 4);
       if (ptx::elect_one()) {
@@ -270,22 +292,24 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       __syncwarp();
       return true;
     };
-    // O (+)= P V_c (P buffer c & 1, V = ring item 2c+1); the first tile of
-    // item k starts the accumulator once the epilogue of item k-1 has read it
+    // O^T (+)= V_c^T P^T (P buffer c & 1, V = ring item 2c+1); the first tile
+    // of item k starts the accumulator once the epilogue of item k-1 read it
     auto issue_pv = [&](int c, bool first, int k) -> bool {
       if (!wait(bar(L::kBarP + (c & 1)), (c >> 1) & 1, 45)) return false;
+      if (lane == 0) FA_TRACE_AT(c, 10);
       if (!wait(bar(L::kBarFull + slot_of(2 * c + 1)), phase_of(2 * c + 1), 46)) return false;
+      if (lane == 0) FA_TRACE_AT(c, 9);
       if (first && k > 0 && !wait(bar(L::kBarOFree), (k - 1) & 1, 47)) return false;
       ptx::tc_fence_after();
+      if (lane == 0) FA_TRACE_AT(c, 3);
       const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(2 * c + 1) * L::kTile) >> 4);
-      const uint64_t pd = p_desc + static_cast<uint64_t>((2 * (c & 1) * L::kPRows) >> 4);
+      const uint64_t pd = p_desc + static_cast<uint64_t>(((c & 1) * L::kPBuf) >> 4);
       if (ptx::elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < kBlockN / 16; ++kk)
-          ptx::mma_ss(tmem + L::tO,
+          ptx::mma_ss(tmem + L::tO, vd + static_cast<uint64_t>((kk * 2048) >> 4),
                       pd + static_cast<uint64_t>(((kk / 4) * L::kPRows + (kk % 4) * 32) >> 4),
-                      vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
-                      (first && kk == 0) ? 0u : 1u);
+                      idesc_pv, (first && kk == 0) ? 0u : 1u);
         ptx::mma_commit(bar(L::kBarPV + (c & 1)));
         ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * c + 1)));
       }
@@ -332,7 +356,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     const int nrows = p.Nq;
     float* red = reinterpret_cast<float*>(smem + L::kOffRed);
     float* sums = reinterpret_cast<float*>(smem + L::kOffSum);
-    // this thread's P column in operand block (key / 64) of a buffer: row r at
+    // this thread's P column in the buffer's 64-key block key / 64: row r at
     // r/8 * 1024 + (r%8) * 128, 16-byte chunk (key%64)/8 XOR r%8
     const int kc = t & 63;
     uint8_t* pcol = smem + L::kOffP + (t >> 6) * L::kPRows + (kc & 7) * 2;
@@ -341,82 +365,64 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     // PV of tile c (from P buffer c & 1) has completed
     auto wait_pv = [&](int c, int site) {
       return __all_sync(0xffffffffu,
-                        bar_wait(bar(L::kBarPV + (c & 1)), (c >> 1) & 1, wc, site));
+                        dec_wait(bar(L::kBarPV + (c & 1)), (c >> 1) & 1, wc, site));
     };
-    // Epilogue of an item (warp 0, lane = query row): O / l from TMEM to the
-    // output (one split) or the split workspace.  Deferred to the next item's
-    // first tile, whose softmax waits for the item's last PV anyway.
-    auto epilogue = [&](int bh, int sp, float mq, float lq) {
+    // the item whose epilogue is pending: its head, split, row maxima and sums
+    bool pend = false;
+    int pend_bh = 0, pend_sp = 0;
+    float pend_m[R], pend_l[R];
+    // Epilogue of an item (all four warps; thread t holds column t of O, one
+    // TMEM column per query row): O / l to the output (one split) or the split
+    // workspace, coalesced along d.  Deferred to the next item's first tile,
+    // whose softmax waits for the item's last PV anyway.
+    auto epilogue = [&](int bh, int sp) {
+      const float(&mq)[R] = pend_m;
+      const float(&lq)[R] = pend_l;
       ptx::tc_fence_after();
-      const int q = lane;
-      const bool row_ok = q < nrows;
-      const float inv_l = (lq > 0.f) ? 1.0f / lq : 0.f;
-      const float m_use = (mq == -INFINITY) ? 0.f : mq;
-      const float lse_row = (lq > 0.f) ? (m_use + __log2f(lq)) * 0.69314718055994530942f : -INFINITY;
-      const long long row = static_cast<long long>(bh) * p.Nq + q;
-      if (p.n_splits == 1) {
-        T* orow = reinterpret_cast<T*>(p.o) + row * D;
-#pragma unroll 1
-        for (int ch = 0; ch < D / 32; ++ch) {
-          uint32_t o[32];
-          ptx::tmem_ld32(tmem + L::tO + ch * 32, o);
-          ptx::tmem_wait_ld();
-          pin_after_wait<32>(o);
-          if (row_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v4;
-              v4.x = pack2<BF16>(__uint_as_float(o[8 * i]) * inv_l, __uint_as_float(o[8 * i + 1]) * inv_l);
-              v4.y = pack2<BF16>(__uint_as_float(o[8 * i + 2]) * inv_l, __uint_as_float(o[8 * i + 3]) * inv_l);
-              v4.z = pack2<BF16>(__uint_as_float(o[8 * i + 4]) * inv_l, __uint_as_float(o[8 * i + 5]) * inv_l);
-              v4.w = pack2<BF16>(__uint_as_float(o[8 * i + 6]) * inv_l, __uint_as_float(o[8 * i + 7]) * inv_l);
-              dst[i] = v4;
-            }
-          }
-        }
-        if (row_ok && p.lse != nullptr) p.lse[row] = lse_row;
-      } else {
-        const size_t ws_row = static_cast<size_t>(sp) * n_rows + row;
-        float* wrow = p.ws_o + ws_row * D;
-#pragma unroll 1
-        for (int ch = 0; ch < D / 32; ++ch) {
-          uint32_t o[32];
-          ptx::tmem_ld32(tmem + L::tO + ch * 32, o);
-          ptx::tmem_wait_ld();
-          pin_after_wait<32>(o);
-          if (row_ok) {
-            float4* dst = reinterpret_cast<float4*>(wrow + ch * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
-                                   __uint_as_float(o[4 * i + 2]) * inv_l, __uint_as_float(o[4 * i + 3]) * inv_l);
-          }
-        }
-        if (row_ok) p.ws_lse[ws_row] = lse_row;
-      }
+      uint32_t u[16];
+      ptx::tmem_ld16(tmem + lane_base + L::tO, u);
+      ptx::tmem_wait_ld();
+      pin_after_wait<16>(u);
       ptx::tc_fence_before();
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        if (q >= nrows) break;
+        const float inv_l = (lq[q] > 0.f) ? 1.0f / lq[q] : 0.f;
+        const long long row = static_cast<long long>(bh) * p.Nq + q;
+        const float val = __uint_as_float(u[q]) * inv_l;
+        const bool lse_thread = t == q;
+        float lse_row = 0.f;
+        if (lse_thread) {
+          const float m_use = (mq[q] == -INFINITY) ? 0.f : mq[q];
+          lse_row = (lq[q] > 0.f) ? (m_use + __log2f(lq[q])) * 0.69314718055994530942f : -INFINITY;
+        }
+        if (p.n_splits == 1) {
+          if (t < D) reinterpret_cast<T*>(p.o)[row * D + t] = T(val);
+          if (lse_thread && p.lse != nullptr) p.lse[row] = lse_row;
+        } else {
+          const size_t ws_row = static_cast<size_t>(sp) * n_rows + row;
+          if (t < D) p.ws_o[ws_row * D + t] = val;
+          if (lse_thread) p.ws_lse[ws_row] = lse_row;
+        }
+      }
     };
     // `ok` is this thread's status since the last named barrier; every
     // barrier ANDs it over the four warps, so they stop at the same barrier
     // (a thread whose wait failed skips its work but still reaches it).
     bool ok = true;
     int c = 0;
-    // the item whose epilogue is pending (warp 0): its head, split, and this
-    // lane's row max and row sum
-    bool pend = false;
-    int pend_bh = 0, pend_sp = 0;
-    float pend_m = -INFINITY, pend_l = 0.f;
     bool run = true;
     for (int w = blockIdx.x; run && w < n_work; w += gridDim.x) {
       DecItem it;
       dec_item(p, w, it);
       if (it.n == 0) {
         // a lone split without visible keys: O = 0, LSE = -inf
-        if (p.n_splits == 1 && warp == 0 && lane < nrows) {
-          T* orow = reinterpret_cast<T*>(p.o) + (static_cast<long long>(it.bh) * p.Nq + lane) * D;
-          for (int i = 0; i < D; ++i) orow[i] = T(0.f);
-          if (p.lse != nullptr) p.lse[static_cast<long long>(it.bh) * p.Nq + lane] = -INFINITY;
+        if (p.n_splits == 1) {
+          for (int q = 0; q < nrows; ++q) {
+            const long long row = static_cast<long long>(it.bh) * p.Nq + q;
+            if (t < D) reinterpret_cast<T*>(p.o)[row * D + t] = T(0.f);
+            if (t == q && p.lse != nullptr) p.lse[row] = -INFINITY;
+          }
         }
         continue;
       }
@@ -431,7 +437,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         float x[R];
 #pragma unroll
         for (int q = 0; q < R; ++q) x[q] = -INFINITY;
-        if (ok) ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarS + b), (c >> 1) & 1, wc, 50));
+        if (ok) ok = __all_sync(0xffffffffu, dec_wait(bar(L::kBarS + b), (c >> 1) & 1, wc, 50));
+        if (t == 0) FA_TRACE_AT(c, 4);
         if (ok) {
           ptx::tc_fence_after();
           uint32_t u[16];
@@ -459,6 +466,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
           run = false;
           break;
         }
+        if (t == 0) FA_TRACE_AT(c, 5);
         float mt[R];
         {
           const float4* r4 = reinterpret_cast<const float4*>(red + b * 4 * R);
@@ -486,49 +494,44 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         if (any) {
 #pragma unroll
           for (int q = 0; q < R; ++q) l[q] *= alpha[q];
-          // O holds PV of tiles < j once PV(c-1) completed; PV(c) waits for P(c)
-          if (warp == 0 && (ok = wait_pv(c - 1, 52))) {
+          // O^T holds PV of tiles < j once PV(c-1) completed; PV(c) waits
+          // for P(c).  Column q of this thread's lane scales by alpha[q].
+          if ((ok = wait_pv(c - 1, 52))) {
             ptx::tc_fence_after();
-            float a = 1.0f;
+            uint32_t u[16];
+            ptx::tmem_ld16(tmem + lane_base + L::tO, u);
+            ptx::tmem_wait_ld();
+            pin_after_wait<16>(u);
 #pragma unroll
-            for (int q = 0; q < R; ++q)
-              if (lane == q) a = alpha[q];
-#pragma unroll 1
-            for (int ch = 0; ch < D / 32; ++ch) {
-              uint32_t o[32];
-              ptx::tmem_ld32(tmem + L::tO + ch * 32, o);
-              ptx::tmem_wait_ld();
-              pin_after_wait<32>(o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
-              ptx::tmem_st32(tmem + L::tO + ch * 32, o);
-            }
+            for (int q = 0; q < R; ++q) u[q] = __float_as_uint(__uint_as_float(u[q]) * alpha[q]);
+            ptx::tmem_st16(tmem + lane_base + L::tO, u);
             ptx::tmem_wait_st();
             ptx::tc_fence_before();
           }
         }
-        if (ok && pend && warp == 0) {
+        if (ok && pend) {
           // the previous item's last PV (tile c-1) completed: read its O, then
           // let this item's first PV overwrite the accumulator
           if ((ok = wait_pv(c - 1, 53))) {
-            epilogue(pend_bh, pend_sp, pend_m, pend_l);
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(bar(L::kBarOFree));
+            epilogue(pend_bh, pend_sp);
+            ptx::mbar_arrive(bar(L::kBarOFree));
           }
           pend = false;
         }
         // P buffer b was last read by PV(c-2)
         if (ok && c >= 2) ok = wait_pv(c - 2, 54);
+        if (t == 0) FA_TRACE_AT(c, 7);
         if (ok) {
 #pragma unroll
           for (int q = 0; q < R; ++q) {
             const float e = ptx::ex2_approx(x[q] - (m[q] == -INFINITY ? 0.f : m[q]));
             l[q] += e;
-            *reinterpret_cast<T*>(pcol + 2 * b * L::kPRows + (q >> 3) * 1024 + (q & 7) * 128 +
+            *reinterpret_cast<T*>(pcol + b * L::kPBuf + (q >> 3) * 1024 + (q & 7) * 128 +
                                   ((chunk ^ (q & 7)) << 4)) = T(e);
           }
           ptx::fence_proxy_async_smem();
           ptx::mbar_arrive(bar(L::kBarP + b));
+          if (t == 0) FA_TRACE_AT(c, 6);
         }
       }
       if (!run) break;
@@ -538,28 +541,32 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       const float wsum = dec_reduce<R, false>(l, lane);
       if (!(lane & dec_low<R>())) sums[warp * R + dec_row<R>(lane)] = wsum;
       if (!(ok = ptx::bar_and(L::kNamedBar, 128, ok))) break;
-      // warp 0 reads the sums before the next item's first barrier, after
-      // which the other warps may overwrite them
-      if (warp == 0) {
-        pend_l = 0.f;
-        pend_m = -INFINITY;
-        if (lane < R) {
-          pend_l = sums[lane] + sums[R + lane] + sums[2 * R + lane] + sums[3 * R + lane];
+      // the sums are read before the next item's first barrier, after which
+      // they may be overwritten
+      {
+        const float4* s4 = reinterpret_cast<const float4*>(sums);
 #pragma unroll
-          for (int i = 0; i < R; ++i)
-            if (lane == i) pend_m = m[i];
+        for (int i = 0; i < R / 4; ++i) {
+          const float4 a = s4[i], e = s4[R / 4 + i], f = s4[2 * (R / 4) + i], g = s4[3 * (R / 4) + i];
+          pend_l[4 * i] = (a.x + e.x) + (f.x + g.x);
+          pend_l[4 * i + 1] = (a.y + e.y) + (f.y + g.y);
+          pend_l[4 * i + 2] = (a.z + e.z) + (f.z + g.z);
+          pend_l[4 * i + 3] = (a.w + e.w) + (f.w + g.w);
         }
-        pend_bh = it.bh;
-        pend_sp = it.sp;
-        pend = true;
+#pragma unroll
+        for (int q = 0; q < R; ++q) pend_m[q] = m[q];
       }
+      pend_bh = it.bh;
+      pend_sp = it.sp;
+      pend = true;
     }
-    if (ok && pend && warp == 0 && wait_pv(c - 1, 53)) epilogue(pend_bh, pend_sp, pend_m, pend_l);
+    if (ok && pend && wait_pv(c - 1, 53)) epilogue(pend_bh, pend_sp);
   }
 
   // ---- teardown
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) FA_TRACE_AT(kTraceTiles - 1, 31);
   if (warp == kDecWarpMma) {
     __syncwarp();
     ptx::tc_fence_after();

@@ -155,6 +155,31 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, const Wa
   return bar_wait_slow(bar, parity, c, site, respect_abort);
 }
 
+// Bounded wait that polls without suspending the thread: for short waits on
+// the critical path, where a suspended thread may resume late.  The timer is
+// read every 256 polls.
+__device__ __noinline__ bool bar_wait_spin_slow(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                                int site) {
+  const uint64_t t0 = ptx::global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ptx::mbar_test_wait(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
+      if (*c.abort) return false;
+      if (ptx::global_timer_ns() - t0 > c.timeout_ns) {
+        *c.abort = 1;
+        record_error(c.epoch, FA_ERR_TIMEOUT_BASE + site);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool bar_wait_spin(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                              int site) {
+  if (ptx::mbar_test_wait(bar, parity)) return true;
+  return bar_wait_spin_slow(bar, parity, c, site);
+}
+
 // Make the values produced by tcgen05.ld visible to ordinary instructions
 // only after tcgen05.wait::ld (the empty volatile asm cannot move above it).
 template <int N>
