@@ -206,6 +206,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
   if (threadIdx.x == 0) FA_TRACE_AT(kTraceTiles - 1, 30);
+  // the split combine (a programmatic dependent) may launch now; it waits
+  // for this grid's completion before it reads anything
+  ptx::launch_dependents();
 
   if (warp == kDecWarpLoad) {
     // ===================================================== TMA producer

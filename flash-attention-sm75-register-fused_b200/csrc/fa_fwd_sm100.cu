@@ -1022,13 +1022,16 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 // over the splits that hold data for the row's tile (the same count the
 // attention kernel derives from kv_tiles_for_tile).  Rows without any
 // visible key get O = 0 and LSE = -inf.
-template <int D, bool BF16>
+template <int D, bool BF16, int kBatch>
 __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__ FwdParams p) {
   constexpr int E = D / 32;  // elements per lane
   const long long n_rows = static_cast<long long>(p.B) * p.heads * p.Nq;
   const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= n_rows) return;
   const int lane = threadIdx.x & 31;
+  // launched as a programmatic dependent of the attention kernel: the
+  // partial results are complete and visible after this
+  ptx::grid_dep_wait();
   const int q_row = static_cast<int>(row % p.Nq);
   const int total = kv_tiles_for_tile(p, q_row / kBlockM);
   // slots holding data: one per split with tiles (two in dual mode, where an
@@ -1036,7 +1039,9 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
   const int ns = min(p.n_splits, (total + p.tiles_per_split - 1) / p.tiles_per_split) *
                  (p.dual ? 2 : 1);
   // The slots' loads are independent: LSEs one per lane, then the O rows
-  // eight at a time, so a row costs a few memory round trips, not one per slot.
+  // kBatch at a time (16 for many splits, 8 for few, which keeps registers
+  // and so occupancy up for many rows), so a row costs a few memory round
+  // trips, not one per slot.
   float mx = -INFINITY;
   // first 32 slots' LSEs stay in registers for the weights
   const float ls0 = lane < ns ? p.ws_lse[static_cast<size_t>(lane) * n_rows + row] : -INFINITY;
@@ -1057,10 +1062,10 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
         w = (ls == -INFINITY) ? 0.f : expf(ls - mx);
       }
       wsum += w;
-      for (int i = 0; i < cnt; i += 8) {
-        float ww[8], v[8][E];
+      for (int i = 0; i < cnt; i += kBatch) {
+        float ww[kBatch], v[kBatch][E];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < kBatch; ++u) {
           ww[u] = __shfl_sync(0xffffffffu, w, (i + u) & 31);
           if (i + u >= cnt) ww[u] = 0.f;
           const float* src =
@@ -1083,7 +1088,7 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
           }
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < kBatch; ++u)
 #pragma unroll
           for (int e = 0; e < E; ++e) acc[e] = fmaf(ww[u], v[u][e], acc[e]);
       }
@@ -1137,17 +1142,38 @@ cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t
   return bf16 ? launch_impl<128, true>(p, grid, stream) : launch_impl<128, false>(p, grid, stream);
 }
 
+// The combine is launched as a programmatic dependent of the attention
+// kernel (which allows it early): its CTAs start while the attention kernel
+// drains and wait in griddepcontrol.wait for its results.
+#ifndef FA_COMBINE_PDL
+#define FA_COMBINE_PDL 1
+#endif
 cudaError_t launch_combine(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
   const long long n_rows = static_cast<long long>(p.B) * p.heads * p.Nq;
   const unsigned grid = static_cast<unsigned>((n_rows + 7) / 8);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = FA_COMBINE_PDL;
+  const bool wide = p.n_splits * (p.dual ? 2 : 1) > 8;
   if (head_dim == 64) {
-    if (bf16) fa_combine_kernel<64, true><<<grid, 256, 0, stream>>>(p);
-    else fa_combine_kernel<64, false><<<grid, 256, 0, stream>>>(p);
-  } else {
-    if (bf16) fa_combine_kernel<128, true><<<grid, 256, 0, stream>>>(p);
-    else fa_combine_kernel<128, false><<<grid, 256, 0, stream>>>(p);
+    if (wide)
+      return bf16 ? cudaLaunchKernelEx(&cfg, fa_combine_kernel<64, true, 16>, p)
+                  : cudaLaunchKernelEx(&cfg, fa_combine_kernel<64, false, 16>, p);
+    return bf16 ? cudaLaunchKernelEx(&cfg, fa_combine_kernel<64, true, 8>, p)
+                : cudaLaunchKernelEx(&cfg, fa_combine_kernel<64, false, 8>, p);
   }
-  return cudaGetLastError();
+  if (wide)
+    return bf16 ? cudaLaunchKernelEx(&cfg, fa_combine_kernel<128, true, 16>, p)
+                : cudaLaunchKernelEx(&cfg, fa_combine_kernel<128, false, 16>, p);
+  return bf16 ? cudaLaunchKernelEx(&cfg, fa_combine_kernel<128, true, 8>, p)
+              : cudaLaunchKernelEx(&cfg, fa_combine_kernel<128, false, 8>, p);
 }
 
 int smem_bytes_for(int head_dim) {

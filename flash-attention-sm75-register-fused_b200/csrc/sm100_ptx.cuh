@@ -138,6 +138,17 @@ __device__ __forceinline__ bool bar_and(uint32_t id, uint32_t n, bool v) {
   return r != 0;
 }
 
+// Programmatic dependent launch: the dependent grid (launched with the
+// programmatic-serialization attribute) may start once every CTA of this grid
+// has executed launch_dependents (or exited); grid_dep_wait blocks until the
+// grids it depends on have completed and their memory is visible.
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
