@@ -234,7 +234,8 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   // kernel (keys on the MMA's M dimension, persistent CTAs walking (head, key
   // split) items).  The split is chosen for balance: fewest waves of items
   // over the SMs, each item costing its tiles plus about half a tile of
-  // hand-off; at most 64 splits per row keep the combine short.
+  // hand-off; at most 64 splits per row keep the combine short.  Splits count
+  // 128-key tiles also at d = 64, where the kernel's tiles are 256 keys.
   k.decode = k.rows <= kDecodeRows;
   if (k.decode) {
     k.dual = false;
@@ -244,6 +245,8 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
       for (long long tps = 1; tps <= n; ++tps) {
         const long long ns = (n + tps - 1) / tps;
         if (ns > 64 || (n + ns - 1) / ns != tps) continue;  // balanced splits only
+        // d = 64 tiles are 256 keys: splits start on a 256-key boundary
+        if (d == 64 && (tps & 1) && tps != n) continue;
         const long long waves = (units * ns + sms - 1) / sms;
         const long long cost = waves * (2 * tps + 1);
         if (best_cost < 0 || cost < best_cost) {
@@ -307,9 +310,11 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
 
   fa::FwdParams p;
   const long long bh = static_cast<long long>(B) * k.heads;
+  // the decode kernel's K/V tiles are 256 keys at d = 64 (32 KB, like d = 128)
+  const unsigned kv_box = (k.decode && head_dim == 64) ? 256 : 128;
   if (!make_map(&p.tm_q, Q, head_dim, k.rows, bh, bf16, k.decode ? kDecodeRows : 128) ||
-      !make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16) ||
-      !make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16))
+      !make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16, kv_box) ||
+      !make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16, kv_box))
     return FA_ERR_TENSOR_MAP;
   p.o = O;
   p.o_rs = head_dim;

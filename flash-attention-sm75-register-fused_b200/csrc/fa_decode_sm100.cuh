@@ -58,21 +58,26 @@ constexpr int kDecWarpMma = 5;
 
 template <int D>
 struct DecLayout {
-  static constexpr int kTile = kBlockN * D * 2;          // one K or V tile
-  static constexpr int kBlockBytes = kBlockN * 128;      // 64-column block of a tile
-  static constexpr int kSlots = (D == 128) ? 6 : 12;     // K/V ring (192 KB)
+  // keys per K/V tile (a softmax round): 256 at d = 64, so that every tile
+  // carries 32 KB and the per-round chain is paid per 32 KB; a thread then
+  // owns keys t and t + 128 (two "halves")
+  static constexpr int kKeys = (D == 64) ? 256 : 128;
+  static constexpr int kHalves = kKeys / 128;
+  static constexpr int kTile = kKeys * D * 2;            // one K or V tile (32 KB)
+  static constexpr int kBlockBytes = kKeys * 128;        // 64-column block of a tile
+  static constexpr int kSlots = 6;                       // K/V ring (192 KB)
   static constexpr int kQBytes = kDecRows * D * 2;       // 16-row Q block
   static constexpr int kQBlock = kDecRows * 128;         // 64-column block of it
-  // P buffer b: two 64-key blocks of [16 rows x 128 B] at kOffP + b * kPBuf
+  // P buffer b: kKeys / 64 blocks of [16 rows x 128 B] at kOffP + b * kPBuf
   static constexpr int kPRows = kDecRows * 128;          // 2 KB
-  static constexpr int kPBuf = 2 * kPRows;
-  // shared memory (offsets from a 1024-aligned base)
-  static constexpr int kOffP = 0;
-  static constexpr int kOffKV = kOffP + 2 * kPBuf;
-  // d = 64: the V^T operand's second 64-row block (M = 128) starts one block
-  // past the V tile; for the last slot that is this pad
-  static constexpr int kOffPad = kOffKV + kSlots * kTile;
-  static constexpr int kOffQ = kOffPad + (D == 64 ? kBlockBytes : 0);  // Q double buffer
+  static constexpr int kPBuf = (kKeys / 64) * kPRows;
+  // shared memory (offsets from a 1024-aligned base).  At d = 64 the PV's
+  // unused M rows 64-127 read 16 KB past each K step's V rows, up to 48 KB
+  // past a slot's start: for the last slot that is the P buffers, so the ring
+  // comes first and P right after it.
+  static constexpr int kOffKV = 0;
+  static constexpr int kOffP = kOffKV + kSlots * kTile;
+  static constexpr int kOffQ = kOffP + 2 * kPBuf;  // Q double buffer
   static constexpr int kOffRed = kOffQ + 2 * kQBytes;    // [2][4 warps][16] row maxima
   static constexpr int kOffSum = kOffRed + 2 * 4 * kDecRows * 4;  // [4 warps][16] row sums
   static constexpr int kOffBar = kOffSum + 4 * kDecRows * 4;
@@ -93,13 +98,16 @@ struct DecLayout {
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kDynBytes = kBytes + 1024;
-  // tensor memory: S^T buffers at columns 0 / 16, O^T at 32
-  static constexpr uint32_t kTmemCols = 64;
-  __host__ __device__ static constexpr uint32_t tS(int b) { return b ? 16u : 0u; }
-  static constexpr uint32_t tO = 32;
+  // tensor memory: S^T buffer b at columns 16 * kHalves * b (16 columns per
+  // half), O^T after them
+  static constexpr uint32_t kTmemCols = 32 * kHalves * 2;
+  __host__ __device__ static constexpr uint32_t tS(int b) { return b ? 16u * kHalves : 0u; }
+  static constexpr uint32_t tO = 32 * kHalves;
   static_assert(kDynBytes <= 227 * 1024, "shared memory budget");
+  static_assert(D == 128 || kOffKV + (kSlots - 1) * kTile + 16384 + kKeys * 128 <= kOffQ,
+                "d = 64: the V^T operand's padding rows stay inside the ring and P");
   static_assert(kOffKV % 1024 == 0 && kOffQ % 1024 == 0 && kTile % 1024 == 0 &&
-                    kQBytes % 1024 == 0,
+                    kQBytes % 1024 == 0 && kPBuf % 1024 == 0 && kOffP % 1024 == 0,
                 "128-byte-swizzled operands need 1024-byte alignment");
 };
 
@@ -190,8 +198,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
   // P rows past the block (R..15) are never written: zero them once
   if (warp < 4) {
     uint4* pz = reinterpret_cast<uint4*>(smem + L::kOffP);
-    for (int i = threadIdx.x; i < (L::kOffKV - L::kOffP) / 16; i += 128)
-      pz[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < 2 * L::kPBuf / 16; i += 128) pz[i] = make_uint4(0u, 0u, 0u, 0u);
     ptx::fence_proxy_async_smem();
   }
   __syncthreads();
@@ -233,7 +240,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
           ptx::tma_load_3d(sbase + L::kOffQ + qb * L::kQBytes + c * L::kQBlock, &p.tm_q,
                            bar(L::kBarQ + qb), c * 64, 0, it.bh, pol_q);
         ++q_loads[qb];
-        for (int i = 0; i < 2 * it.n; ++i, ++ring) {  // K_j, V_j, K_j+1, ...
+        const int nr = (it.n + L::kHalves - 1) / L::kHalves;  // rounds of kKeys keys
+        for (int i = 0; i < 2 * nr; ++i, ++ring) {  // K_j, V_j, K_j+1, ...
           const int slot = ring % L::kSlots;
           if (ring >= L::kSlots &&
               !(ok = dec_wait(bar(L::kBarEmpty + slot), ((ring / L::kSlots) - 1) & 1, wc, 41)))
@@ -245,7 +253,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
             ptx::tma_load_3d(dst + c * L::kBlockBytes, map, bar(L::kBarFull + slot), c * 64,
-                             (it.jb + (i >> 1)) * kBlockN, it.bh_kv, pol_kv);
+                             (it.jb + (i >> 1) * L::kHalves) * kBlockN, it.bh_kv, pol_kv);
           FA_TRACE_AT(ring >> 1, ring & 1);
         }
         ++k;
@@ -262,11 +270,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     constexpr uint32_t idesc_s = ptx::make_idesc_f16(kBlockN, kDecRows, fmt, 0, 0);
     constexpr uint32_t idesc_pv = ptx::make_idesc_f16(128, kDecRows, fmt, 1, 0);
     const uint64_t k_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16, 1024);
-    const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
+    const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16384, 1024);
     const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
     const uint64_t p_desc = ptx::smem_desc_sw128(sbase + L::kOffP, 16, 1024);
-    // V as the MN-major A operand of O^T (M = d in 64-row blocks kBlockBytes
-    // apart): the same descriptor as V in the attention kernel's PV
+    // V as the MN-major A operand of O^T: M = d in 64-row blocks 16 KB apart
+    // (d = 128: the tile's second column block, the same descriptor as V in
+    // the attention kernel's PV; d = 64: rows 64-127 of M read the tile's
+    // second half, products that land in O^T lanes that are never read)
     auto slot_of = [](int item) { return item % L::kSlots; };
     auto phase_of = [](int item) { return static_cast<uint32_t>((item / L::kSlots) & 1); };
     auto wait = [&](uint32_t b, uint32_t ph, int site) {
@@ -282,12 +292,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(2 * c) * L::kTile) >> 4);
       const uint64_t qd = q_desc0 + static_cast<uint64_t>((qb * L::kQBytes) >> 4);
       if (ptx::elect_one()) {
+        // half h: keys 128h.. of the tile (rows 16 KB further) into 16 columns
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          ptx::mma_ss(tmem + L::tS(c & 1),
-                      kd + static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4),
-                      qd + static_cast<uint64_t>(((kk / 4) * L::kQBlock + (kk % 4) * 32) >> 4),
-                      idesc_s, kk > 0 ? 1u : 0u);
+        for (int h = 0; h < L::kHalves; ++h)
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            ptx::mma_ss(tmem + L::tS(c & 1) + 16 * h,
+                        kd + static_cast<uint64_t>(
+                                 (h * 16384 + (kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4),
+                        qd + static_cast<uint64_t>(((kk / 4) * L::kQBlock + (kk % 4) * 32) >> 4),
+                        idesc_s, kk > 0 ? 1u : 0u);
         ptx::mma_commit(bar(L::kBarS + (c & 1)));
         ptx::mma_commit(bar(L::kBarEmpty + slot_of(2 * c)));
         if (last_of_item) ptx::mma_commit(bar(L::kBarQFree + qb));
@@ -309,7 +323,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       const uint64_t pd = p_desc + static_cast<uint64_t>(((c & 1) * L::kPBuf) >> 4);
       if (ptx::elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk)
+        for (int kk = 0; kk < L::kKeys / 16; ++kk)
           ptx::mma_ss(tmem + L::tO, vd + static_cast<uint64_t>((kk * 2048) >> 4),
                       pd + static_cast<uint64_t>(((kk / 4) * L::kPRows + (kk % 4) * 32) >> 4),
                       idesc_pv, (first && kk == 0) ? 0u : 1u);
@@ -331,13 +345,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       dec_item(p, w, it);
       if (it.n == 0) continue;
       const int qb = k & 1;
-      for (int j = 0; ok && j < it.n; ++j, ++c) {
+      const int nr = (it.n + L::kHalves - 1) / L::kHalves;
+      for (int j = 0; ok && j < nr; ++j, ++c) {
         if (pending && !ptx::mbar_test_wait(bar(L::kBarFull + slot_of(2 * c)), phase_of(2 * c))) {
           if (!(ok = issue_pv(pend_c, pend_first, pend_k))) break;
           pending = false;
         }
         if (j == 0 && !(ok = wait(bar(L::kBarQ + qb), (k >> 1) & 1, 48))) break;
-        if (!(ok = issue_s(c, qb, j == it.n - 1))) break;
+        if (!(ok = issue_s(c, qb, j == nr - 1))) break;
         if (pending && !(ok = issue_pv(pend_c, pend_first, pend_k))) break;
         pending = true;
         pend_c = c;
@@ -354,7 +369,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
   } else {
     // ===================================================== softmax (warps 0-3)
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    const int t = threadIdx.x;  // key of the tile, TMEM lane
+    const int t = threadIdx.x;  // key of the tile (and t + 128: half 1), TMEM lane
+    constexpr int H = L::kHalves;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const int nrows = p.Nq;
     float* red = reinterpret_cast<float*>(smem + L::kOffRed);
@@ -435,33 +451,43 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         m[q] = -INFINITY;
         l[q] = 0.f;
       }
-      for (int j = 0; j < it.n; ++j, ++c) {
+      const int nr = (it.n + H - 1) / H;  // rounds of kKeys keys
+      for (int j = 0; j < nr; ++j, ++c) {
         const int b = c & 1;
-        float x[R];
+        float x[H][R];
 #pragma unroll
-        for (int q = 0; q < R; ++q) x[q] = -INFINITY;
+        for (int h = 0; h < H; ++h)
+#pragma unroll
+          for (int q = 0; q < R; ++q) x[h][q] = -INFINITY;
         if (ok) ok = __all_sync(0xffffffffu, dec_wait(bar(L::kBarS + b), (c >> 1) & 1, wc, 50));
         if (t == 0) FA_TRACE_AT(c, 4);
         if (ok) {
           ptx::tc_fence_after();
-          uint32_t u[16];
-          ptx::tmem_ld16(tmem + lane_base + L::tS(b), u);
+          uint32_t u[H][16];
+#pragma unroll
+          for (int h = 0; h < H; ++h) ptx::tmem_ld16(tmem + lane_base + L::tS(b) + 16 * h, u[h]);
           ptx::tmem_wait_ld();
-          pin_after_wait<16>(u);
+#pragma unroll
+          for (int h = 0; h < H; ++h) pin_after_wait<16>(u[h]);
           ptx::tc_fence_before();
           ptx::mbar_arrive(bar(L::kBarSFree + b));
-          // scaled scores; -inf for rows past the block and keys a row does not see
-          const int key = (it.jb + j) * kBlockN + t;
+          // scaled scores; -inf for rows past the block and keys a row does not
+          // see (keys past the split's tiles in a round are past Nk or past
+          // every row's causal limit)
 #pragma unroll
-          for (int q = 0; q < R; ++q) {
-            bool vis = q < nrows && key < p.Nk;
-            if (p.causal) vis = vis && key <= q % p.pos_mod + p.causal_off;
-            x[q] = vis ? __uint_as_float(u[q]) * p.scale_log2 : -INFINITY;
+          for (int h = 0; h < H; ++h) {
+            const int key = (it.jb + j * H) * kBlockN + 128 * h + t;
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+              bool vis = q < nrows && key < p.Nk;
+              if (p.causal) vis = vis && key <= q % p.pos_mod + p.causal_off;
+              x[h][q] = vis ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
+            }
           }
-          // tile maxima of the rows over the warp's 32 keys
+          // tile maxima of the rows over the warp's keys
           float v[R];
 #pragma unroll
-          for (int q = 0; q < R; ++q) v[q] = x[q];
+          for (int q = 0; q < R; ++q) v[q] = H == 2 ? fmaxf(x[0][q], x[H - 1][q]) : x[0][q];
           const float wmax = dec_reduce<R, true>(v, lane);
           if (!(lane & dec_low<R>())) red[(b * 4 + warp) * R + dec_row<R>(lane)] = wmax;
         }
@@ -526,12 +552,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         if (t == 0) FA_TRACE_AT(c, 7);
         if (ok) {
 #pragma unroll
-          for (int q = 0; q < R; ++q) {
-            const float e = ptx::ex2_approx(x[q] - (m[q] == -INFINITY ? 0.f : m[q]));
-            l[q] += e;
-            *reinterpret_cast<T*>(pcol + b * L::kPBuf + (q >> 3) * 1024 + (q & 7) * 128 +
-                                  ((chunk ^ (q & 7)) << 4)) = T(e);
-          }
+          for (int h = 0; h < H; ++h)
+#pragma unroll
+            for (int q = 0; q < R; ++q) {
+              const float e = ptx::ex2_approx(x[h][q] - (m[q] == -INFINITY ? 0.f : m[q]));
+              l[q] += e;
+              *reinterpret_cast<T*>(pcol + b * L::kPBuf + h * 2 * L::kPRows + (q >> 3) * 1024 +
+                                    (q & 7) * 128 + ((chunk ^ (q & 7)) << 4)) = T(e);
+            }
           ptx::fence_proxy_async_smem();
           ptx::mbar_arrive(bar(L::kBarP + b));
           if (t == 0) FA_TRACE_AT(c, 6);
