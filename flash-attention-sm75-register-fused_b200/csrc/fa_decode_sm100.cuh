@@ -373,6 +373,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     constexpr int H = L::kHalves;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const int nrows = p.Nq;
+    // keys below vis_all are visible to every row of the block (row 0 has
+    // the smallest causal limit, causal_off)
+    const int vis_all = p.causal ? min(p.Nk, max(p.causal_off + 1, 0)) : p.Nk;
     float* red = reinterpret_cast<float*>(smem + L::kOffRed);
     float* sums = reinterpret_cast<float*>(smem + L::kOffSum);
     // this thread's P column in the buffer's 64-key block key / 64: row r at
@@ -473,15 +476,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
           ptx::mbar_arrive(bar(L::kBarSFree + b));
           // scaled scores; -inf for rows past the block and keys a row does not
           // see (keys past the split's tiles in a round are past Nk or past
-          // every row's causal limit)
+          // every row's causal limit).  Tiles below vis_all hold no such key:
+          // only rows past the block are masked there.
+          const int key0 = (it.jb + j * H) * kBlockN;
+          if (key0 + L::kKeys <= vis_all) {
 #pragma unroll
-          for (int h = 0; h < H; ++h) {
-            const int key = (it.jb + j * H) * kBlockN + 128 * h + t;
+            for (int h = 0; h < H; ++h)
 #pragma unroll
-            for (int q = 0; q < R; ++q) {
-              bool vis = q < nrows && key < p.Nk;
-              if (p.causal) vis = vis && key <= q % p.pos_mod + p.causal_off;
-              x[h][q] = vis ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
+              for (int q = 0; q < R; ++q)
+                x[h][q] = q < nrows ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
+          } else {
+#pragma unroll
+            for (int h = 0; h < H; ++h) {
+              const int key = key0 + 128 * h + t;
+#pragma unroll
+              for (int q = 0; q < R; ++q) {
+                bool vis = q < nrows && key < p.Nk;
+                if (p.causal) vis = vis && key <= q % p.pos_mod + p.causal_off;
+                x[h][q] = vis ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
+              }
             }
           }
           // tile maxima of the rows over the warp's keys
@@ -509,33 +522,37 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
           }
         }
         // lazy rescale (the same threshold as the attention kernel); every
-        // thread holds the same m, so the branch is uniform
-        bool any = false;
-        float alpha[R];
+        // thread holds the same m, so the branches are uniform.  A row's max
+        // moves only when it grows past the threshold, which after the first
+        // tile is rare: the factors are computed in that branch only.
+        bool grow_any = false;
 #pragma unroll
-        for (int q = 0; q < R; ++q) {
-          const float mn = fmaxf(m[q], mt[q]);
-          const bool grow = mn > m[q] + kRescaleThreshold;
-          alpha[q] = (grow && j > 0) ? ptx::ex2_approx(m[q] - mn) : 1.0f;
-          any |= grow && j > 0;
-          if (grow) m[q] = mn;
-        }
-        if (any) {
+        for (int q = 0; q < R; ++q) grow_any |= mt[q] > m[q] + kRescaleThreshold;
+        if (grow_any) {
+          float alpha[R];
 #pragma unroll
-          for (int q = 0; q < R; ++q) l[q] *= alpha[q];
-          // O^T holds PV of tiles < j once PV(c-1) completed; PV(c) waits
-          // for P(c).  Column q of this thread's lane scales by alpha[q].
-          if ((ok = wait_pv(c - 1, 52))) {
-            ptx::tc_fence_after();
-            uint32_t u[16];
-            ptx::tmem_ld16(tmem + lane_base + L::tO, u);
-            ptx::tmem_wait_ld();
-            pin_after_wait<16>(u);
+          for (int q = 0; q < R; ++q) {
+            const bool grow = mt[q] > m[q] + kRescaleThreshold;
+            alpha[q] = (grow && j > 0) ? ptx::ex2_approx(m[q] - mt[q]) : 1.0f;
+            if (grow) m[q] = mt[q];
+          }
+          if (j > 0) {
 #pragma unroll
-            for (int q = 0; q < R; ++q) u[q] = __float_as_uint(__uint_as_float(u[q]) * alpha[q]);
-            ptx::tmem_st16(tmem + lane_base + L::tO, u);
-            ptx::tmem_wait_st();
-            ptx::tc_fence_before();
+            for (int q = 0; q < R; ++q) l[q] *= alpha[q];
+            // O^T holds PV of tiles < j once PV(c-1) completed; PV(c) waits
+            // for P(c).  Column q of this thread's lane scales by alpha[q].
+            if ((ok = wait_pv(c - 1, 52))) {
+              ptx::tc_fence_after();
+              uint32_t u[16];
+              ptx::tmem_ld16(tmem + lane_base + L::tO, u);
+              ptx::tmem_wait_ld();
+              pin_after_wait<16>(u);
+#pragma unroll
+              for (int q = 0; q < R; ++q) u[q] = __float_as_uint(__uint_as_float(u[q]) * alpha[q]);
+              ptx::tmem_st16(tmem + lane_base + L::tO, u);
+              ptx::tmem_wait_st();
+              ptx::tc_fence_before();
+            }
           }
         }
         if (ok && pend) {
