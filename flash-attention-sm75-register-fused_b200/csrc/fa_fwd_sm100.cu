@@ -337,9 +337,33 @@ struct WorkItem {
 // O element offset (rows o_rs apart) and LSE index (rows 1 apart) of local
 // query row 0 of work item w, and its number of query rows.  Recomputed for
 // the epilogue rather than kept live through the softmax loop.
+// Work item (without its split) -> (Q pair from the heavy end, batch*head).
+// Non-causal: head-major.  Causal pairs differ in work: items go pair-major
+// within groups of kFwdHeadGroup heads and head-major across groups, so each
+// group starts its heaviest pairs first while the CTAs that run together
+// still share a few heads' K/V in L2 (measured: C4 causal +12 % against
+// head-major order with groups of 8, +5 % with 4; fully pair-major order
+// loses the L2 sharing and was slower).
+constexpr int kFwdHeadGroup = 8;
+__device__ __forceinline__ void item_order(const FwdParams& p, int rest, int& qp_heavy, int& bh) {
+  if (!p.causal) {
+    qp_heavy = rest % p.n_qpairs;
+    bh = rest / p.n_qpairs;
+    return;
+  }
+  const int n_heads = p.B * p.heads;
+  const int per_group = kFwdHeadGroup * p.n_qpairs;
+  const int g = rest / per_group;
+  const int r = rest % per_group;
+  const int g_heads = min(kFwdHeadGroup, n_heads - g * kFwdHeadGroup);
+  qp_heavy = r / g_heads;
+  bh = g * kFwdHeadGroup + r % g_heads;
+}
+
 __device__ __forceinline__ void item_out(const FwdParams& p, int w, long long& o_row0,
                                          long long& lse_row0, int& nq) {
-  const int bh = (w / p.n_splits) / p.n_qpairs;
+  int qp_unused, bh;
+  item_order(p, w / p.n_splits, qp_unused, bh);
   if (p.ranges == 0) {
     nq = p.Nq;
     lse_row0 = static_cast<long long>(bh) * p.Nq;
@@ -361,10 +385,9 @@ __device__ __forceinline__ void item_out(const FwdParams& p, int w, long long& o
 
 __device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem& it) {
   it.sp = w % p.n_splits;
-  const int rest = w / p.n_splits;
-  it.bh = rest / p.n_qpairs;
-  int qp = rest % p.n_qpairs;
-  if (p.causal) qp = p.n_qpairs - 1 - qp;  // causal pairs of one head: heaviest first
+  int qp;
+  item_order(p, w / p.n_splits, qp, it.bh);
+  if (p.causal) qp = p.n_qpairs - 1 - qp;  // causal: heaviest pairs first
   it.qp = qp;
   const int b = it.bh / p.heads;
   const int hq = it.bh % p.heads;
