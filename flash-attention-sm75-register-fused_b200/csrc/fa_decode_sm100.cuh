@@ -28,9 +28,10 @@
 // split writes a normalised partial O and its LSE for fa_combine_kernel
 // (n_splits > 1), otherwise the final O / LSE.
 //
-// Warps (192 threads): 0-3 softmax (thread t = key t of the tile, and column
-// t of O^T for its rescale and the epilogue), 4 TMA producer, 5 MMA issuer +
-// TMEM owner.
+// Warps: 0-3 softmax (thread t = key t of the tile, and column t of O^T for
+// its rescale and the epilogue; 16-row blocks: warps 0-7, warp w and w + 4
+// taking rows 0-7 / 8-15 of the same keys), then the TMA producer and the
+// MMA issuer + TMEM owner (192 or 320 threads).
 //
 // Development builds (-DFA_TRACE) record per tile c of the CTA (c < 63):
 // producer issued K_c / V_c (0, 1); MMA warp issued S^T(c) / PV(c) (2, 3),
@@ -40,7 +41,7 @@
 namespace fa {
 namespace {
 
-constexpr int kDecThreads = 192;
+
 // critical-path waits poll (bar_wait_spin) instead of suspending
 #ifndef FA_DEC_SPIN
 #define FA_DEC_SPIN 1
@@ -53,8 +54,6 @@ __device__ __forceinline__ bool dec_wait(uint32_t bar, uint32_t parity, const Wa
 #endif
 }
 constexpr int kDecRows = 16;  // query rows per item: the S^T MMA's N
-constexpr int kDecWarpLoad = 4;
-constexpr int kDecWarpMma = 5;
 
 template <int D>
 struct DecLayout {
@@ -169,9 +168,16 @@ __device__ __forceinline__ int dec_row(int lane) {
   return row;
 }
 
-template <int D, bool BF16, int R>
-__global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_constant__ FwdParams p) {
+// RS = 2 splits a block's rows between two softmax warpgroups (warps w and
+// w + 4 read the same TMEM lanes, i.e. the same keys, and different row
+// columns), halving each thread's exponentials for 16-row blocks.
+template <int D, bool BF16, int R, int RS>
+__global__ void __launch_bounds__(32 * (4 * RS + 2), 1) fa_decode_kernel(const __grid_constant__ FwdParams p) {
   static_assert(R == 4 || R == 8 || R == 16, "rows per block");
+  static_assert(RS == 1 || (RS == 2 && R == 16), "row split");
+  constexpr int kDecWarpLoad = 4 * RS;
+  constexpr int kDecWarpMma = 4 * RS + 1;
+  constexpr uint32_t kSoftThreads = 128 * RS;
   using L = DecLayout<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -191,14 +197,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     for (int i = 0; i < L::kNumBars; ++i) {
       const bool all = (i == L::kBarSFree || i == L::kBarSFree + 1 || i == L::kBarP ||
                         i == L::kBarP + 1 || i == L::kBarOFree);
-      ptx::mbar_init(bar(i), all ? 128u : 1u);
+      ptx::mbar_init(bar(i), all ? kSoftThreads : 1u);
     }
     ptx::fence_barrier_init();
   }
   // P rows past the block (R..15) are never written: zero them once
-  if (warp < 4) {
+  if (warp < 4 * RS) {
     uint4* pz = reinterpret_cast<uint4*>(smem + L::kOffP);
-    for (int i = threadIdx.x; i < 2 * L::kPBuf / 16; i += 128) pz[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < 2 * L::kPBuf / 16; i += kSoftThreads) pz[i] = make_uint4(0u, 0u, 0u, 0u);
     ptx::fence_proxy_async_smem();
   }
   __syncthreads();
@@ -367,11 +373,22 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     __syncwarp();
     bar_wait(bar(L::kBarDrain), 0, wc, 49, false);
   } else {
-    // ===================================================== softmax (warps 0-3)
+    // ===================================================== softmax (warps 0 .. 4 RS - 1)
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    const int t = threadIdx.x;  // key of the tile (and t + 128: half 1), TMEM lane
+    const int t = threadIdx.x & 127;  // key of the tile (and t + 128: half 1), TMEM lane
     constexpr int H = L::kHalves;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    constexpr int RP = R / RS;        // rows of this thread: q0 .. q0 + RP - 1
+    const int q0 = (warp >> 2) * RP;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    // this thread's RP row columns starting at TMEM column `col` (+ q0)
+    auto ld_rows = [&](uint32_t col, uint32_t (&r)[16]) {
+      if constexpr (RS == 1) ptx::tmem_ld16(tmem + lane_base + col, r);
+      else ptx::tmem_ld8(tmem + lane_base + col + q0, r);
+    };
+    auto st_rows = [&](uint32_t col, const uint32_t (&r)[16]) {
+      if constexpr (RS == 1) ptx::tmem_st16(tmem + lane_base + col, r);
+      else ptx::tmem_st8(tmem + lane_base + col + q0, r);
+    };
     const int nrows = p.Nq;
     // keys below vis_all are visible to every row of the block (row 0 has
     // the smallest causal limit, causal_off)
@@ -392,27 +409,28 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
     // the item whose epilogue is pending: its head, split, row maxima and sums
     bool pend = false;
     int pend_bh = 0, pend_sp = 0;
-    float pend_m[R], pend_l[R];
-    // Epilogue of an item (all four warps; thread t holds column t of O, one
-    // TMEM column per query row): O / l to the output (one split) or the split
+    float pend_m[RP], pend_l[RP];
+    // Epilogue of an item (all softmax warps; thread t holds column t of O,
+    // one TMEM column per query row, its RP rows): O / l to the output (one split) or the split
     // workspace, coalesced along d.  Deferred to the next item's first tile,
     // whose softmax waits for the item's last PV anyway.
     auto epilogue = [&](int bh, int sp) {
-      const float(&mq)[R] = pend_m;
-      const float(&lq)[R] = pend_l;
+      const float(&mq)[RP] = pend_m;
+      const float(&lq)[RP] = pend_l;
       ptx::tc_fence_after();
       uint32_t u[16];
-      ptx::tmem_ld16(tmem + lane_base + L::tO, u);
+      ld_rows(L::tO, u);
       ptx::tmem_wait_ld();
       pin_after_wait<16>(u);
       ptx::tc_fence_before();
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
-        if (q >= nrows) break;
+      for (int q = 0; q < RP; ++q) {
+        const int qg = q0 + q;
+        if (qg >= nrows) break;
         const float inv_l = (lq[q] > 0.f) ? 1.0f / lq[q] : 0.f;
-        const long long row = static_cast<long long>(bh) * p.Nq + q;
+        const long long row = static_cast<long long>(bh) * p.Nq + qg;
         const float val = __uint_as_float(u[q]) * inv_l;
-        const bool lse_thread = t == q;
+        const bool lse_thread = t == qg;
         float lse_row = 0.f;
         if (lse_thread) {
           const float m_use = (mq[q] == -INFINITY) ? 0.f : mq[q];
@@ -429,7 +447,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       }
     };
     // `ok` is this thread's status since the last named barrier; every
-    // barrier ANDs it over the four warps, so they stop at the same barrier
+    // barrier ANDs it over the softmax warps, so they stop at the same barrier
     // (a thread whose wait failed skips its work but still reaches it).
     bool ok = true;
     int c = 0;
@@ -440,35 +458,35 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
       if (it.n == 0) {
         // a lone split without visible keys: O = 0, LSE = -inf
         if (p.n_splits == 1) {
-          for (int q = 0; q < nrows; ++q) {
-            const long long row = static_cast<long long>(it.bh) * p.Nq + q;
+          for (int qg = q0; qg < min(nrows, q0 + RP); ++qg) {
+            const long long row = static_cast<long long>(it.bh) * p.Nq + qg;
             if (t < D) reinterpret_cast<T*>(p.o)[row * D + t] = T(0.f);
-            if (t == q && p.lse != nullptr) p.lse[row] = -INFINITY;
+            if (t == qg && p.lse != nullptr) p.lse[row] = -INFINITY;
           }
         }
         continue;
       }
-      float m[R], l[R];
+      float m[RP], l[RP];
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
+      for (int q = 0; q < RP; ++q) {
         m[q] = -INFINITY;
         l[q] = 0.f;
       }
       const int nr = (it.n + H - 1) / H;  // rounds of kKeys keys
       for (int j = 0; j < nr; ++j, ++c) {
         const int b = c & 1;
-        float x[H][R];
+        float x[H][RP];
 #pragma unroll
         for (int h = 0; h < H; ++h)
 #pragma unroll
-          for (int q = 0; q < R; ++q) x[h][q] = -INFINITY;
+          for (int q = 0; q < RP; ++q) x[h][q] = -INFINITY;
         if (ok) ok = __all_sync(0xffffffffu, dec_wait(bar(L::kBarS + b), (c >> 1) & 1, wc, 50));
-        if (t == 0) FA_TRACE_AT(c, 4);
+        if (threadIdx.x == 0) FA_TRACE_AT(c, 4);
         if (ok) {
           ptx::tc_fence_after();
           uint32_t u[H][16];
 #pragma unroll
-          for (int h = 0; h < H; ++h) ptx::tmem_ld16(tmem + lane_base + L::tS(b) + 16 * h, u[h]);
+          for (int h = 0; h < H; ++h) ld_rows(L::tS(b) + 16 * h, u[h]);
           ptx::tmem_wait_ld();
 #pragma unroll
           for (int h = 0; h < H; ++h) pin_after_wait<16>(u[h]);
@@ -483,38 +501,39 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
 #pragma unroll
             for (int h = 0; h < H; ++h)
 #pragma unroll
-              for (int q = 0; q < R; ++q)
-                x[h][q] = q < nrows ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
+              for (int q = 0; q < RP; ++q)
+                x[h][q] = q0 + q < nrows ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
           } else {
 #pragma unroll
             for (int h = 0; h < H; ++h) {
               const int key = key0 + 128 * h + t;
 #pragma unroll
-              for (int q = 0; q < R; ++q) {
-                bool vis = q < nrows && key < p.Nk;
-                if (p.causal) vis = vis && key <= q % p.pos_mod + p.causal_off;
+              for (int q = 0; q < RP; ++q) {
+                bool vis = q0 + q < nrows && key < p.Nk;
+                if (p.causal) vis = vis && key <= (q0 + q) % p.pos_mod + p.causal_off;
                 x[h][q] = vis ? __uint_as_float(u[h][q]) * p.scale_log2 : -INFINITY;
               }
             }
           }
           // tile maxima of the rows over the warp's keys
-          float v[R];
+          float v[RP];
 #pragma unroll
-          for (int q = 0; q < R; ++q) v[q] = H == 2 ? fmaxf(x[0][q], x[H - 1][q]) : x[0][q];
-          const float wmax = dec_reduce<R, true>(v, lane);
-          if (!(lane & dec_low<R>())) red[(b * 4 + warp) * R + dec_row<R>(lane)] = wmax;
+          for (int q = 0; q < RP; ++q) v[q] = H == 2 ? fmaxf(x[0][q], x[H - 1][q]) : x[0][q];
+          const float wmax = dec_reduce<RP, true>(v, lane);
+          if (!(lane & dec_low<RP>())) red[(b * 4 * RS + warp) * RP + dec_row<RP>(lane)] = wmax;
         }
-        if (!(ok = ptx::bar_and(L::kNamedBar, 128, ok))) {
+        if (!(ok = ptx::bar_and(L::kNamedBar, kSoftThreads, ok))) {
           run = false;
           break;
         }
-        if (t == 0) FA_TRACE_AT(c, 5);
-        float mt[R];
+        if (threadIdx.x == 0) FA_TRACE_AT(c, 5);
+        float mt[RP];
         {
-          const float4* r4 = reinterpret_cast<const float4*>(red + b * 4 * R);
+          // the four warps that hold this thread's rows
+          const float4* r4 = reinterpret_cast<const float4*>(red + (b * 4 * RS + (warp & ~3)) * RP);
 #pragma unroll
-          for (int i = 0; i < R / 4; ++i) {
-            const float4 a = r4[i], e = r4[R / 4 + i], f = r4[2 * (R / 4) + i], g = r4[3 * (R / 4) + i];
+          for (int i = 0; i < RP / 4; ++i) {
+            const float4 a = r4[i], e = r4[RP / 4 + i], f = r4[2 * (RP / 4) + i], g = r4[3 * (RP / 4) + i];
             mt[4 * i] = fmaxf(fmaxf(a.x, e.x), fmaxf(f.x, g.x));
             mt[4 * i + 1] = fmaxf(fmaxf(a.y, e.y), fmaxf(f.y, g.y));
             mt[4 * i + 2] = fmaxf(fmaxf(a.z, e.z), fmaxf(f.z, g.z));
@@ -527,29 +546,29 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         // tile is rare: the factors are computed in that branch only.
         bool grow_any = false;
 #pragma unroll
-        for (int q = 0; q < R; ++q) grow_any |= mt[q] > m[q] + kRescaleThreshold;
+        for (int q = 0; q < RP; ++q) grow_any |= mt[q] > m[q] + kRescaleThreshold;
         if (grow_any) {
-          float alpha[R];
+          float alpha[RP];
 #pragma unroll
-          for (int q = 0; q < R; ++q) {
+          for (int q = 0; q < RP; ++q) {
             const bool grow = mt[q] > m[q] + kRescaleThreshold;
             alpha[q] = (grow && j > 0) ? ptx::ex2_approx(m[q] - mt[q]) : 1.0f;
             if (grow) m[q] = mt[q];
           }
           if (j > 0) {
 #pragma unroll
-            for (int q = 0; q < R; ++q) l[q] *= alpha[q];
+            for (int q = 0; q < RP; ++q) l[q] *= alpha[q];
             // O^T holds PV of tiles < j once PV(c-1) completed; PV(c) waits
             // for P(c).  Column q of this thread's lane scales by alpha[q].
             if ((ok = wait_pv(c - 1, 52))) {
               ptx::tc_fence_after();
               uint32_t u[16];
-              ptx::tmem_ld16(tmem + lane_base + L::tO, u);
+              ld_rows(L::tO, u);
               ptx::tmem_wait_ld();
               pin_after_wait<16>(u);
 #pragma unroll
-              for (int q = 0; q < R; ++q) u[q] = __float_as_uint(__uint_as_float(u[q]) * alpha[q]);
-              ptx::tmem_st16(tmem + lane_base + L::tO, u);
+              for (int q = 0; q < RP; ++q) u[q] = __float_as_uint(__uint_as_float(u[q]) * alpha[q]);
+              st_rows(L::tO, u);
               ptx::tmem_wait_st();
               ptx::tc_fence_before();
             }
@@ -566,43 +585,44 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
         }
         // P buffer b was last read by PV(c-2)
         if (ok && c >= 2) ok = wait_pv(c - 2, 54);
-        if (t == 0) FA_TRACE_AT(c, 7);
+        if (threadIdx.x == 0) FA_TRACE_AT(c, 7);
         if (ok) {
 #pragma unroll
           for (int h = 0; h < H; ++h)
 #pragma unroll
-            for (int q = 0; q < R; ++q) {
+            for (int q = 0; q < RP; ++q) {
+              const int qg = q0 + q;
               const float e = ptx::ex2_approx(x[h][q] - (m[q] == -INFINITY ? 0.f : m[q]));
               l[q] += e;
-              *reinterpret_cast<T*>(pcol + b * L::kPBuf + h * 2 * L::kPRows + (q >> 3) * 1024 +
-                                    (q & 7) * 128 + ((chunk ^ (q & 7)) << 4)) = T(e);
+              *reinterpret_cast<T*>(pcol + b * L::kPBuf + h * 2 * L::kPRows + (qg >> 3) * 1024 +
+                                    (qg & 7) * 128 + ((chunk ^ (qg & 7)) << 4)) = T(e);
             }
           ptx::fence_proxy_async_smem();
           ptx::mbar_arrive(bar(L::kBarP + b));
-          if (t == 0) FA_TRACE_AT(c, 6);
+          if (threadIdx.x == 0) FA_TRACE_AT(c, 6);
         }
       }
       if (!run) break;
 
       // ---- end of the item: row sums over the 128 keys (the O readout is
       // deferred to the next item's first tile)
-      const float wsum = dec_reduce<R, false>(l, lane);
-      if (!(lane & dec_low<R>())) sums[warp * R + dec_row<R>(lane)] = wsum;
-      if (!(ok = ptx::bar_and(L::kNamedBar, 128, ok))) break;
+      const float wsum = dec_reduce<RP, false>(l, lane);
+      if (!(lane & dec_low<RP>())) sums[warp * RP + dec_row<RP>(lane)] = wsum;
+      if (!(ok = ptx::bar_and(L::kNamedBar, kSoftThreads, ok))) break;
       // the sums are read before the next item's first barrier, after which
       // they may be overwritten
       {
-        const float4* s4 = reinterpret_cast<const float4*>(sums);
+        const float4* s4 = reinterpret_cast<const float4*>(sums + (warp & ~3) * RP);
 #pragma unroll
-        for (int i = 0; i < R / 4; ++i) {
-          const float4 a = s4[i], e = s4[R / 4 + i], f = s4[2 * (R / 4) + i], g = s4[3 * (R / 4) + i];
+        for (int i = 0; i < RP / 4; ++i) {
+          const float4 a = s4[i], e = s4[RP / 4 + i], f = s4[2 * (RP / 4) + i], g = s4[3 * (RP / 4) + i];
           pend_l[4 * i] = (a.x + e.x) + (f.x + g.x);
           pend_l[4 * i + 1] = (a.y + e.y) + (f.y + g.y);
           pend_l[4 * i + 2] = (a.z + e.z) + (f.z + g.z);
           pend_l[4 * i + 3] = (a.w + e.w) + (f.w + g.w);
         }
 #pragma unroll
-        for (int q = 0; q < R; ++q) pend_m[q] = m[q];
+        for (int q = 0; q < RP; ++q) pend_m[q] = m[q];
       }
       pend_bh = it.bh;
       pend_sp = it.sp;
@@ -622,9 +642,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) fa_decode_kernel(const __grid_
   }
 }
 
-template <int D, bool BF16, int R>
+template <int D, bool BF16, int R, int RS>
 cudaError_t launch_decode_impl(const FwdParams& p, int grid, cudaStream_t stream) {
-  auto kern = fa_decode_kernel<D, BF16, R>;
+  auto kern = fa_decode_kernel<D, BF16, R, RS>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -634,16 +654,18 @@ cudaError_t launch_decode_impl(const FwdParams& p, int grid, cudaStream_t stream
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_done[dev] = 1;
   }
-  kern<<<grid, kDecThreads, DecLayout<D>::kDynBytes, stream>>>(p);
+  kern<<<grid, 32 * (4 * RS + 2), DecLayout<D>::kDynBytes, stream>>>(p);
   return cudaGetLastError();
 }
 
 // the smallest row count (4, 8, 16) that holds the block
 template <int D, bool BF16>
 cudaError_t launch_decode_rows(const FwdParams& p, int grid, cudaStream_t stream) {
-  if (p.Nq <= 4) return launch_decode_impl<D, BF16, 4>(p, grid, stream);
-  if (p.Nq <= 8) return launch_decode_impl<D, BF16, 8>(p, grid, stream);
-  return launch_decode_impl<D, BF16, 16>(p, grid, stream);
+  if (p.Nq <= 4) return launch_decode_impl<D, BF16, 4, 1>(p, grid, stream);
+  if (p.Nq <= 8) return launch_decode_impl<D, BF16, 8, 1>(p, grid, stream);
+  // 16 rows: two softmax warpgroups of 8 rows each (measured 1.26x at d=128,
+  // 1.46x at d=64 against one warpgroup of 16 rows)
+  return launch_decode_impl<D, BF16, 16, 2>(p, grid, stream);
 }
 
 }  // namespace
