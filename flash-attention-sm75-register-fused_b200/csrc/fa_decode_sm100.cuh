@@ -29,9 +29,10 @@
 // (n_splits > 1), otherwise the final O / LSE.
 //
 // Warps: 0-3 softmax (thread t = key t of the tile, and column t of O^T for
-// its rescale and the epilogue; 8- and 16-row blocks: warps 0-7, warp w and
-// w + 4 taking the first / second half of the rows of the same keys), then the TMA producer and the
-// MMA issuer + TMEM owner (192 or 320 threads).
+// its rescale and the epilogue; 8-row blocks: warps 0-7 and 16-row blocks:
+// warps 0-15, warp w + 4k taking the k-th share of the rows of the same
+// keys), then the TMA producer and the MMA issuer + TMEM owner (192, 320 or
+// 576 threads).
 //
 // Development builds (-DFA_TRACE) record per tile c of the CTA (c < 63):
 // producer issued K_c / V_c (0, 1); MMA warp issued S^T(c) / PV(c) (2, 3),
@@ -168,13 +169,13 @@ __device__ __forceinline__ int dec_row(int lane) {
   return row;
 }
 
-// RS = 2 splits a block's rows between two softmax warpgroups (warps w and
-// w + 4 read the same TMEM lanes, i.e. the same keys, and different row
-// columns), halving each thread's exponentials for 16-row blocks.
+// RS = 2 or 4 splits a block's rows between that many softmax warpgroups
+// (warps w, w + 4, ... read the same TMEM lanes, i.e. the same keys, and
+// different row columns), dividing each thread's exponentials by RS.
 template <int D, bool BF16, int R, int RS>
 __global__ void __launch_bounds__(32 * (4 * RS + 2), 1) fa_decode_kernel(const __grid_constant__ FwdParams p) {
   static_assert(R == 4 || R == 8 || R == 16, "rows per block");
-  static_assert(RS == 1 || (RS == 2 && R >= 8), "row split");
+  static_assert(RS == 1 || (RS == 2 && R >= 8) || (RS == 4 && R == 16), "row split");
   constexpr int kDecWarpLoad = 4 * RS;
   constexpr int kDecWarpMma = 4 * RS + 1;
   constexpr uint32_t kSoftThreads = 128 * RS;
@@ -382,12 +383,15 @@ __global__ void __launch_bounds__(32 * (4 * RS + 2), 1) fa_decode_kernel(const _
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     // this thread's RP row columns starting at TMEM column `col` (+ q0)
     auto ld_rows = [&](uint32_t col, uint32_t (&r)[16]) {
-      if constexpr (RS == 1) ptx::tmem_ld16(tmem + lane_base + col, r);
-      else ptx::tmem_ld8(tmem + lane_base + col + q0, r);
+      if constexpr (RP == 16) ptx::tmem_ld16(tmem + lane_base + col, r);
+      else if constexpr (RP == 8) ptx::tmem_ld8(tmem + lane_base + col + q0, r);
+      else ptx::tmem_ld4(tmem + lane_base + col + q0, r);
     };
+    // (stores exactly this thread's RP columns: other warpgroups own the rest)
     auto st_rows = [&](uint32_t col, const uint32_t (&r)[16]) {
-      if constexpr (RS == 1) ptx::tmem_st16(tmem + lane_base + col, r);
-      else ptx::tmem_st8(tmem + lane_base + col + q0, r);
+      if constexpr (RP == 16) ptx::tmem_st16(tmem + lane_base + col, r);
+      else if constexpr (RP == 8) ptx::tmem_st8(tmem + lane_base + col + q0, r);
+      else ptx::tmem_st4(tmem + lane_base + col + q0, r);
     };
     const int nrows = p.Nq;
     // keys below vis_all are visible to every row of the block (row 0 has
@@ -658,14 +662,15 @@ cudaError_t launch_decode_impl(const FwdParams& p, int grid, cudaStream_t stream
   return cudaGetLastError();
 }
 
-// the smallest row count (4, 8, 16) that holds the block; 8 and 16 rows are
-// split between two softmax warpgroups (measured 1.08-1.11x for 8 rows,
-// 1.26-1.46x for 16, against one warpgroup holding all rows)
+// the smallest row count (4, 8, 16) that holds the block; 8 rows are split
+// between two softmax warpgroups and 16 rows between four, 4 rows per thread
+// (measured against one warpgroup holding all rows: 1.08-1.11x for 8 rows;
+// 16 rows 1.26-1.46x over two warpgroups, 1.06-1.08x more over four)
 template <int D, bool BF16>
 cudaError_t launch_decode_rows(const FwdParams& p, int grid, cudaStream_t stream) {
   if (p.Nq <= 4) return launch_decode_impl<D, BF16, 4, 1>(p, grid, stream);
   if (p.Nq <= 8) return launch_decode_impl<D, BF16, 8, 2>(p, grid, stream);
-  return launch_decode_impl<D, BF16, 16, 2>(p, grid, stream);
+  return launch_decode_impl<D, BF16, 16, 4>(p, grid, stream);
 }
 
 }  // namespace
