@@ -54,6 +54,8 @@ CASES = [
     (1, 2, 2, 128, 64, False), (1, 2, 2, 128, 128, True), (1, 1, 1, 1, 64, False),
     (1, 2, 2, 17, 128, True), (2, 4, 2, 200, 64, True), (1, 4, 1, 300, 128, False),
     (2, 2, 2, 384, 64, False), (1, 8, 2, 256, 128, True), (1, 3, 3, 513, 64, True),
+    # causal launch order groups 4 heads: 9 KV heads / 18 query heads leave a partial last group
+    (3, 6, 3, 600, 64, True),
 ]
 
 

@@ -62,6 +62,8 @@ SMALL = [
     (1, 1, 1, 257, 128, False), (2, 3, 3, 384, 64, False), (1, 2, 2, 512, 128, True),
     (1, 1, 1, 1000, 64, True), (2, 2, 2, 1024, 128, False), (1, 8, 8, 1024, 64, True),
     (1, 8, 2, 640, 128, True), (2, 6, 1, 333, 64, False), (1, 4, 4, 2048, 128, True),
+    # causal work items group 8 heads: 10 and 18 heads leave a partial last group
+    (2, 5, 5, 700, 64, True), (3, 6, 2, 900, 128, True),
 ]
 
 
