@@ -460,6 +460,7 @@ def other_configs(lib, abi, dtype, dev):
 KVCACHE_CONFIGS = {
     "decode_b8_gqa4_8k": (8, 32, 8, 1, 8192, 128, 0),
     "decode_b1_gqa4_64k": (1, 32, 8, 1, 65536, 128, 0),
+    "decode_b8_gqa8_8k": (8, 64, 8, 1, 8192, 128, 0),
     "decode_b16_mha_4k_d64": (16, 16, 16, 1, 4096, 64, 0),
     "chunk_512_of_8k_causal": (1, 32, 8, 512, 8192, 128, 1),
     # speculative decoding: 4 draft tokens x GQA 4 = a 16-row block per KV head
