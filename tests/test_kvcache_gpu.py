@@ -135,6 +135,9 @@ DECODE_BLOCKS = [
     (3, 4, 4, 16, 2000, 128),   # MHA, 16 tokens
     (1, 6, 2, 5, 128, 128),     # 15 rows, exactly one K/V tile
     (2, 8, 8, 3, 50, 64),       # Nk below one tile
+    (2, 16, 2, 1, 1500, 64),    # 8 rows at d = 64: two warpgroups x two key halves
+    (1, 6, 1, 1, 777, 64),      # 6 of 8 rows: the second warpgroup's last rows are past the block
+    (1, 10, 1, 1, 300, 128),    # 10 of 16 rows: four warpgroups, the last one empty
     (1, 17, 1, 1, 500, 64),     # 17 rows: the attention kernel
 ]
 
