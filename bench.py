@@ -388,12 +388,16 @@ def main():
 
     if not args.no_extras and rank == 0:
         line["e2e"] = e2e_leg(cfg, q, k, v, dtype, dev, flash_attention_forward_host)
-        flops, cpu_s, cores, slices, rows_n = cpu_sample(cfg)
-        line["cpu_baseline"] = {
-            "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
-            "sample": f"{slices} (b,h) slices of {cfg.name}, {rows_n} query rows x {cfg.N} keys each, "
-                      f"fp32 torch CPU oracle, {cpu_s:.1f} s"}
         if world == 1:
+            # the CPU baseline is taken at N = 1 only: with more ranks the other
+            # processes share the host cores and the figure means nothing
+            flops, cpu_s, cores, slices, rows_n = cpu_sample(cfg)
+            line["cpu_baseline"] = {
+                "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
+                "sample": f"{slices} (b,h) slices of {cfg.name}, {rows_n} query rows x {cfg.N} keys "
+                          f"each, fp32 torch CPU oracle, {cpu_s:.1f} s"}
+        else:
+            line["cpu_baseline"] = None
             line["configs"] = other_configs(lib, abi, dtype, dev)
             line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
             line["backward"] = backward_configs(lib, abi, dtype, dev)
