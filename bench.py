@@ -396,12 +396,12 @@ def main():
                 "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
                 "sample": f"{slices} (b,h) slices of {cfg.name}, {rows_n} query rows x {cfg.N} keys "
                           f"each, fp32 torch CPU oracle, {cpu_s:.1f} s"}
-        else:
-            line["cpu_baseline"] = None
             line["configs"] = other_configs(lib, abi, dtype, dev)
             line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
             line["backward"] = backward_configs(lib, abi, dtype, dev)
             line["varlen"] = varlen_configs(lib, abi, dtype, dev)
+        else:
+            line["cpu_baseline"] = None
     elif rank == 0:
         line["e2e"] = None
     if world > 1:
