@@ -26,7 +26,7 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 KERNEL_SOURCES = ["fa_fwd_sm100.cu", "fa_abi.cu"]
-KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_fwd.h", "fa_bwd_sm100.cuh"]
+KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_fwd.h", "fa_bwd_sm100.cuh", "fa_decode_sm100.cuh"]
 
 
 def _run(cmd, verbose):

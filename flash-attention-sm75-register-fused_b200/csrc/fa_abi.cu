@@ -791,25 +791,16 @@ namespace {
 constexpr unsigned long long kNoAllocScratchFloats = 4ull << 20;  // 16 MiB of fp32 scores
 __device__ __align__(256) float g_naive_noalloc_scratch[kNoAllocScratchFloats];
 
-std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[64] = {};
-
 // Device address of the scratch array for the current device.  Host code may
 // not pass the symbol itself to a kernel (on the host it names a host-side
-// stand-in); the address is looked up once per device, with that device
-// current, and cached.
+// stand-in); the address is looked up on every call, with the calling
+// thread's current device, so it stays valid after a cudaDeviceReset reloads
+// this module.  The lookup allocates nothing.
 int noalloc_scratch(float** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
-  if (dev < 0 || dev >= 64) return FA_ERR_DEVICE;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_naive_noalloc_scratch) != cudaSuccess || p == nullptr)
-      return FA_ERR_CUDA;
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_naive_noalloc_scratch) != cudaSuccess || p == nullptr)
+    return FA_ERR_CUDA;
+  *out = static_cast<float*>(p);
   return FA_OK;
 }
 

@@ -226,9 +226,11 @@ int fa_naive_fwd(const void* Q, const void* K, const void* V, void* O, int batch
  *     problems return FA_ERR_SCRATCH_LIMIT and launch nothing.  Every GPU that
  *     loads this library holds those 16 MiB until the process exits.
  *   - Nothing is allocated or freed: no cudaMalloc/cudaFree, no allocating
- *     library call.  The first call on a device looks up the array's device
- *     address (cudaGetSymbolAddress) with that device current; make that first
- *     call before any stream capture on the device.
+ *     library call.  Every call looks up the array's device address
+ *     (cudaGetSymbolAddress) for the calling thread's current device, so the
+ *     address stays right after a cudaDeviceReset; the first call on a device
+ *     may also load this library's module there, so make that first call
+ *     before any stream capture on the device.
  *   - All calls on a device share the one array and it keeps the last call's
  *     contents (every score is rewritten before it is read, so nothing needs
  *     clearing).  Calls whose work overlaps on the GPU race on the array:
