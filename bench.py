@@ -1,25 +1,34 @@
 """Attention-forward benchmark (driver contract: one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c5] [--dtype f16|bf16] [--no-extras] [--kvcache-only NAME|all]
-                    [--varlen-only NAME|all] [--backward-only NAME|all]
+                    [--config c5] [--dtype f16|bf16] [--scaling strong|weak]
+                    [--no-extras] [--kvcache-only NAME|all] [--varlen-only NAME|all]
+                    [--backward-only NAME|all]
 
 Metric: attention-forward TFLOPS, FLOPs = 4*B*H*N^2*d (halved
-for causal, the reference's convention), whole-job aggregate over N GPUs.
+for causal, the reference's convention).  `value` is the whole-job aggregate
+over the N GPUs; `tflops_per_gpu` = value / N.
 Default workload: configuration C5 full — B=4, H=32, N=8192, d=128, fp16,
 1 % of K rows scaled x8 — the shape the north-star target is quoted on; it
-fits one GPU.  Multi-GPU (torchrun, one rank per GPU): weak scaling, each
-rank owns its own B=4 slice of a global batch of 4*N; (batch, head) units are
-independent, so no collective touches the data path (NCCL only takes the max
-of the per-rank times).
+fits one GPU.
 
-A step is one attention forward over the rank's batch, inputs resident in
-HBM (1.07 GB per step read+written, larger than the 126 MB L2, so no L2 flush
-is needed between steps).  `e2e` times the same forward through the public
-Python API for host buffers (`flash_attention_forward_host`): the step's Q/K/V
-are copied from pinned host memory and O back inside the timed region, with the
-copies of each (batch, KV-head group) chunk overlapping the other chunks'
-computation.
+Multi-GPU (torchrun, one rank per GPU), default `--scaling strong`: the global
+C5 problem stays B=4 H=32 at every N and its independent (batch, KV-head
+group) units are split into contiguous ranges (`sharding.shard_units`), so at
+N=8 each rank owns 16 of the 128 (batch, head) units.  Every rank builds the
+same seeded global inputs and runs its range as one launch; no collective
+touches the timed data path.  After timing, an NCCL all-gather brings every
+rank's O and LSE to rank 0, which checks sampled rows of the first and the
+last (batch, head) unit against the CPU oracle.  `--scaling weak` gives each
+rank its own B=4 batch instead.
+
+A step is one attention forward over the rank's units, inputs resident in
+HBM (1.07 GB per step read+written at N=1, larger than the 126 MB L2, so no
+L2 flush is needed between steps).  `e2e` times the same forward through the
+public Python API for host buffers (`flash_attention_forward_host`) on every
+rank's units: the step's Q/K/V are copied from pinned host memory and O back
+inside the timed region, with the copies of each (batch, KV-head group) chunk
+overlapping the other chunks' computation.
 """
 import argparse
 import json
@@ -37,7 +46,8 @@ for _p in (REPO, PKG_DIR):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-METRIC = "attn fwd TFLOPS/GPU (causal-halved) at 1/2/4/8 B200; % of tensor peak"
+METRIC = ("attn fwd TFLOPS (causal-halved), whole-job aggregate over 1/2/4/8 B200 "
+          "(per GPU: tflops_per_gpu); % of tensor peak")
 FALLBACK_PEAK_TFLOPS = 1590.0
 FALLBACK_HBM_GBS = 6650.0
 
@@ -50,6 +60,9 @@ CONFIG_TEXT = {
     "c5c": "C5 causal attention B=4 H=32 N=8192 d=128 (1% K rows x8)",
 }
 
+# rows sampled per checked (batch, head) slice, besides the tile edges
+PARITY_ROWS = 96
+
 
 def parse_args():
     ap = argparse.ArgumentParser()
@@ -59,8 +72,11 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c5", choices=sorted(CONFIG_TEXT))
     ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the global problem is fixed and split over the ranks "
+                         "(default); weak: every rank runs its own full batch")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip e2e, cpu_baseline and the per-config table (profiling runs)")
+                    help="skip e2e, cpu_baseline and the per-config tables (profiling runs)")
     ap.add_argument("--kvcache-only", default=None, metavar="NAME|all",
                     help="time only fa_fwd_kvcache workloads (decode / chunked prefill) and print "
                          "their table as one JSON line (profiling runs)")
@@ -70,6 +86,9 @@ def parse_args():
     ap.add_argument("--backward-only", default=None, metavar="NAME|all",
                     help="time only fa_bwd workloads (attention backward) and print their table "
                          "as one JSON line (profiling runs)")
+    ap.add_argument("--configs-only", default=None, metavar="NAME|all",
+                    help="time only the forward of the BASELINE configurations (kernel time, "
+                         "parity of sampled rows, SDPA beside it) as one JSON line")
     return ap.parse_args()
 
 
@@ -100,6 +119,20 @@ def load_traffic(config):
     except OSError:
         pass
     return None
+
+
+def config_dict(cfg, world, scaling):
+    """The `config` object of both arms' JSON lines (same keys, same values)."""
+    strong = scaling == "strong"
+    return {
+        "workload": CONFIG_TEXT[cfg.name], "B": cfg.B, "Hq": cfg.Hq, "Hkv": cfg.Hkv,
+        "N": cfg.N, "d": cfg.d, "causal": cfg.causal,
+        "global_batch": cfg.B if strong else cfg.B * world,
+        "parallelism": (f"{world} rank(s), contiguous ranges of the B*Hkv (batch, KV-head "
+                        f"group) units" if strong else f"{world} rank(s), one B={cfg.B} batch each"),
+        "l2": ("inputs+outputs > 126 MB L2 per step; no flush needed" if cfg.min_bytes > 126e6
+               else "L2 not flushed (inputs smaller than L2)"),
+    }
 
 
 # ----------------------------------------------------------------- clocks
@@ -177,7 +210,9 @@ class ClockSampler:
 def make_device_inputs(cfg, b0, b1, dtype, device, seed=42):
     """Seeded synthetic inputs for global batch entries [b0, b1): per entry a
     CUDA generator seeded from (seed, b) draws Q, K, V ~ N(0,1) (times the
-    config's input scale), then K rows ``randperm(N)[:frac*N]`` per head x8."""
+    config's input scale), then K rows ``randperm(N)[:frac*N]`` per head x8.
+    Entry b's data do not depend on b0 / b1, so every rank that builds the
+    global batch holds the same bits."""
     import torch
     qs, ks, vs = [], [], []
     for b in range(b0, b1):
@@ -199,23 +234,94 @@ def make_device_inputs(cfg, b0, b1, dtype, device, seed=42):
     return torch.cat(qs).contiguous(), torch.cat(ks).contiguous(), torch.cat(vs).contiguous()
 
 
+class RankShard:
+    """The contiguous range of (batch, KV-head group) units rank r runs: views
+    of the global [B, H, N, d] tensors flattened to [B*H, N, d] (one launch
+    with batch 1 and the range's heads)."""
+
+    def __init__(self, cfg, world, rank, scaling):
+        from flash_attention_sm75.sharding import shard_units
+        self.G = cfg.Hq // cfg.Hkv
+        if scaling == "strong":
+            s = shard_units(cfg.B, cfg.Hq, cfg.Hkv, world, rank)
+            self.u0 = s.groups[0][0] * cfg.Hkv + s.groups[0][1] if s.groups else 0
+            self.units = len(s.groups)
+        else:  # weak: the rank's own batch is the whole problem
+            self.u0, self.units = 0, cfg.B * cfg.Hkv
+        self.q_heads = self.units * self.G
+
+    def views(self, cfg, q, k, v, o, lse):
+        G, u0, n = self.G, self.u0, self.units
+        fl = lambda t: t.view(-1, cfg.N, cfg.d)
+        return (fl(q)[u0 * G:(u0 + n) * G], fl(k)[u0:u0 + n], fl(v)[u0:u0 + n],
+                fl(o)[u0 * G:(u0 + n) * G], lse.view(-1, cfg.N)[u0 * G:(u0 + n) * G])
+
+
+# ----------------------------------------------------------------- parity
+def parity_check(cfg, q, k, v, o, lse, units=None, n_rows=PARITY_ROWS):
+    """Sampled-row parity of a computed O / LSE against the CPU oracle (the
+    reference's fp32 attention restated): rows 0, N-1, every 128-row tile's
+    edges and ``n_rows`` seeded random rows of the (batch, query head) units in
+    ``units`` (default: the first and the last), each against all N keys.
+    Tolerance: |err| <= 2e-3 + 1e-2*|ref| (bf16: 1.6e-2 + 2e-2*|ref|) on O,
+    1e-4 on LSE."""
+    from oracle import attention_oracle as orc
+    import torch
+    G = cfg.Hq // cfg.Hkv
+    if units is None:
+        units = [(0, 0), (cfg.B - 1, cfg.Hq - 1)]
+    bf16 = q.dtype == torch.bfloat16
+    atol, rtol = (1.6e-2, 2e-2) if bf16 else (orc.ATOL, orc.RTOL)
+    rows = orc.sample_rows(cfg.N, n_rows, seed=0)
+    res = {"max_abs_err": 0.0, "max_rel_err": 0.0, "max_err_over_bound": 0.0, "lse_err": 0.0}
+    ok = True
+    for b, h in units:
+        qs = q[b:b + 1, h:h + 1].cpu()
+        ks = k[b:b + 1, h // G:h // G + 1].cpu()
+        vs = v[b:b + 1, h // G:h // G + 1].cpu()
+        ref_o, ref_l = orc.attention_fp32(qs, ks, vs, causal=cfg.causal, rows=rows)
+        got = o[b:b + 1, h:h + 1].cpu()[:, :, rows].float()
+        err = (got - ref_o).abs()
+        bound = atol + rtol * ref_o.abs()
+        r = orc.check(got, ref_o, atol=atol, rtol=rtol)
+        rl = orc.check_lse(lse[b:b + 1, h:h + 1].cpu()[:, :, rows], ref_l)
+        res["max_abs_err"] = max(res["max_abs_err"], r["max_abs_err"])
+        res["max_rel_err"] = max(res["max_rel_err"], r["max_rel_err"])
+        res["max_err_over_bound"] = max(res["max_err_over_bound"], (err / bound).max().item())
+        res["lse_err"] = max(res["lse_err"], rl["max_abs_err"])
+        ok = ok and r["ok"] and rl["ok"]
+    res["ok"] = ok
+    res["checked"] = f"{len(rows)} rows x {len(units)} (b,h) units {units}"
+    return res
+
+
 # ----------------------------------------------------------------- CPU legs
-def cpu_sample(cfg, budget_s=8.0, seed=42):
+def cpu_slice(cfg, g):
+    """One (batch, head) slice of the workload's inputs on the CPU, drawn like
+    oracle.make_inputs (N(0,1) x input scale, the K outlier rows) from the
+    generator ``g``: Q, K, V [1, 1, N, d] fp16."""
+    import torch
+    q = torch.randn(1, 1, cfg.N, cfg.d, generator=g) * cfg.input_scale
+    k = torch.randn(1, 1, cfg.N, cfg.d, generator=g) * cfg.input_scale
+    v = torch.randn(1, 1, cfg.N, cfg.d, generator=g) * cfg.input_scale
+    n_out = int(cfg.N * cfg.k_outlier_frac)
+    if n_out:
+        k[0, 0, torch.randperm(cfg.N, generator=g)[:n_out]] *= cfg.k_outlier_scale
+    return q.half(), k.half(), v.half()
+
+
+def cpu_time_slices(cfg, g, n_slices=None, budget_s=None, rows_n=512):
     """Times the CPU oracle (the reference's fp32 attention restated,
-    oracle/attention_oracle.py) with all host threads on (b, h) slices of the
-    workload: each slice is one query head with 512 of its query rows against
-    all N keys.  Returns (flops, seconds, cores, slices, rows per slice)."""
+    oracle/attention_oracle.py) with all host threads on fresh (b, h) slices of
+    the workload, each ``rows_n`` seeded query rows against all N keys, for
+    ``n_slices`` slices or until ``budget_s`` seconds of oracle time.  Input
+    generation is not timed.  Returns (flops, seconds, slices)."""
     import torch
     from oracle import attention_oracle as orc
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    rows_n = min(512, cfg.N)
-    g = torch.Generator().manual_seed(seed)
+    rows_n = min(rows_n, cfg.N)
     flops, secs, slices = 0.0, 0.0, 0
-    while secs < budget_s:
-        q = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
-        k = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
-        v = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
+    while (n_slices is not None and slices < n_slices) or (budget_s is not None and secs < budget_s):
+        q, k, v = cpu_slice(cfg, g)
         rows = torch.randperm(cfg.N, generator=g)[:rows_n].sort().values
         t1 = time.perf_counter()
         orc.attention_fp32(q, k, v, causal=cfg.causal, rows=rows)
@@ -223,40 +329,44 @@ def cpu_sample(cfg, budget_s=8.0, seed=42):
         flops += (float(4.0 * cfg.d * (rows + 1).sum().item()) if cfg.causal
                   else 4.0 * rows_n * cfg.N * cfg.d)
         slices += 1
-    return flops, secs, cores, slices, rows_n
+    return flops, secs, slices
+
+
+def cpu_threads():
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    return cores
 
 
 def run_reference(args, cfg):
     """--impl reference: the reference's CPU path (the oracle port) on the host
-    cores, on this arm's metric and config; each step is a bounded sample."""
+    cores, on this arm's metric and config.  Each step is a bounded sample of
+    the workload: enough fresh 512-row (b, h) slices (with the K outlier rows)
+    for about 0.3 s of oracle time, the slice count fixed during warm-up — the
+    same sampling as the GPU arm's `cpu_baseline` leg."""
     import torch
-    from oracle import attention_oracle as orc
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    rows_n = min(256, cfg.N)
+    cores = cpu_threads()
     g = torch.Generator().manual_seed(42)
-    q = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
-    k = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
-    v = torch.randn(1, 1, cfg.N, cfg.d, generator=g).half()
-    rows = torch.randperm(cfg.N, generator=g)[:rows_n].sort().values
-    step_flops = (float(4.0 * cfg.d * (rows + 1).sum().item()) if cfg.causal
-                  else 4.0 * rows_n * cfg.N * cfg.d)
+    t_slice = min(cpu_time_slices(cfg, g, n_slices=1)[1] for _ in range(3))
+    per_step = max(1, int(round(0.3 / max(t_slice, 1e-6))))
     for _ in range(args.warmup):
-        orc.attention_fp32(q, k, v, causal=cfg.causal, rows=rows)
-    t0 = time.perf_counter()
+        cpu_time_slices(cfg, g, n_slices=per_step)
+    flops, secs = 0.0, 0.0
     for _ in range(args.steps):
-        orc.attention_fp32(q, k, v, causal=cfg.causal, rows=rows)
-    dt = time.perf_counter() - t0
-    tflops = step_flops * args.steps / dt / 1e12
-    sample = (f"per step: one (b,h) slice of {cfg.name}, {rows_n} query rows x {cfg.N} keys, "
-              f"d={cfg.d}, fp32 torch CPU oracle")
+        f, s, n = cpu_time_slices(cfg, g, n_slices=per_step)
+        flops += f
+        secs += s
+    tflops = flops / secs / 1e12
+    sample = (f"per step: {per_step} fresh (b,h) slices of {cfg.name}, 512 query rows x "
+              f"{cfg.N} keys each, d={cfg.d}, K outlier rows as the workload, fp32 torch CPU "
+              f"oracle, {secs:.1f} s in total")
     line = {
         "metric": METRIC, "value": tflops, "unit": "TFLOPS", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": CONFIG_TEXT[cfg.name], "B": cfg.B, "Hq": cfg.Hq, "Hkv": cfg.Hkv,
-                   "N": cfg.N, "d": cfg.d, "causal": cfg.causal},
+        "config": config_dict(cfg, args.gpus, args.scaling),
         "cpu_baseline": {"value": tflops, "unit": "TFLOPS", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": tflops, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
@@ -278,10 +388,31 @@ def time_steps(fn, steps, stream):
     return e0.elapsed_time(e1)
 
 
+def units_per_rank(cfg, world, scaling):
+    """(batch, KV-head group) units each rank runs."""
+    from flash_attention_sm75.sharding import shard_units
+    if scaling != "strong":
+        return [cfg.B * cfg.Hkv] * world
+    return [len(shard_units(cfg.B, cfg.Hq, cfg.Hkv, world, r).groups) for r in range(world)]
+
+
+def gather_to_rank0(dist, t, count, max_count, world, dev):
+    """All-gather of each rank's first-dimension range (``count`` rows of
+    ``t``, padded to ``max_count``) over NCCL; returns the [world, max_count,
+    ...] result (used on rank 0)."""
+    import torch
+    pad = torch.zeros((max_count,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+    if count:
+        pad[:count].copy_(t[:count])
+    out = torch.empty((world * max_count,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+    dist.all_gather_into_tensor(out, pad)
+    return out.view((world, max_count) + tuple(t.shape[1:]))
+
+
 def main():
     args = parse_args()
     rank, world, local_rank = dist_env()
-    from oracle import attention_oracle as orc  # config table and CPU legs only
+    from oracle import attention_oracle as orc  # config table, CPU legs and parity checks only
     cfg = orc.CONFIGS[args.config]
 
     if args.impl == "reference":
@@ -291,56 +422,51 @@ def main():
 
     import torch
     import torch.distributed as dist
-    import flash_attn_sm75_cuda as _C
+    import flash_attn_sm75_cuda as _C  # noqa: F401  (the pybind module must load)
     from flash_attention_sm75 import flash_attention_forward_host
-    from flash_attention_sm75.sharding import batch_range
     from flash_attention_sm75 import capi as abi
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if args.kvcache_only:
-        if rank == 0:
-            dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
-            names = None if args.kvcache_only == "all" else [args.kvcache_only]
-            print(json.dumps({"kvcache": kvcache_configs(abi.load(), abi, dtype, dev, names)}),
-                  flush=True)
-        return
-    if args.varlen_only:
-        if rank == 0:
-            dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
-            names = None if args.varlen_only == "all" else [args.varlen_only]
-            print(json.dumps({"varlen": varlen_configs(abi.load(), abi, dtype, dev, names)}),
-                  flush=True)
-        return
-    if args.backward_only:
-        if rank == 0:
-            dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
-            names = None if args.backward_only == "all" else [args.backward_only]
-            print(json.dumps({"backward": backward_configs(abi.load(), abi, dtype, dev, names)}),
-                  flush=True)
-        return
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    only = [("kvcache", args.kvcache_only, kvcache_configs),
+            ("varlen", args.varlen_only, varlen_configs),
+            ("backward", args.backward_only, backward_configs),
+            ("configs", args.configs_only, other_configs)]
+    for key, sel, fn in only:
+        if sel:
+            if rank == 0:
+                names = None if sel == "all" else [sel]
+                print(json.dumps({key: fn(abi.load(), abi, dtype, dev, names)}), flush=True)
+            return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
-    b0, b1 = batch_range(cfg.B, rank)
-    q, k, v = make_device_inputs(cfg, b0, b1, dtype, dev)
-    o = torch.empty_like(q)
-    lse = torch.empty(q.shape[:3], dtype=torch.float32, device=dev)
+    strong = args.scaling == "strong"
+    shard = RankShard(cfg, world, rank, args.scaling)
+    # every rank builds the same global inputs (strong) or its own batch (weak)
+    b0 = 0 if strong else rank * cfg.B
+    q, k, v = make_device_inputs(cfg, b0, b0 + cfg.B, dtype, dev)
+    o = torch.zeros_like(q)
+    lse = torch.zeros(q.shape[:3], dtype=torch.float32, device=dev)
+    qs, ks, vs, os_, ls = shard.views(cfg, q, k, v, o, lse)
     stream = torch.cuda.current_stream(dev)
     scale = 1.0 / math.sqrt(cfg.d)
     dt_code = 1 if dtype == torch.bfloat16 else 0
     lib = abi.load()
-    qp, kp, vp, op, lp, sp = (abi.ptr(q), abi.ptr(k), abi.ptr(v), abi.ptr(o), abi.ptr(lse),
+    qp, kp, vp, op, lp, sp = (abi.ptr(qs), abi.ptr(ks), abi.ptr(vs), abi.ptr(os_), abi.ptr(ls),
                               abi.stream_ptr(stream))
+    n_heads, n_kv = shard.q_heads, shard.units
 
     def step():
-        rc = lib.fa_fwd(qp, kp, vp, op, lp, cfg.B, cfg.Hq, cfg.Hkv, cfg.N, cfg.d, scale,
+        if n_heads == 0:
+            return
+        rc = lib.fa_fwd(qp, kp, vp, op, lp, 1, n_heads, n_kv, cfg.N, cfg.d, scale,
                         int(cfg.causal), dt_code, sp)
         if rc != 0:
             raise RuntimeError(lib.fa_error_string(rc).decode())
 
-    for _ in range(args.warmup):
+    for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -360,86 +486,142 @@ def main():
     if status != 0:
         raise RuntimeError(f"device watchdog fired: {lib.fa_error_string(status).decode()}")
 
+    # ---- parity of this run's output (outside the timed region)
+    if world > 1 and strong:
+        max_heads = -(-cfg.B * cfg.Hkv // world) * shard.G
+        go = gather_to_rank0(dist, os_, n_heads, max_heads, world, dev)
+        gl = gather_to_rank0(dist, ls, n_heads, max_heads, world, dev)
+        counts = torch.tensor([n_heads], device=dev, dtype=torch.int64)
+        all_counts = torch.empty(world, device=dev, dtype=torch.int64)
+        dist.all_gather_into_tensor(all_counts, counts)
+        if rank == 0:
+            o_full = torch.cat([go[r, :int(c)] for r, c in enumerate(all_counts.tolist())])
+            l_full = torch.cat([gl[r, :int(c)] for r, c in enumerate(all_counts.tolist())])
+            o_chk = o_full.view_as(o)
+            l_chk = l_full.view_as(lse)
+        del go, gl
+    else:
+        o_chk, l_chk = o, lse
+    parity = parity_check(cfg, q, k, v, o_chk, l_chk) if rank == 0 else None
+
     ms_step = ms / args.steps
-    total_flops = cfg.flops * world
+    total_flops = cfg.flops * (1 if strong else world)
     value = total_flops / (ms_step * 1e-3) / 1e12
     peak, hbm, peak_kind = load_peaks()
     per_gpu = value / world
     traffic = load_traffic(cfg.name)
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": args.dtype, "data": "synthetic (seeded N(0,1), 1% K rows x8 for C5)",
-        "config": {"workload": CONFIG_TEXT[cfg.name], "B_per_gpu": cfg.B, "Hq": cfg.Hq,
-                   "Hkv": cfg.Hkv, "N": cfg.N, "d": cfg.d, "causal": cfg.causal,
-                   "global_batch": cfg.B * world, "parallelism": f"dp{world} over (batch, head)",
-                   "l2": "inputs+outputs 1.07 GB/step > 126 MB L2; no flush needed"
-                   if cfg.min_bytes > 126e6 else "L2 not flushed (small config)"},
+        "config": config_dict(cfg, world, args.scaling),
         "tflops_per_gpu": per_gpu,
-        "gpu_launches": args.steps,
+        "units_per_rank": units_per_rank(cfg, world, args.scaling),
+        "gpu_launches": args.steps * world,
+        "gpu_launches_per_rank": args.steps,
         "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                      "frac": per_gpu / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
                      "frac_of_spec_2250": per_gpu / 2250.0,
-                     "traffic": traffic,
-                     "algorithmic_bytes": cfg.min_bytes},
+                     "traffic": traffic if world == 1 else None,
+                     "algorithmic_bytes": cfg.min_bytes / (world if strong else 1)},
         "clocks": clocks,
+        "parity": parity,
     }
-
-    if not args.no_extras and rank == 0:
-        line["e2e"] = e2e_leg(cfg, q, k, v, dtype, dev, flash_attention_forward_host)
-        if world == 1:
-            # the CPU baseline is taken at N = 1 only: with more ranks the other
-            # processes share the host cores and the figure means nothing
-            flops, cpu_s, cores, slices, rows_n = cpu_sample(cfg)
-            line["cpu_baseline"] = {
-                "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
-                "sample": f"{slices} (b,h) slices of {cfg.name}, {rows_n} query rows x {cfg.N} keys "
-                          f"each, fp32 torch CPU oracle, {cpu_s:.1f} s"}
-            line["configs"] = other_configs(lib, abi, dtype, dev)
-            line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
-            line["backward"] = backward_configs(lib, abi, dtype, dev)
-            line["varlen"] = varlen_configs(lib, abi, dtype, dev)
-        else:
-            line["cpu_baseline"] = None
+    if not args.no_extras:
+        line["e2e"] = e2e_leg(cfg, shard, qs, ks, vs, dev, flash_attention_forward_host,
+                              dist if world > 1 else None, strong, world)
+    if not args.no_extras and rank == 0 and world == 1:
+        # the CPU baseline is taken at N = 1 only: with more ranks the other
+        # processes share the host cores and the figure means nothing
+        cores = cpu_threads()
+        flops, cpu_s, slices = cpu_time_slices(cfg, torch.Generator().manual_seed(42),
+                                               budget_s=8.0)
+        line["cpu_baseline"] = {
+            "value": flops / cpu_s / 1e12, "unit": "TFLOPS", "cores": cores, "kind": "port",
+            "sample": f"{slices} fresh (b,h) slices of {cfg.name}, 512 query rows x {cfg.N} keys "
+                      f"each, K outlier rows as the workload, fp32 torch CPU oracle, "
+                      f"{cpu_s:.1f} s"}
+        del q, k, v, o, lse, qs, ks, vs, os_, ls
+        torch.cuda.empty_cache()
+        line["configs"] = other_configs(lib, abi, dtype, dev)
+        line["kvcache"] = kvcache_configs(lib, abi, dtype, dev)
+        line["backward"] = backward_configs(lib, abi, dtype, dev)
+        line["varlen"] = varlen_configs(lib, abi, dtype, dev)
     elif rank == 0:
-        line["e2e"] = None
+        line["cpu_baseline"] = None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+        if parity is not None and not parity["ok"]:
+            sys.exit(f"parity check of the timed output failed: {parity}")
 
 
-def e2e_leg(cfg, q, k, v, dtype, dev, fwd_host, steps=5):
+def e2e_leg(cfg, shard, qs, ks, vs, dev, fwd_host, dist, strong, world, steps=5):
     """Public API end to end: ``flash_attention_forward_host`` on pinned host
-    Q/K/V, O returned in pinned host memory (H2D, forward and D2H of each
-    (batch, KV-head group) chunk overlap inside the call)."""
+    copies of this rank's units (Q [1, heads, N, d], K/V [1, units, N, d]), O
+    returned in pinned host memory (H2D, forward and D2H of each (batch,
+    KV-head group) chunk overlap inside the call).  Multi-GPU: every rank runs
+    its units; the step time is the max over ranks."""
     import torch
-    hq = q.cpu().pin_memory()
-    hk = k.cpu().pin_memory()
-    hv = v.cpu().pin_memory()
+    hq = qs.unsqueeze(0).cpu().pin_memory()
+    hk = ks.unsqueeze(0).cpu().pin_memory()
+    hv = vs.unsqueeze(0).cpu().pin_memory()
     ho = torch.empty_like(hq).pin_memory()
     stream = torch.cuda.current_stream(dev)
+    n = shard.q_heads
 
     def step():
-        fwd_host(hq, hk, hv, causal=cfg.causal, out=ho)
+        if n:
+            fwd_host(hq, hk, hv, causal=cfg.causal, out=ho)
 
     step()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     ms = time_steps(step, steps, stream) / steps
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = ho.numel() * ho.element_size()
-    return {"value": cfg.flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms,
+    if dist is not None:
+        t = torch.tensor([ms, h2d, d2h], device=dev, dtype=torch.float64)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        ms, h2d, d2h = float(tmax[0].item()), int(t[1].item()), int(t[2].item())
+    flops = cfg.flops * (1 if strong else world)
+    return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 
-def other_configs(lib, abi, dtype, dev):
-    """Kernel-only TFLOPS of the other BASELINE configurations (reported, not the headline)."""
+def sdpa_time(q, k, v, causal, n):
+    """PyTorch's scaled_dot_product_attention on the same inputs (its default
+    backend choice), ms per call; a same-box comparison column only."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    gqa = q.size(1) != k.size(1)
+    # fused backends only: the math backend would materialise the N x N scores
+    with sdpa_kernel([SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+                      SDPBackend.EFFICIENT_ATTENTION]):
+        fn = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=gqa)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return time_steps(fn, n, torch.cuda.current_stream()) / n
+
+
+def other_configs(lib, abi, dtype, dev, names=None):
+    """Kernel-only TFLOPS of the BASELINE configurations (reported, not the
+    headline), with the sampled-row parity of each timed output and PyTorch
+    SDPA's time on the same inputs as a same-box comparison column."""
     import torch
     from oracle import attention_oracle as orc
     out = {}
-    for name in ("c1", "c2", "c3", "c4", "c5c"):
+    for name in ("c1", "c2", "c3", "c4", "c5", "c5c"):
+        if names is not None and name not in names:
+            continue
         c = orc.CONFIGS[name]
         q, k, v = make_device_inputs(c, 0, c.B, dtype, dev)
         o = torch.empty_like(q)
@@ -454,8 +636,19 @@ def other_configs(lib, abi, dtype, dev):
         torch.cuda.synchronize()
         n = max(20, min(2000, int(2e12 / c.flops)))
         ms = time_steps(fn, n, s) / n
+        par = parity_check(c, q, k, v, o, lse)
+        try:
+            ms_sdpa = sdpa_time(q, k, v, c.causal, n)
+        except RuntimeError:  # no fused SDPA backend takes this shape
+            ms_sdpa = float("nan")
         out[name] = {"tflops": round(c.flops / ms / 1e9, 1), "us": round(ms * 1e3, 2),
-                     "gbs": round(c.min_bytes / (ms * 1e-3) / 1e9, 1)}
+                     "gbs": round(c.min_bytes / (ms * 1e-3) / 1e9, 1),
+                     "max_abs_err": par["max_abs_err"], "max_rel_err": par["max_rel_err"],
+                     "max_err_over_bound": par["max_err_over_bound"], "lse_err": par["lse_err"],
+                     "parity_ok": par["ok"],
+                     "sdpa_tflops": round(c.flops / ms_sdpa / 1e9, 1),
+                     "sdpa_us": round(ms_sdpa * 1e3, 2)}
+        del q, k, v, o, lse
     return out
 
 

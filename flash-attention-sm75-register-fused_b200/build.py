@@ -4,6 +4,8 @@ Outputs (all next to the sources, so they travel with the tree):
   lib/libfa_b200.so                      C ABI (include/fa_b200.h), sm_100a kernels
   flash_attn_sm75_cuda<ext-suffix>.so    pybind module (reference's L3 name)
   lib/flash_mha_flatargs, lib/flash_mha_v2   standalone CLIs (reference argv/stdout)
+  lib/libfa_selftest.so                  stage tests of the kernel's building blocks
+                                         (loaded by tests/ only)
 
 Every CUDA file is compiled with
   -gencode arch=compute_100a,code=sm_100a -lineinfo
@@ -26,7 +28,8 @@ NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 KERNEL_SOURCES = ["fa_fwd_sm100.cu", "fa_abi.cu"]
-KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_fwd.h", "fa_bwd_sm100.cuh", "fa_decode_sm100.cuh"]
+KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_softmax.cuh", "fa_fwd.h", "fa_bwd_sm100.cuh",
+                  "fa_decode_sm100.cuh"]
 
 
 def _run(cmd, verbose):
@@ -114,10 +117,28 @@ def build_cli(force=False, verbose=False):
     return outs
 
 
+def selftest_path():
+    return os.path.join(LIB, "libfa_selftest.so")
+
+
+def build_selftest(force=False, verbose=False):
+    """Test library of the kernel's building blocks (csrc/fa_selftest.cu):
+    exp2 polynomial, softmax stage and single-tile tcgen05 products."""
+    os.makedirs(LIB, exist_ok=True)
+    out = selftest_path()
+    src = os.path.join(CSRC, "fa_selftest.cu")
+    deps = [src] + [os.path.join(CSRC, h) for h in ("sm100_ptx.cuh", "fa_softmax.cuh")]
+    if force or _stale(out, deps):
+        _run([NVCC, "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
+              "-I", CSRC, src, "-o", out, "-lcudart"], verbose)
+    return out
+
+
 def build(force=False, verbose=False):
     build_lib(force, verbose)
     build_ext(force, verbose)
     build_cli(force, verbose)
+    build_selftest(force, verbose)
 
 
 if __name__ == "__main__":

@@ -38,6 +38,7 @@
 
 #include "fa_fwd.h"
 #include "sm100_ptx.cuh"
+#include "fa_softmax.cuh"
 
 namespace fa {
 
@@ -228,48 +229,6 @@ constexpr int kTraceCtas = 8, kTraceTiles = 64, kTraceEvents = 32;
   } while (0)
 #endif
 
-// Fraction of exponentials evaluated by the FMA-pipe polynomial instead of
-// the MUFU unit: pair c of every group of kEmuPeriod pairs uses the
-// polynomial when c % kEmuPeriod >= kEmuPeriod - kEmuCount.
-#ifndef FA_EMU_PERIOD
-#define FA_EMU_PERIOD 4
-#endif
-#ifndef FA_EMU_COUNT
-#define FA_EMU_COUNT 1
-#endif
-constexpr int kEmuPeriod = FA_EMU_PERIOD;
-constexpr int kEmuCount = FA_EMU_COUNT;
-
-// Three-input max / min (sm_100 forms of max.f32 / min.f32).
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float fmin3(float a, float b, float c) {
-  float d;
-  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// Max (kMin: min) of N scores in four independent three-input chains.
-template <int N, bool kMin>
-__device__ __forceinline__ float row_extreme(const float (&x)[N]) {
-  static_assert(N % 8 == 0 && N >= 16, "row length");
-  auto op3 = [](float a, float b, float c) { return kMin ? fmin3(a, b, c) : fmax3(a, b, c); };
-  float a = x[0], b = x[1], c = x[2], d = x[3];
-#pragma unroll
-  for (int i = 4; i + 8 <= N; i += 8) {
-    a = op3(a, x[i], x[i + 1]);
-    b = op3(b, x[i + 2], x[i + 3]);
-    c = op3(c, x[i + 4], x[i + 5]);
-    d = op3(d, x[i + 6], x[i + 7]);
-  }
-  a = op3(a, x[N - 4], x[N - 3]);
-  b = op3(b, x[N - 2], x[N - 1]);
-  return op3(a, b, kMin ? fminf(c, d) : fmaxf(c, d));
-}
-
 // The first kPEarlyQuarters quarters of P (32 keys each) are announced to the
 // MMA warp before the rest is computed, so the PV steps on them overlap the
 // softmax's tail.
@@ -293,14 +252,8 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       const int i = 32 * h + 2 * c;
-      float t0, t1, e0, e1;
-      ptx::ffma2(t0, t1, x[i], x[i + 1], sl, sl, neg_m, neg_m);
-      if (kEmulate && (c % kEmuPeriod) >= kEmuPeriod - kEmuCount) {
-        ptx::exp2_poly2(e0, e1, t0, t1);
-      } else {
-        e0 = ptx::ex2_approx(t0);
-        e1 = ptx::ex2_approx(t1);
-      }
+      float e0, e1;
+      exp2_pair<kEmulate>(c, x[i], x[i + 1], sl, neg_m, e0, e1);
       if (c & 1)
         ptx::fadd2(b0, b1, b0, b1, e0, e1);
       else

@@ -63,3 +63,13 @@ def test_header_is_plain_c():
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)  # declarations only, not comments
     for forbidden in ("torch", "at::", "Tensor", "std::"):
         assert forbidden not in text
+
+
+def test_selftest_library_exports_its_stage_tests():
+    """The test-only library of the kernel's building blocks (exp2 polynomial,
+    softmax stage, single-tile tcgen05 products) loads without a GPU."""
+    import os
+    path = os.path.join(os.path.dirname(abi.LIB_PATH), "libfa_selftest.so")
+    lib = ctypes.CDLL(path)
+    for name in ("fa_selftest_exp2", "fa_selftest_softmax", "fa_selftest_mma"):
+        assert hasattr(lib, name)

@@ -74,3 +74,59 @@ def test_gloo_two_ranks_assemble_full_output(tmp_path):
     full, _ = orc.attention_fp32(q, k, v, causal=True)
     got = torch.load(out_path)
     assert torch.allclose(got, full, atol=1e-6)
+
+
+def _bench_worker(rank, world, port, out_path):
+    """One rank of bench.py's strong-scaling path on CPU: its RankShard views
+    of the global tensors, the oracle in place of the kernel, then the
+    all-gather that brings every rank's O / LSE to rank 0."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here),
+                                                         "flash-attention-sm75-register-fused_b200")]
+    import bench
+    from oracle import attention_oracle as orc
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = orc.AttnConfig("t", 3, 8, 2, 80, 64, True)
+        q, k, v = orc.make_inputs(cfg, seed=6)
+        o = torch.zeros(q.shape, dtype=torch.float32)
+        lse = torch.zeros(q.shape[:3])
+        sh = bench.RankShard(cfg, world, rank, "strong")
+        qs, ks, vs, os_, ls = sh.views(cfg, q, k, v, o, lse)
+        if sh.units:
+            oo, ll = orc.attention_fp32(qs[None], ks[None], vs[None], causal=True)
+            os_.copy_(oo[0])
+            ls.copy_(ll[0])
+        max_heads = -(-cfg.B * cfg.Hkv // world) * sh.G
+        go = bench.gather_to_rank0(dist, os_, sh.q_heads, max_heads, world, "cpu")
+        gl = bench.gather_to_rank0(dist, ls, sh.q_heads, max_heads, world, "cpu")
+        counts = bench.units_per_rank(cfg, world, "strong")
+        if rank == 0:
+            o_full = torch.cat([go[r, :c * sh.G] for r, c in enumerate(counts)]).view_as(o)
+            l_full = torch.cat([gl[r, :c * sh.G] for r, c in enumerate(counts)]).view_as(lse)
+            torch.save((o_full, l_full), out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_bench_strong_scaling_shards_reassemble(tmp_path, world):
+    """bench.py's strong-scaling split (6 KV-head groups over 2 or 4 ranks, the
+    latter uneven) gathers back to exactly the single-process result."""
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    out_path = str(tmp_path / "out.pt")
+    mp.start_processes(_bench_worker, args=(world, port, out_path), nprocs=world,
+                       start_method="spawn", join=True)
+    from oracle import attention_oracle as orc
+    cfg = orc.AttnConfig("t", 3, 8, 2, 80, 64, True)
+    q, k, v = orc.make_inputs(cfg, seed=6)
+    full, full_l = orc.attention_fp32(q, k, v, causal=True)
+    got, got_l = torch.load(out_path)
+    assert torch.allclose(got, full, atol=1e-6)
+    assert torch.allclose(got_l, full_l, atol=1e-6)
