@@ -174,6 +174,7 @@ struct Plan {
   bool decode = false;  // at most 16 query rows: the decode kernel
   bool dual = false;  // one Q tile: the two softmax groups split the key tiles
   int n_ctas = 0;     // persistent CTAs (dual mode), 0 = one per work item
+  bool q_tile = true;  // the tile kernel (else the pair kernel)
   int heads = 0, rows = 0, group = 1, pos_mod = 1, n_qpairs = 0, n_kv_tiles = 0;
   int n_splits = 1, tiles_per_split = 0;
   size_t ws_o_bytes = 0, ws_bytes = 0;
@@ -189,7 +190,12 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   k.rows = k.pack ? G * Nq : Nq;
   k.group = k.pack ? 1 : G;
   k.pos_mod = k.pack ? Nq : k.rows;
-  k.n_qpairs = (k.rows + 255) / 256;
+  // Square and chunked prefill run the tile kernel (one 128-row Q tile per
+  // work item); FA_DEBUG_PAIR_KERNEL selects the pair kernel (two tiles per
+  // item) for comparisons.  Dual and decode launches have one unit per row
+  // block either way.
+  k.q_tile = (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_PAIR_KERNEL) == 0;
+  k.n_qpairs = k.q_tile ? (k.rows + 127) / 128 : (k.rows + 255) / 256;
   k.n_kv_tiles = (Nk + 127) / 128;
   k.tiles_per_split = k.n_kv_tiles;
   const long long units = static_cast<long long>(k.n_qpairs) * B * k.heads;
@@ -307,7 +313,7 @@ int check_args(const void* Q, const void* K, const void* V, const void* O, const
   if (!std::isfinite(scale)) return FA_ERR_INVALID_ARG;
   const long long rows = static_cast<long long>(B) * Hq * Nq;
   if (Nq > (1 << 30) || Nk > (1 << 30) || rows > (1LL << 40) ||
-      static_cast<long long>(B) * Hq * ((static_cast<long long>(Nq) + 255) / 256) > 0x7fffffffLL)
+      static_cast<long long>(B) * Hq * ((static_cast<long long>(Nq) + 127) / 128) > 0x7fffffffLL)
     return FA_ERR_TOO_LARGE;
   return check_device();
 }
@@ -345,6 +351,7 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.Nk = Nk;
   p.group = k.group;
   p.n_qpairs = k.n_qpairs;
+  p.q_tile = (k.q_tile && !k.dual && !k.decode) ? 1 : 0;
   p.n_kv_tiles = k.n_kv_tiles;
   p.causal = causal != FA_CAUSAL_NONE ? 1 : 0;
   p.causal_off = causal == FA_CAUSAL_BOTTOM_RIGHT ? Nk - Nq : 0;
@@ -424,7 +431,8 @@ int launch_ranged(bool packed, const void* Q, const void* K, const void* V, void
   p.Nq = Nq;
   p.Nk = Nk;
   p.group = Hq / Hkv;
-  p.n_qpairs = (Nq + 255) / 256;
+  p.q_tile = (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_PAIR_KERNEL) == 0;
+  p.n_qpairs = p.q_tile ? (Nq + 127) / 128 : (Nq + 255) / 256;
   p.n_kv_tiles = (Nk + 127) / 128;
   p.causal = causal != FA_CAUSAL_NONE ? 1 : 0;
   // packed: per-sequence offsets come from causal_br in the kernel; padded:

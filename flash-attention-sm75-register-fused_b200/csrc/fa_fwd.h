@@ -23,7 +23,9 @@ struct alignas(64) FwdParams {
   // another (the same memory as [B, Hq, len, d]).
   int B, heads, Hkv, Nq, Nk;
   int group;         // query "heads" per KV head (1 when packed)
-  int n_qpairs;      // ceil(Nq / 256): Q pairs per (batch, head)
+  int n_qpairs;      // Q units per (batch, head): ceil(Nq / 128) tiles (q_tile) or ceil(Nq / 256) pairs
+  int q_tile;        // 1: the tile kernel (one 128-row Q tile per work item, S double-buffered);
+                     // 0: the pair kernel (two Q tiles per item; dual mode)
   int n_kv_tiles;    // ceil(Nk / 128)
   int causal;        // key j visible to row r iff j <= pos(r) + causal_off
   int causal_off;

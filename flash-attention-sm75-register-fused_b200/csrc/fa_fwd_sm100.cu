@@ -1086,7 +1086,31 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
   if (lane == 0 && p.lse != nullptr) p.lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
 }
 
+#include "fa_fwd_tile.cuh"
+
 }  // namespace
+
+template <int D, bool BF16>
+static cudaError_t launch_tile_impl(const FwdParams& p, int grid, cudaStream_t stream) {
+  auto kern = tile::fa_fwd_tile_kernel<D, BF16>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    // the setmaxnreg split assumes exactly kLaunchRegs registers per thread
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads)
+      return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             tile::TLayout<D>::kDynBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
+  }
+  kern<<<grid, kThreads, tile::TLayout<D>::kDynBytes, stream>>>(p);
+  return cudaGetLastError();
+}
 
 template <int D, bool BF16>
 static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream) {
@@ -1113,6 +1137,13 @@ static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream
 
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
   const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
+  if (p.q_tile) {
+    if (head_dim == 64)
+      return bf16 ? launch_tile_impl<64, true>(p, n_work, stream)
+                  : launch_tile_impl<64, false>(p, n_work, stream);
+    return bf16 ? launch_tile_impl<128, true>(p, n_work, stream)
+                : launch_tile_impl<128, false>(p, n_work, stream);
+  }
   const int grid = (p.n_ctas > 0 && p.n_ctas < n_work) ? p.n_ctas : n_work;
   if (head_dim == 64) return bf16 ? launch_impl<64, true>(p, grid, stream) : launch_impl<64, false>(p, grid, stream);
   return bf16 ? launch_impl<128, true>(p, grid, stream) : launch_impl<128, false>(p, grid, stream);

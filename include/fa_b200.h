@@ -54,7 +54,11 @@ enum {
 };
 
 /* Test hooks (fa_set_debug_flags). */
-enum { FA_DEBUG_SKIP_Q_LOAD = 1 /* producer never loads Q: the MMA warp's wait must time out */ };
+enum {
+  FA_DEBUG_SKIP_Q_LOAD = 1, /* producer never loads Q: the consumers' wait must time out */
+  FA_DEBUG_PAIR_KERNEL = 2  /* square / chunked prefill on the pair kernel (two Q tiles per
+                               CTA) instead of the tile kernel, for comparisons */
+};
 
 /*
  * fa_fwd — asynchronous attention forward on `stream` (cudaStream_t; NULL =
