@@ -37,10 +37,57 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Encoded tensor maps of recent calls: a map is a pure function of its
+// arguments, so a call that repeats (pointer, shape, dtype, box) -- every
+// layer of a model, every benchmark step -- reuses the encoding instead of
+// paying the driver's encoder again.  Direct-mapped, guarded by a mutex.
+struct MapKey {
+  const void* base;
+  long long n, bh;
+  int d, box_rows, bf16, kind;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && n == o.n && bh == o.bh && d == o.d && box_rows == o.box_rows &&
+           bf16 == o.bf16 && kind == o.kind;
+  }
+};
+constexpr int kMapCacheSize = 64;
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+std::mutex g_map_mu;
+MapEntry g_map_cache[kMapCacheSize];
+
+int map_slot(const MapKey& k) {
+  uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+  h ^= static_cast<uint64_t>(k.n) * 0xC2B2AE3D27D4EB4Full + static_cast<uint64_t>(k.bh) * 31 +
+       static_cast<uint64_t>(k.d * 7 + k.box_rows * 13 + k.bf16 * 3 + k.kind);
+  return static_cast<int>((h >> 32) % kMapCacheSize);
+}
+
+bool cached_map(CUtensorMap* map, const MapKey& k) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  const MapEntry& e = g_map_cache[map_slot(k)];
+  if (!e.valid || !(e.key == k)) return false;
+  *map = e.map;
+  return true;
+}
+
+void remember_map(const CUtensorMap& map, const MapKey& k) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  MapEntry& e = g_map_cache[map_slot(k)];
+  e.key = k;
+  e.map = map;
+  e.valid = true;
+}
+
 // [rows = B*H*N, d] tensor viewed as 3-D (d, N, B*H) so that a box of
 // `box_rows` rows never crosses into the next head: rows >= N read as zeros.
 bool make_map(CUtensorMap* map, const void* base, int d, int n, long long bh, bool bf16,
               unsigned box_rows = 128) {
+  const MapKey key{base, n, bh, d, static_cast<int>(box_rows), bf16 ? 1 : 0, 0};
+  if (cached_map(map, key)) return true;
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(n),
@@ -54,7 +101,9 @@ bool make_map(CUtensorMap* map, const void* base, int d, int n, long long bh, bo
          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  remember_map(*map, key);
+  return true;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -182,6 +231,18 @@ struct Plan {
 
 constexpr int kDecodeRows = 16;  // query rows of the decode kernel's blocks
 
+// Kernel choice for a launch whose pair kernel would have `pair_units` work
+// items (measured on B200: the tile kernel is faster only while the pair
+// kernel leaves SMs idle in its single wave, e.g. 10.6 vs 17.1 us at
+// B=1 H=1 N=512; from C2 to C5 the pair kernel is 3-30 % faster).
+// FA_DEBUG_PAIR_KERNEL / FA_DEBUG_TILE_KERNEL force one of them.
+bool use_tile_kernel(long long pair_units) {
+  const int flags = g_debug_flags.load(std::memory_order_relaxed);
+  if (flags & FA_DEBUG_PAIR_KERNEL) return false;
+  if (flags & FA_DEBUG_TILE_KERNEL) return true;
+  return pair_units < sm_count();
+}
+
 Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) {
   Plan k;
   const int G = Hq / Hkv;
@@ -190,11 +251,11 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   k.rows = k.pack ? G * Nq : Nq;
   k.group = k.pack ? 1 : G;
   k.pos_mod = k.pack ? Nq : k.rows;
-  // Square and chunked prefill run the tile kernel (one 128-row Q tile per
-  // work item); FA_DEBUG_PAIR_KERNEL selects the pair kernel (two tiles per
-  // item) for comparisons.  Dual and decode launches have one unit per row
-  // block either way.
-  k.q_tile = (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_PAIR_KERNEL) == 0;
+  // Square and chunked prefill run the pair kernel (two 128-row Q tiles per
+  // work item) unless its work items would not fill one wave of SMs; then
+  // the tile kernel (one tile per item) doubles the CTAs.  Dual and decode
+  // launches have one unit per row block either way.
+  k.q_tile = use_tile_kernel(static_cast<long long>((k.rows + 255) / 256) * B * k.heads);
   k.n_qpairs = k.q_tile ? (k.rows + 127) / 128 : (k.rows + 255) / 256;
   k.n_kv_tiles = (Nk + 127) / 128;
   k.tiles_per_split = k.n_kv_tiles;
@@ -381,6 +442,8 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
 // head's 128 consecutive tokens, laid out in shared memory exactly like a
 // (64, 128, 1) box of make_map.  Rows >= T read as zeros.
 bool make_map_packed(CUtensorMap* map, const void* base, int d, int h, long long t, bool bf16) {
+  const MapKey key{base, t, h, d, 128, bf16 ? 1 : 0, 1};
+  if (cached_map(map, key)) return true;
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(h),
@@ -394,7 +457,9 @@ bool make_map_packed(CUtensorMap* map, const void* base, int d, int h, long long
          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  remember_map(*map, key);
+  return true;
 }
 
 // Launch of the attention kernel over per-batch row ranges (fa_fwd_varlen:
@@ -431,7 +496,7 @@ int launch_ranged(bool packed, const void* Q, const void* K, const void* V, void
   p.Nq = Nq;
   p.Nk = Nk;
   p.group = Hq / Hkv;
-  p.q_tile = (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_PAIR_KERNEL) == 0;
+  p.q_tile = use_tile_kernel(static_cast<long long>((Nq + 255) / 256) * B * Hq) ? 1 : 0;
   p.n_qpairs = p.q_tile ? (Nq + 127) / 128 : (Nq + 255) / 256;
   p.n_kv_tiles = (Nk + 127) / 128;
   p.causal = causal != FA_CAUSAL_NONE ? 1 : 0;

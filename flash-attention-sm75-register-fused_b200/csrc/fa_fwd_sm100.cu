@@ -1090,26 +1090,35 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
 
 }  // namespace
 
-template <int D, bool BF16>
+template <int D, bool BF16, int kSplit>
 static cudaError_t launch_tile_impl(const FwdParams& p, int grid, cudaStream_t stream) {
-  auto kern = tile::fa_fwd_tile_kernel<D, BF16>;
+  using C = tile::TCfg<kSplit>;
+  auto kern = tile::fa_fwd_tile_kernel<D, BF16, kSplit>;
+  constexpr int kSmem = tile::TLayout<D, kSplit>::kDynBytes;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    // the setmaxnreg split assumes exactly kLaunchRegs registers per thread
+    // a setmaxnreg split assumes exactly kLaunchRegs registers per thread
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return e;
-    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads)
+    constexpr bool kSplitRegs = C::kRegsSoftmax != C::kLaunchRegs;
+    if ((kSplitRegs && fa.numRegs != C::kLaunchRegs) || fa.numRegs > C::kLaunchRegs ||
+        fa.maxThreadsPerBlock < C::kThreads)
       return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             tile::TLayout<D>::kDynBytes);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_done[dev] = 1;
   }
-  kern<<<grid, kThreads, tile::TLayout<D>::kDynBytes, stream>>>(p);
+  kern<<<grid, C::kThreads, kSmem, stream>>>(p);
   return cudaGetLastError();
+}
+
+template <int D, bool BF16>
+static cudaError_t launch_tile(const FwdParams& p, int grid, cudaStream_t stream) {
+  if (p.debug_flags & FA_DEBUG_TILE_SPLIT2) return launch_tile_impl<D, BF16, 2>(p, grid, stream);
+  return launch_tile_impl<D, BF16, 4>(p, grid, stream);
 }
 
 template <int D, bool BF16>
@@ -1139,10 +1148,8 @@ cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t
   const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
   if (p.q_tile) {
     if (head_dim == 64)
-      return bf16 ? launch_tile_impl<64, true>(p, n_work, stream)
-                  : launch_tile_impl<64, false>(p, n_work, stream);
-    return bf16 ? launch_tile_impl<128, true>(p, n_work, stream)
-                : launch_tile_impl<128, false>(p, n_work, stream);
+      return bf16 ? launch_tile<64, true>(p, n_work, stream) : launch_tile<64, false>(p, n_work, stream);
+    return bf16 ? launch_tile<128, true>(p, n_work, stream) : launch_tile<128, false>(p, n_work, stream);
   }
   const int grid = (p.n_ctas > 0 && p.n_ctas < n_work) ? p.n_ctas : n_work;
   if (head_dim == 64) return bf16 ? launch_impl<64, true>(p, grid, stream) : launch_impl<64, false>(p, grid, stream);

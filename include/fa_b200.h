@@ -56,8 +56,12 @@ enum {
 /* Test hooks (fa_set_debug_flags). */
 enum {
   FA_DEBUG_SKIP_Q_LOAD = 1, /* producer never loads Q: the consumers' wait must time out */
-  FA_DEBUG_PAIR_KERNEL = 2  /* square / chunked prefill on the pair kernel (two Q tiles per
-                               CTA) instead of the tile kernel, for comparisons */
+  FA_DEBUG_PAIR_KERNEL = 2, /* square / chunked prefill always on the pair kernel (two Q
+                               tiles per CTA), for comparisons */
+  FA_DEBUG_TILE_SPLIT2 = 4, /* tile kernel with each tile's keys split between 2 softmax
+                               warpgroups instead of 4, for comparisons */
+  FA_DEBUG_TILE_KERNEL = 8  /* square / chunked prefill always on the tile kernel (one Q
+                               tile per CTA, S double-buffered), for comparisons */
 };
 
 /*

@@ -242,3 +242,43 @@ def test_parity_late_max_growth_kvcache(sm100, Nq, Nk):
     assert r["ok"], r
     lerr = (lse.cpu() - ref_lse).abs()
     assert (lerr <= orc.LSE_ATOL + 2e-6 * ref_lse.abs()).all(), lerr.max().item()
+
+
+# Both forward kernels on the same shapes: the pair kernel (two Q tiles per
+# CTA, the default once a launch fills a wave) and the tile kernel (one Q tile
+# per CTA, S double-buffered; the default for launches that would leave SMs
+# idle), each forced through its debug flag.
+FORCED = [(1, 1, 1, 1, 64, True), (1, 2, 2, 17, 128, False), (1, 1, 1, 129, 64, False),
+          (1, 2, 2, 255, 128, True), (1, 8, 2, 640, 128, True), (2, 6, 1, 333, 64, False),
+          (3, 6, 2, 900, 128, True), (1, 4, 4, 2048, 128, True), (2, 5, 5, 700, 64, True)]
+
+
+@pytest.mark.parametrize("flag", [2, 8, 8 | 4], ids=["pair", "tile4", "tile2"])
+@pytest.mark.parametrize("B,Hq,Hkv,N,d,causal", FORCED)
+def test_parity_forced_kernel(sm100, flag, B, Hq, Hkv, N, d, causal):
+    lib = abi.load()
+    lib.fa_set_debug_flags(flag)
+    try:
+        parity(B, Hq, Hkv, N, d, causal, seed=3 * N + d)
+    finally:
+        lib.fa_set_debug_flags(0)
+
+
+@pytest.mark.parametrize("flag", [2, 8], ids=["pair", "tile4"])
+@pytest.mark.parametrize("d,causal", [(64, True), (128, False)])
+def test_forced_kernels_bf16_and_outliers(sm100, flag, d, causal):
+    """bf16, and K rows x8 (the C5 outliers: late running-max growth and the
+    lazy rescale) on a 32-head launch that fills several waves."""
+    lib = abi.load()
+    lib.fa_set_debug_flags(flag)
+    try:
+        parity(2, 4, 2, 700, d, causal, dtype=torch.bfloat16, seed=12)
+        cfg = orc.AttnConfig("t", 1, 32, 32, 1024, d, causal, k_outlier_frac=0.01)
+        q, k, v = orc.make_inputs(cfg, seed=5)
+        o, lse = run(q.cuda(), k.cuda(), v.cuda(), causal)
+        rows = orc.sample_rows(1024, 64, seed=1)
+        ref_o, ref_lse = orc.attention_fp32(q, k, v, causal=causal, rows=rows)
+        assert orc.check(o.cpu()[:, :, rows], ref_o)["ok"]
+        assert orc.check_lse(lse.cpu()[:, :, rows], ref_lse)["ok"]
+    finally:
+        lib.fa_set_debug_flags(0)
