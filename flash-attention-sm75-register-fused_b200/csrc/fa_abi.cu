@@ -224,6 +224,7 @@ struct Plan {
   bool dual = false;  // one Q tile: the two softmax groups split the key tiles
   int n_ctas = 0;     // persistent CTAs (dual mode), 0 = one per work item
   bool q_tile = true;  // the tile kernel (else the pair kernel)
+  bool pair2 = false;  // the pair kernel on CTA pairs (n_qpairs counts 512-row quads)
   int heads = 0, rows = 0, group = 1, pos_mod = 1, n_qpairs = 0, n_kv_tiles = 0;
   int n_splits = 1, tiles_per_split = 0;
   size_t ws_o_bytes = 0, ws_bytes = 0;
@@ -238,9 +239,21 @@ constexpr int kDecodeRows = 16;  // query rows of the decode kernel's blocks
 // FA_DEBUG_PAIR_KERNEL / FA_DEBUG_TILE_KERNEL force one of them.
 bool use_tile_kernel(long long pair_units) {
   const int flags = g_debug_flags.load(std::memory_order_relaxed);
-  if (flags & FA_DEBUG_PAIR_KERNEL) return false;
+  if (flags & (FA_DEBUG_PAIR_KERNEL | FA_DEBUG_PAIR2_KERNEL)) return false;
   if (flags & FA_DEBUG_TILE_KERNEL) return true;
   return pair_units < sm_count();
+}
+
+// The pair kernel on CTA pairs (fa_fwd_pair2: each product issued once for
+// two SMs, each SM streaming half of every K/V tile) applies to d = 128 over
+// plain rows (no GQA packing, more than one tile of queries).  It is opt-in
+// (FA_DEBUG_PAIR2_KERNEL): measured on B200 against the one-SM pair kernel
+// on one box, C5 1110-1129 vs 1129-1136 TFLOPS and C4 GQA causal 923 vs
+// 1034 (a causal group computes its extra diagonal tile for both CTAs).
+bool use_pair2_kernel(bool /*tile*/, int d, bool packed, int rows) {
+  const int flags = g_debug_flags.load(std::memory_order_relaxed);
+  if (d != 128 || packed || rows <= 128) return false;
+  return (flags & FA_DEBUG_PAIR2_KERNEL) != 0;
 }
 
 Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) {
@@ -256,12 +269,17 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   // the tile kernel (one tile per item) doubles the CTAs.  Dual and decode
   // launches have one unit per row block either way.
   k.q_tile = use_tile_kernel(static_cast<long long>((k.rows + 255) / 256) * B * k.heads);
-  k.n_qpairs = k.q_tile ? (k.rows + 127) / 128 : (k.rows + 255) / 256;
+  k.pair2 = use_pair2_kernel(k.q_tile, d, k.pack, k.rows);
+  k.n_qpairs = k.q_tile  ? (k.rows + 127) / 128
+               : k.pair2 ? (k.rows + 511) / 512
+                         : (k.rows + 255) / 256;
   k.n_kv_tiles = (Nk + 127) / 128;
   k.tiles_per_split = k.n_kv_tiles;
   const long long units = static_cast<long long>(k.n_qpairs) * B * k.heads;
   const int sms = sm_count();
-  if (allow_split && units < sms && k.n_kv_tiles > 1) {
+  // (CTA pairs are only chosen when the pair kernel's units fill a wave, so
+  // they never split)
+  if (allow_split && !k.pair2 && units < sms && k.n_kv_tiles > 1) {
     // One CTA per (unit, split): pick the balanced split with the fewest
     // waves x (tiles per split + start-up), a CTA's start-up (first loads,
     // epilogue, its share of the combine) counted as 4 tiles, at least two
@@ -394,8 +412,10 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   const long long bh = static_cast<long long>(B) * k.heads;
   // the decode kernel's K/V tiles are 256 keys at d = 64 (32 KB, like d = 128)
   const unsigned kv_box = (k.decode && head_dim == 64) ? 256 : 128;
+  // CTA pairs load half of a K tile (64 keys) per CTA
+  const unsigned k_box = k.pair2 ? 64 : kv_box;
   if (!make_map(&p.tm_q, Q, head_dim, k.rows, bh, bf16, k.decode ? kDecodeRows : 128) ||
-      !make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16, kv_box) ||
+      !make_map(&p.tm_k, K, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16, k_box) ||
       !make_map(&p.tm_v, V, head_dim, Nk, static_cast<long long>(B) * Hkv, bf16, kv_box))
     return FA_ERR_TENSOR_MAP;
   p.o = O;
@@ -412,7 +432,7 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.Nk = Nk;
   p.group = k.group;
   p.n_qpairs = k.n_qpairs;
-  p.q_tile = (k.q_tile && !k.dual && !k.decode) ? 1 : 0;
+  p.q_tile = (k.q_tile && !k.dual && !k.decode) ? 1 : (k.pair2 && !k.dual && !k.decode) ? 2 : 0;
   p.n_kv_tiles = k.n_kv_tiles;
   p.causal = causal != FA_CAUSAL_NONE ? 1 : 0;
   p.causal_off = causal == FA_CAUSAL_BOTTOM_RIGHT ? Nk - Nq : 0;

@@ -25,7 +25,8 @@ struct alignas(64) FwdParams {
   int group;         // query "heads" per KV head (1 when packed)
   int n_qpairs;      // Q units per (batch, head): ceil(Nq / 128) tiles (q_tile) or ceil(Nq / 256) pairs
   int q_tile;        // 1: the tile kernel (one 128-row Q tile per work item, S double-buffered);
-                     // 0: the pair kernel (two Q tiles per item; dual mode)
+                     // 0: the pair kernel (two Q tiles per item; dual mode);
+                     // 2: the pair kernel on CTA pairs (d = 128; n_qpairs = 512-row quads)
   int n_kv_tiles;    // ceil(Nk / 128)
   int causal;        // key j visible to row r iff j <= pos(r) + causal_off
   int causal_off;

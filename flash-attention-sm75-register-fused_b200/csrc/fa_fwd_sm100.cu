@@ -240,11 +240,11 @@ static_assert(kPEarlyQuarters >= 1 && kPEarlyQuarters <= 3, "early part of P: 1-
 
 // exp2(x * sl - m) for the 128 scores of this thread's row; the packed
 // f16/bf16 values go to TMEM (P operand of the PV MMA) in four 16-column
-// quarters, the first kPEarlyQuarters announced on `half_bar` as soon as they
-// are written; returns their fp32 sum.
-template <bool BF16, bool kEmulate>
+// quarters, the first kPEarlyQuarters announced (`announce()`, an mbarrier
+// arrival) as soon as they are written; returns their fp32 sum.
+template <bool BF16, bool kEmulate, typename Announce>
 __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, float neg_m,
-                                          uint32_t tP, uint32_t half_bar) {
+                                          uint32_t tP, Announce announce) {
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
@@ -264,7 +264,7 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
     if (h == kPEarlyQuarters - 1) {
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(half_bar);
+      announce();
     }
   }
   ptx::fadd2(a0, a1, a0, a1, b0, b1);
@@ -895,8 +895,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 
       // P = exp2(x * sl_eff - m): packed FMA, then exp2 split between the MUFU
       // unit and a polynomial on the FMA pipe; written to TMEM in two halves.
-      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP, bar(L::kBarPH + g))
-                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP, bar(L::kBarPH + g));
+      const uint32_t half_bar = bar(L::kBarPH + g);
+      auto announce = [half_bar] { ptx::mbar_arrive(half_bar); };
+      const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP, announce)
+                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP, announce);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       if (lane == 0) FA_TRACE_AT(dual ? ((cnt + j) & 63) : j, 8 + sw);
@@ -1087,6 +1089,7 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const __grid_constant__
 }
 
 #include "fa_fwd_tile.cuh"
+#include "fa_fwd_pair2.cuh"
 
 }  // namespace
 
@@ -1121,6 +1124,39 @@ static cudaError_t launch_tile(const FwdParams& p, int grid, cudaStream_t stream
   return launch_tile_impl<D, BF16, 4>(p, grid, stream);
 }
 
+template <bool BF16>
+static cudaError_t launch_pair2_impl(const FwdParams& p, int n_clusters, cudaStream_t stream) {
+  auto kern = pair2::fa_fwd_pair2_kernel<BF16>;
+  constexpr int kSmem = pair2::PLayout::kDynBytes;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    // the setmaxnreg split assumes exactly kLaunchRegs registers per thread
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < kThreads)
+      return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2u * static_cast<unsigned>(n_clusters));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 template <int D, bool BF16>
 static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream) {
   auto kern = fa_fwd_kernel<D, BF16>;
@@ -1146,6 +1182,10 @@ static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream
 
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
   const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
+  if (p.q_tile == 2) {  // CTA pairs, d = 128: one cluster per (batch*head, Q quad)
+    if (head_dim != 128 || p.n_splits != 1 || p.dual || p.ranges) return cudaErrorInvalidValue;
+    return bf16 ? launch_pair2_impl<true>(p, n_work, stream) : launch_pair2_impl<false>(p, n_work, stream);
+  }
   if (p.q_tile) {
     if (head_dim == 64)
       return bf16 ? launch_tile<64, true>(p, n_work, stream) : launch_tile<64, false>(p, n_work, stream);

@@ -60,8 +60,10 @@ enum {
                                tiles per CTA), for comparisons */
   FA_DEBUG_TILE_SPLIT2 = 4, /* tile kernel with each tile's keys split between 2 softmax
                                warpgroups instead of 4, for comparisons */
-  FA_DEBUG_TILE_KERNEL = 8  /* square / chunked prefill always on the tile kernel (one Q
+  FA_DEBUG_TILE_KERNEL = 8, /* square / chunked prefill always on the tile kernel (one Q
                                tile per CTA, S double-buffered), for comparisons */
+  FA_DEBUG_PAIR2_KERNEL = 16 /* d = 128 square / chunked prefill on CTA pairs (one product
+                               for two SMs) wherever they apply (opt-in) */
 };
 
 /*

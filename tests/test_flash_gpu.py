@@ -244,16 +244,17 @@ def test_parity_late_max_growth_kvcache(sm100, Nq, Nk):
     assert (lerr <= orc.LSE_ATOL + 2e-6 * ref_lse.abs()).all(), lerr.max().item()
 
 
-# Both forward kernels on the same shapes: the pair kernel (two Q tiles per
-# CTA, the default once a launch fills a wave) and the tile kernel (one Q tile
-# per CTA, S double-buffered; the default for launches that would leave SMs
-# idle), each forced through its debug flag.
+# The forward kernels on the same shapes, each forced through its debug flag:
+# the pair kernel (two Q tiles per CTA; the default once a launch fills a
+# wave), its CTA-pair form (one product for two SMs, d = 128; opt-in) and the
+# tile kernel (one Q tile per CTA, S double-buffered; the default for
+# launches that would leave SMs idle).
 FORCED = [(1, 1, 1, 1, 64, True), (1, 2, 2, 17, 128, False), (1, 1, 1, 129, 64, False),
           (1, 2, 2, 255, 128, True), (1, 8, 2, 640, 128, True), (2, 6, 1, 333, 64, False),
           (3, 6, 2, 900, 128, True), (1, 4, 4, 2048, 128, True), (2, 5, 5, 700, 64, True)]
 
 
-@pytest.mark.parametrize("flag", [2, 8, 8 | 4], ids=["pair", "tile4", "tile2"])
+@pytest.mark.parametrize("flag", [2, 8, 8 | 4, 16], ids=["pair", "tile4", "tile2", "pair2"])
 @pytest.mark.parametrize("B,Hq,Hkv,N,d,causal", FORCED)
 def test_parity_forced_kernel(sm100, flag, B, Hq, Hkv, N, d, causal):
     lib = abi.load()
@@ -264,8 +265,8 @@ def test_parity_forced_kernel(sm100, flag, B, Hq, Hkv, N, d, causal):
         lib.fa_set_debug_flags(0)
 
 
-@pytest.mark.parametrize("flag", [2, 8], ids=["pair", "tile4"])
-@pytest.mark.parametrize("d,causal", [(64, True), (128, False)])
+@pytest.mark.parametrize("flag", [2, 8, 16], ids=["pair", "tile4", "pair2"])
+@pytest.mark.parametrize("d,causal", [(64, True), (128, False), (128, True)])
 def test_forced_kernels_bf16_and_outliers(sm100, flag, d, causal):
     """bf16, and K rows x8 (the C5 outliers: late running-max growth and the
     lazy rescale) on a 32-head launch that fills several waves."""
