@@ -441,6 +441,8 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.tiles_per_split = k.tiles_per_split;
   p.dual = k.dual ? 1 : 0;
   p.n_ctas = k.n_ctas;
+  p.item0 = 0;
+  p.item_end = 0;
   const bool use_ws = k.n_splits > 1 || k.dual;
   p.ws_o = use_ws ? static_cast<float*>(workspace) : nullptr;
   p.ws_lse = use_ws ? reinterpret_cast<float*>(static_cast<char*>(workspace) + k.ws_o_bytes)
@@ -451,8 +453,35 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = k.decode ? fa::launch_decode(p, head_dim, bf16, s)
-                                 : fa::launch_fwd(p, head_dim, bf16, s);
+  // Wave tail: a non-causal pair-kernel launch of several waves whose last
+  // wave is at most half full runs those last items on the tile kernel, as
+  // twice as many one-tile items (each ~0.6 of a pair item's time), so the
+  // last wave ends sooner.  (C5 sharded over 8 GPUs: 512 items, 3.46 waves.)
+  const long long n_items = static_cast<long long>(k.n_qpairs) * B * k.heads * k.n_splits;
+  const int sms = sm_count();
+  const long long rem = n_items % sms;
+  const bool tail = !k.decode && !k.dual && !k.q_tile && !k.pair2 && k.n_splits == 1 &&
+                    p.causal == 0 && n_items > sms && rem > 0 && 2 * rem <= sms &&
+                    (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_NO_TAIL_SPLIT) == 0;
+  cudaError_t e;
+  if (tail) {
+    const int full = static_cast<int>(n_items - rem);
+    p.item_end = full;
+    e = fa::launch_fwd(p, head_dim, bf16, s);
+    if (e == cudaSuccess) {
+      // pair items are head-major (item = bh * pairs + pair): the tiles of
+      // items >= full are tile items >= bh * tiles + 2 * pair of item `full`
+      fa::FwdParams pt = p;
+      const int tiles = (k.rows + 127) / 128;
+      pt.q_tile = 1;
+      pt.n_qpairs = tiles;
+      pt.item0 = (full / k.n_qpairs) * tiles + 2 * (full % k.n_qpairs);
+      pt.item_end = 0;
+      e = fa::launch_fwd(pt, head_dim, bf16, s);
+    }
+  } else {
+    e = k.decode ? fa::launch_decode(p, head_dim, bf16, s) : fa::launch_fwd(p, head_dim, bf16, s);
+  }
   if (e != cudaSuccess) return FA_ERR_LAUNCH;
   if (use_ws && fa::launch_combine(p, head_dim, bf16, s) != cudaSuccess) return FA_ERR_LAUNCH;
   return FA_OK;
@@ -528,6 +557,8 @@ int launch_ranged(bool packed, const void* Q, const void* K, const void* V, void
   p.tiles_per_split = p.n_kv_tiles;
   p.dual = 0;
   p.n_ctas = 0;
+  p.item0 = 0;
+  p.item_end = 0;
   p.ws_o = nullptr;
   p.ws_lse = nullptr;
   p.scale_log2 = scale * 1.4426950408889634f;

@@ -39,6 +39,10 @@ struct alignas(64) FwdParams {
   // ("sub-split" 2*split + group) for the combine kernel.
   int dual;
   int n_ctas;        // CTAs launched; 0 = one per work item, fewer = persistent CTAs
+  // Work items [item0, item_end) of the launch's item numbering (item_end 0:
+  // all); a launch may cover a sub-range, e.g. the last items of a pair-kernel
+  // launch handed to the tile kernel as twice as many one-tile items.
+  int item0, item_end;
   float* ws_o;       // partial O [n_splits * (1 + dual)][B*heads][Nq][d] fp32 (normalised)
   float* ws_lse;     // partial LSE [n_splits * (1 + dual)][B*heads][Nq] (natural log)
   float scale_log2;  // scale * log2(e)

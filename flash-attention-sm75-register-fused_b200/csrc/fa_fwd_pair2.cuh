@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_pair2_kernel(const __grid_
 
   if (warp >= 8) {
     ptx::setmaxnreg_dec<kRegsOther>();
-    const Quad qi = decode_quad(p, static_cast<int>(blockIdx.x >> 1));
+    const Quad qi = decode_quad(p, p.item0 + static_cast<int>(blockIdx.x >> 1));
     const int n_loop = max(qi.n_kv[0], qi.n_kv[1]);
     if (warp == kWarpLoad && lane == 0 && n_loop > 0) {
       // ================================================= TMA producer
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_pair2_kernel(const __grid_
   } else {
     // ================================================= softmax groups
     ptx::setmaxnreg_inc<kRegsSoftmax>();
-    const Quad qi = decode_quad(p, static_cast<int>(blockIdx.x >> 1));
+    const Quad qi = decode_quad(p, p.item0 + static_cast<int>(blockIdx.x >> 1));
     const int g = warp >> 2;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;

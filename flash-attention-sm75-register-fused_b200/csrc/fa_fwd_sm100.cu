@@ -438,7 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
 
   const bool dual = p.dual != 0;
-  const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
+  const int n_all = p.n_qpairs * p.B * p.heads * p.n_splits;
+  const int n_work = p.item_end > 0 ? min(p.item_end, n_all) : n_all;
+  const int w0 = p.item0 + static_cast<int>(blockIdx.x);
 
   // ---- set-up: skip the CTA if this launch already failed elsewhere
   if (threadIdx.x == 0) {
@@ -488,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       int pc[2] = {0, 0};  // dual mode: tiles of group g in earlier work items (trace rows)
 #endif
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x, ++k) {
+      for (int w = w0; ok && w < n_work; w += gridDim.x, ++k) {
         WorkItem it;
         decode_item(p, w, it);
         if (!skip_q) {
@@ -641,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       bool ok = true;
       int ring = 0, k = 0;
       int cnt[2] = {0, 0};
-      for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x, ++k) {
+      for (int w = w0; ok && w < n_work; w += gridDim.x, ++k) {
         WorkItem it;
         decode_item(p, w, it);
         const int n_loop = it.n_loop;
@@ -764,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       return false;
     };
     WorkItem it;  // shared mode: one work item per CTA
-    decode_item(p, blockIdx.x, it);
+    decode_item(p, w0, it);
     for (int j = 0; j < it.n_kv[og]; ++j) {
       if (!poll(bar(L::kBarS + og), j & 1)) break;
       FA_TRACE_AT(j, 24 + 2 * og);
@@ -787,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const float sl = p.scale_log2;
     bool ok = true;
     int cnt = 0;  // S / P / O completions of this group before the work item
-    for (int w = blockIdx.x; ok && w < n_work; w += gridDim.x) {
+    for (int w = w0; ok && w < n_work; w += gridDim.x) {
     WorkItem it;
     decode_item(p, w, it);
     const int n_tiles = g ? it.n_kv[1] : it.n_kv[0];
@@ -1181,7 +1183,9 @@ static cudaError_t launch_impl(const FwdParams& p, int grid, cudaStream_t stream
 }
 
 cudaError_t launch_fwd(const FwdParams& p, int head_dim, bool bf16, cudaStream_t stream) {
-  const int n_work = p.n_qpairs * p.B * p.heads * p.n_splits;
+  const int n_all = p.n_qpairs * p.B * p.heads * p.n_splits;
+  const int n_work = (p.item_end > 0 ? min(p.item_end, n_all) : n_all) - p.item0;
+  if (n_work <= 0) return cudaSuccess;
   if (p.q_tile == 2) {  // CTA pairs, d = 128: one cluster per (batch*head, Q quad)
     if (head_dim != 128 || p.n_splits != 1 || p.dual || p.ranges) return cudaErrorInvalidValue;
     return bf16 ? launch_pair2_impl<true>(p, n_work, stream) : launch_pair2_impl<false>(p, n_work, stream);

@@ -186,7 +186,8 @@ __global__ void __launch_bounds__(TCfg<kSplit>::kThreads, 1)
   auto bar = [&](int i) -> uint32_t { return sbase + L::kOffBar + 8u * static_cast<uint32_t>(i); };
 
   WorkItem it;
-  decode(p, blockIdx.x, it);
+  const int w_item = p.item0 + static_cast<int>(blockIdx.x);
+  decode(p, w_item, it);
   const int n = it.n_loop;
 
   if (threadIdx.x == 0) {
@@ -526,7 +527,7 @@ __global__ void __launch_bounds__(TCfg<kSplit>::kThreads, 1)
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     long long o_row0, lse_row0;
     int nq;
-    item_out(p, blockIdx.x, o_row0, lse_row0, nq);
+    item_out(p, w_item, o_row0, lse_row0, nq);
     const bool row_ok = q_row < nq;
     const size_t row_index = static_cast<size_t>(lse_row0) + q_row;
     T* const orow = reinterpret_cast<T*>(p.o) + o_row0 + static_cast<long long>(q_row) * p.o_rs;

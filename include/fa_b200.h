@@ -62,8 +62,10 @@ enum {
                                warpgroups instead of 4, for comparisons */
   FA_DEBUG_TILE_KERNEL = 8, /* square / chunked prefill always on the tile kernel (one Q
                                tile per CTA, S double-buffered), for comparisons */
-  FA_DEBUG_PAIR2_KERNEL = 16 /* d = 128 square / chunked prefill on CTA pairs (one product
-                               for two SMs) wherever they apply (opt-in) */
+  FA_DEBUG_PAIR2_KERNEL = 16, /* d = 128 square / chunked prefill on CTA pairs (one product
+                                for two SMs) wherever they apply (opt-in) */
+  FA_DEBUG_NO_TAIL_SPLIT = 32 /* keep a pair-kernel launch's half-empty last wave on the pair
+                                kernel instead of the tile kernel, for comparisons */
 };
 
 /*

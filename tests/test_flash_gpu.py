@@ -283,3 +283,28 @@ def test_forced_kernels_bf16_and_outliers(sm100, flag, d, causal):
         assert orc.check_lse(lse.cpu()[:, :, rows], ref_lse)["ok"]
     finally:
         lib.fa_set_debug_flags(0)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_wave_tail_items_on_the_tile_kernel(sm100, d):
+    """A non-causal launch whose pair-kernel items fill one wave of SMs plus
+    a few (80 heads x 2 Q pairs = 160 items on 148 SMs) runs the last items on
+    the tile kernel: every head, those included, matches the oracle, and the
+    result agrees with the launch kept on the pair kernel."""
+    lib = abi.load()
+    cfg = orc.AttnConfig("t", 1, 80, 80, 512, d, False)
+    q, k, v = orc.make_inputs(cfg, seed=21)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o, lse = run(qd, kd, vd, False)
+    rows = orc.sample_rows(512, 32, seed=2)
+    for h in (0, 71, 72, 79):  # pair items 0, 143, 144 (tail), 159 (tail)
+        ref_o, ref_l = orc.attention_fp32(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], rows=rows)
+        assert orc.check(o.cpu()[:, h:h + 1, rows], ref_o)["ok"], h
+        assert orc.check_lse(lse.cpu()[:, h:h + 1, rows], ref_l)["ok"], h
+    lib.fa_set_debug_flags(32)  # FA_DEBUG_NO_TAIL_SPLIT
+    try:
+        o2, lse2 = run(qd, kd, vd, False)
+    finally:
+        lib.fa_set_debug_flags(0)
+    assert (o.float() - o2.float()).abs().max().item() <= 4e-3
+    assert (lse - lse2).abs().max().item() <= 1e-4
