@@ -676,6 +676,10 @@ def kvcache_configs(lib, abi, dtype, dev, names=None):
     hbm = peaks.get("hbm_gbs", 6650.0)
     out = {}
     el = 2
+    # SM clocks while these workloads run (they follow the forward loop, so
+    # the GPU is warm and may sit at its power cap)
+    sampler = ClockSampler(dev.index if dev.index is not None else 0)
+    sampler.start()
     for name, (B, Hq, Hkv, Nq, Nk, d, mode) in KVCACHE_CONFIGS.items():
         if names is not None and name not in names:
             continue
@@ -707,6 +711,7 @@ def kvcache_configs(lib, abi, dtype, dev, names=None):
                      "hbm_frac": round(byt / (ms * 1e-3) / 1e9 / hbm, 3),
                      "tflops": round(flops / ms / 1e9, 1), "splits_workspace_bytes": int(nbytes)}
         del q, k, v, o, lse, ws
+    out["clocks"] = sampler.stop()
     return out
 
 

@@ -268,7 +268,11 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
   // work item) unless its work items would not fill one wave of SMs; then
   // the tile kernel (one tile per item) doubles the CTAs.  Dual and decode
   // launches have one unit per row block either way.
-  k.q_tile = use_tile_kernel(static_cast<long long>((k.rows + 255) / 256) * B * k.heads);
+  // (with a workspace, an under-filled launch is split along the keys
+  // instead, which measured faster on the pair kernel: a 512-query causal
+  // chunk of an 8192-key cache 86-101 us against 151 us on the tile kernel)
+  k.q_tile = !allow_split &&
+             use_tile_kernel(static_cast<long long>((k.rows + 255) / 256) * B * k.heads);
   k.pair2 = use_pair2_kernel(k.q_tile, d, k.pack, k.rows);
   k.n_qpairs = k.q_tile  ? (k.rows + 127) / 128
                : k.pair2 ? (k.rows + 511) / 512
@@ -359,6 +363,20 @@ Plan make_plan(int B, int Hq, int Hkv, int Nq, int Nk, int d, bool allow_split) 
     k.n_splits = static_cast<int>((n + best_tps - 1) / best_tps);
     const long long n_work = units * k.n_splits;
     k.n_ctas = static_cast<int>(n_work < sms ? n_work : sms);
+  }
+  // Pair-kernel launches of many waves run persistent CTAs, one per SM: a
+  // CTA's next item starts its loads and first products while the current
+  // item's last tiles and epilogue finish.  Items are dealt out statically,
+  // so with few rounds uneven (causal) items leave some CTAs idle at the end
+  // that hardware scheduling of one CTA per item would have kept busy:
+  // measured on B200, C5 +2-4 % and C5 causal +3-7 % (27.7 rounds), C4 GQA
+  // causal -4 % (6.9 rounds), a causal 16-head N=8192 launch -25 % (3.5
+  // rounds); hence at least 16 rounds.
+  if (!k.dual && !k.decode && !k.q_tile && !k.pair2 && k.n_splits == 1 &&
+      (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_NO_PERSIST) == 0) {
+    constexpr long long kMinRounds = 16;
+    const long long n_work = static_cast<long long>(k.n_qpairs) * B * k.heads;
+    if (n_work >= kMinRounds * sms) k.n_ctas = sms;
   }
   if (k.n_splits > 1 || k.dual) {
     const size_t slots = static_cast<size_t>(k.n_splits) * (k.dual ? 2 : 1);
@@ -477,6 +495,7 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
       pt.n_qpairs = tiles;
       pt.item0 = (full / k.n_qpairs) * tiles + 2 * (full % k.n_qpairs);
       pt.item_end = 0;
+      pt.n_ctas = 0;  // one CTA per tile item
       e = fa::launch_fwd(pt, head_dim, bf16, s);
     }
   } else {

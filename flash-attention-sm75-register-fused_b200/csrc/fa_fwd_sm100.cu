@@ -441,6 +441,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   const int n_all = p.n_qpairs * p.B * p.heads * p.n_splits;
   const int n_work = p.item_end > 0 ? min(p.item_end, n_all) : n_all;
   const int w0 = p.item0 + static_cast<int>(blockIdx.x);
+  // Work item of this CTA's k-th round.  Persistent launches outside dual
+  // mode deal the rounds out boustrophedon-wise (odd rounds in reverse CTA
+  // order), so CTAs that got the heavier item of one round get a lighter
+  // one in the next (causal items are ordered heaviest first).
+  const bool snake = !dual && p.n_ctas > 0;
+  auto work_of = [&](int round) {
+    const int c = static_cast<int>(blockIdx.x), G = static_cast<int>(gridDim.x);
+    return p.item0 + round * G + ((snake && (round & 1)) ? (G - 1 - c) : c);
+  };
 
   // ---- set-up: skip the CTA if this launch already failed elsewhere
   if (threadIdx.x == 0) {
@@ -483,14 +492,14 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // so the next item's K/V tiles load while the current one computes.
       // Dual mode double-buffers Q (work item k uses buffer k & 1): loading
       // item k's Q waits until the MMAs of item k-2, which read that buffer,
-      // have completed.  Shared mode uses both Q buffers for its two tiles and
-      // is never launched with more than one item per CTA.
+      // have completed.  Shared mode uses Q buffer g for group g's tile; a
+      // persistent launch refills it after the previous item's last S_g.
       int ring = 0, k = 0, q_loads[2] = {0, 0};
 #ifdef FA_TRACE
       int pc[2] = {0, 0};  // dual mode: tiles of group g in earlier work items (trace rows)
 #endif
       bool ok = true;
-      for (int w = w0; ok && w < n_work; w += gridDim.x, ++k) {
+      for (int w = w0; ok && w < n_work; w = work_of(++k)) {
         WorkItem it;
         decode_item(p, w, it);
         if (!skip_q) {
@@ -506,9 +515,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
             if (qb) ++q_loads[1]; else ++q_loads[0];
           } else {
             // a group without K/V tiles needs no Q (the MMA warp waits for
-            // Q tile g only when n_kv[g] > 0)
-            for (int g = 0; g < 2; ++g) {
+            // Q tile g only when n_kv[g] > 0).  Persistent launches: Q buffer
+            // g is refilled once the previous item's last S_g has completed.
+            for (int g = 0; g < 2 && ok; ++g) {
               if (it.n_kv[g] == 0) continue;
+              if (q_loads[g] > 0 &&
+                  !(ok = bar_wait(bar(L::kBarQFree + g), (q_loads[g] - 1) & 1, wc, 3)))
+                break;
               ptx::mbar_arrive_expect_tx(bar(L::kBarQ + g), L::kTile);
               const int row = it.qy + it.q_row0 + g * kBlockM;
 #pragma unroll
@@ -523,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               }
               ++q_loads[g];
             }
+            if (!ok) break;
           }
         }
         for (int i = 0; i < it.n_items; ++i, ++ring) {
@@ -643,29 +657,35 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       bool ok = true;
       int ring = 0, k = 0;
       int cnt[2] = {0, 0};
-      for (int w = w0; ok && w < n_work; w += gridDim.x, ++k) {
+      int qc[2] = {0, 0};  // shared mode: Q loads of group g before the item
+      for (int w = w0; ok && w < n_work; w = work_of(++k)) {
         WorkItem it;
         decode_item(p, w, it);
         const int n_loop = it.n_loop;
         if (!dual) {
-          // one work item per CTA: Q tiles in buffers 0 / 1, phases from 0.
-          // A group without tiles in this split issues nothing; with no tiles
-          // at all the producer loads no K/V and this warp waits for nothing.
+          // Q tiles in buffers 0 / 1; ring items numbered from `ring`, barrier
+          // phases from cnt[g] and qc[g] (Q loads of group g so far), so a
+          // persistent CTA walks several items.  A group without tiles in this
+          // item issues nothing; with no tiles at all the producer loads no
+          // K/V and this warp waits for nothing.  After an item's last S_g,
+          // Q buffer g is released for the next item's Q tile.
           const bool g0 = it.n_kv[0] > 0;
           const bool g1 = it.n_kv[1] > 0;
           if (n_loop > 0) {
-            if (g0) ok = wait(bar(L::kBarQ), 0, 10);
-            if (ok && g1) ok = wait(bar(L::kBarQ + 1), 0, 10);
-            if (ok) ok = wait(bar(L::kBarFull + slot_of(0)), phase_of(0), 11);
+            if (g0) ok = wait(bar(L::kBarQ), qc[0] & 1, 10);
+            if (ok && g1) ok = wait(bar(L::kBarQ + 1), qc[1] & 1, 10);
+            if (ok) ok = wait(bar(L::kBarFull + slot_of(ring)), phase_of(ring), 11);
             if (ok) {
-              if (g0) issue_s(0, 0, q_desc0);
-              if (g1) issue_s(1, 0, q_desc1);  // K_0 is ring item 0 for both groups
-              commit(bar(L::kBarEmpty + slot_of(0)));  // K0 read by both groups
+              if (g0) issue_s(0, ring, q_desc0);
+              if (g1) issue_s(1, ring, q_desc1);  // K_0 is the item's first ring item
+              commit(bar(L::kBarEmpty + slot_of(ring)));  // K0 read by both groups
+              if (it.n_kv[0] == 1) commit(bar(L::kBarQFree));
+              if (it.n_kv[1] == 1) commit(bar(L::kBarQFree + 1));
             }
           }
           for (int j = 0; ok && j < n_loop; ++j) {
-            const int item_v = 2 * j + 1;
-            const int item_k = 2 * j + 2;  // K of tile j+1
+            const int item_v = ring + 2 * j + 1;
+            const int item_k = ring + 2 * j + 2;  // K of tile j+1
             const bool next0 = j + 1 < it.n_kv[0];
             const bool next1 = j + 1 < it.n_kv[1];
             // V_j and K_{j+1} are waited for before the P waits, so that a
@@ -681,26 +701,30 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
             if (lane == 0) FA_TRACE_AT(j, 7);
             if (j < it.n_kv[0]) {
               if (lane == 0) FA_TRACE_AT(j, 0);
-              if (!(ok = issue_pv(0, item_v, j == 0, j & 1))) break;
+              if (!(ok = issue_pv(0, item_v, j == 0, (cnt[0] + j) & 1))) break;
               if (lane == 0) FA_TRACE_AT(j, 4);
               if (next0) {
                 if (lane == 0) FA_TRACE_AT(j, 1);
                 issue_s(0, item_k, q_desc0);
                 if (lane == 0) FA_TRACE_AT(j, 5);
+                if (j + 2 == it.n_kv[0]) commit(bar(L::kBarQFree));  // the item's last S0
                 if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
               }
             }
             if (j < it.n_kv[1]) {
               if (lane == 0) FA_TRACE_AT(j, 2);
-              if (!(ok = issue_pv(1, item_v, j == 0, j & 1))) break;
+              if (!(ok = issue_pv(1, item_v, j == 0, (cnt[1] + j) & 1))) break;
             }
             commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
             if (next1) {
               if (lane == 0) FA_TRACE_AT(j, 3);
               issue_s(1, item_k, q_desc1);
+              if (j + 2 == it.n_kv[1]) commit(bar(L::kBarQFree + 1));  // the item's last S1
               commit(bar(L::kBarEmpty + slot_of(item_k)));
             }
           }
+          if (g0) ++qc[0];
+          if (g1) ++qc[1];
         } else {
           // Dual mode: each group streams its own K/V tiles (items from
           // k_item_of), so nothing waits for the other group's P; order per
@@ -789,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const float sl = p.scale_log2;
     bool ok = true;
     int cnt = 0;  // S / P / O completions of this group before the work item
-    for (int w = w0; ok && w < n_work; w += gridDim.x) {
+    for (int round = 0, w = w0; ok && w < n_work; w = work_of(++round)) {
     WorkItem it;
     decode_item(p, w, it);
     const int n_tiles = g ? it.n_kv[1] : it.n_kv[0];

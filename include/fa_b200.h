@@ -64,8 +64,10 @@ enum {
                                tile per CTA, S double-buffered), for comparisons */
   FA_DEBUG_PAIR2_KERNEL = 16, /* d = 128 square / chunked prefill on CTA pairs (one product
                                 for two SMs) wherever they apply (opt-in) */
-  FA_DEBUG_NO_TAIL_SPLIT = 32 /* keep a pair-kernel launch's half-empty last wave on the pair
-                                kernel instead of the tile kernel, for comparisons */
+  FA_DEBUG_NO_TAIL_SPLIT = 32, /* keep a pair-kernel launch's half-empty last wave on the pair
+                                 kernel instead of the tile kernel, for comparisons */
+  FA_DEBUG_NO_PERSIST = 64      /* one CTA per pair-kernel work item instead of persistent
+                                 CTAs, for comparisons */
 };
 
 /*

@@ -308,3 +308,29 @@ def test_wave_tail_items_on_the_tile_kernel(sm100, d):
         lib.fa_set_debug_flags(0)
     assert (o.float() - o2.float()).abs().max().item() <= 4e-3
     assert (lse - lse2).abs().max().item() <= 1e-4
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_persistent_pair_kernel_many_rounds(sm100, causal):
+    """A launch of >= 16 rounds of pair-kernel items runs persistent CTAs that
+    walk several items each (Q buffers refilled across items, barrier phases
+    running on): sampled rows of the first, middle and last heads match the
+    oracle and agree with one CTA per item."""
+    lib = abi.load()
+    cfg = orc.AttnConfig("t", 2, 600, 600, 512, 64, causal)  # 2400 items = 16.2 rounds
+    q, k, v = orc.make_inputs(cfg, seed=31)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o, lse = run(qd, kd, vd, causal)
+    rows = orc.sample_rows(512, 24, seed=3)
+    for b, h in ((0, 0), (0, 299), (1, 300), (1, 599)):
+        ref_o, ref_l = orc.attention_fp32(q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
+                                          v[b:b + 1, h:h + 1], causal=causal, rows=rows)
+        assert orc.check(o.cpu()[b:b + 1, h:h + 1, rows], ref_o)["ok"], (b, h)
+        assert orc.check_lse(lse.cpu()[b:b + 1, h:h + 1, rows], ref_l)["ok"], (b, h)
+    lib.fa_set_debug_flags(64)  # FA_DEBUG_NO_PERSIST
+    try:
+        o2, lse2 = run(qd, kd, vd, causal)
+    finally:
+        lib.fa_set_debug_flags(0)
+    assert torch.equal(o, o2)
+    assert torch.equal(lse, lse2)
