@@ -29,7 +29,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 KERNEL_SOURCES = ["fa_fwd_sm100.cu", "fa_abi.cu"]
 KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_softmax.cuh", "fa_fwd.h", "fa_bwd_sm100.cuh",
-                  "fa_decode_sm100.cuh"]
+                  "fa_decode_sm100.cuh", "fa_fwd_tile.cuh", "fa_fwd_pair2.cuh"]
 
 
 def _run(cmd, verbose):

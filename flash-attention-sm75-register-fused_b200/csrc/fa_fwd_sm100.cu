@@ -156,6 +156,18 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, const Wa
   return bar_wait_slow(bar, parity, c, site, respect_abort);
 }
 
+// The slow path as a call, for warps with registers to spare: their code
+// stays compact around every wait.
+__device__ __noinline__ bool bar_wait_slow_call(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                                int site, bool respect_abort) {
+  return bar_wait_slow(bar, parity, c, site, respect_abort);
+}
+__device__ __forceinline__ bool bar_wait_lean(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                              int site, bool respect_abort = true) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  return bar_wait_slow_call(bar, parity, c, site, respect_abort);
+}
+
 // Bounded wait that polls without suspending the thread: for short waits on
 // the critical path, where a suspended thread may resume late.  The timer is
 // read every 256 polls.
@@ -581,6 +593,14 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     // ===================================================== MMA issuer
     // The whole warp runs this loop so that addresses and descriptors stay
     // warp-uniform; one elected lane issues each batch of tcgen05 ops.
+    // This warp is on the critical path with few instructions to spare: one
+    // tcgen05.mma holds the issuing thread ~50 cycles (measured on B200, for
+    // N = 64 as for N = 128), and while the softmax warps of its
+    // sub-partition run their exponential loops it gets few issue slots, so
+    // every instruction costs several times its latency.  The loop therefore
+    // keeps the waits' slow path out of line (bar_wait_lean), advances ring
+    // slots and phases incrementally instead of dividing, and adds offsets to
+    // the low word of the descriptors only.
     {
       constexpr uint32_t fmt = BF16 ? 1u : 0u;
       constexpr uint32_t idesc_qk = ptx::make_idesc_f16(kBlockM, kBlockN, fmt, 0, 0);
@@ -588,20 +608,29 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 
       auto slot_of = [](int item) { return item % L::kSlots; };
       auto phase_of = [](int item) { return static_cast<uint32_t>((item / L::kSlots) & 1); };
-      // descriptor of the slot-0 K tile (K-major) and V tile (MN-major); a slot
-      // offset is added to the start-address field (16-byte units)
+      // Shared-memory descriptors of the slot-0 K tile (K-major), V tile
+      // (MN-major) and the two Q tiles.  The start address sits in bits 0-13
+      // of the low word and slot / K-step offsets never carry out of it
+      // (shared memory < 256 KB), so offsets are added to the low word; the
+      // high word (stride, version, swizzle) is the same for all four.
       const uint64_t k_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, 16, 1024);
       const uint64_t v_desc0 = ptx::smem_desc_sw128(sbase + L::kOffKV, L::kBlockBytes, 1024);
-      const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
-      const uint64_t q_desc1 = ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024);
-      // S_g = Q K^T with Q at descriptor qd and K in ring item `ki`
-      auto issue_s = [&](int g, int ki, uint64_t qd) {
-        const uint64_t kd = k_desc0 + static_cast<uint64_t>((slot_of(ki) * L::kTile) >> 4);
+      const uint32_t d_hi = static_cast<uint32_t>(k_desc0 >> 32);
+      const uint32_t k_lo0 = static_cast<uint32_t>(k_desc0);
+      const uint32_t v_lo0 = static_cast<uint32_t>(v_desc0);
+      const uint32_t q_lo0 = static_cast<uint32_t>(ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024));
+      const uint32_t q_lo1 =
+          static_cast<uint32_t>(ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024));
+      constexpr uint32_t kSlotStep = L::kTile >> 4;
+      // S_g = Q K^T with Q at descriptor low word q_lo and K in ring slot ks
+      auto issue_s = [&](int g, int ks, uint32_t q_lo) {
+        const uint32_t k_lo = k_lo0 + static_cast<uint32_t>(ks) * kSlotStep;
         if (ptx::elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t off = static_cast<uint64_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
-            ptx::mma_ss(tmem + L::tS(g), qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+            const uint32_t off = static_cast<uint32_t>(((kk / 4) * L::kBlockBytes + (kk % 4) * 32) >> 4);
+            ptx::mma_ss(tmem + L::tS(g), ptx::make_desc(q_lo + off, d_hi),
+                        ptx::make_desc(k_lo + off, d_hi), idesc_qk, kk > 0 ? 1u : 0u);
           }
           ptx::mma_commit(bar(L::kBarS + g));
         }
@@ -612,21 +641,21 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
         __syncwarp();
       };
       auto wait = [&](uint32_t b, uint32_t ph, int site) {
-        return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
+        return __all_sync(0xffffffffu, bar_wait_lean(b, ph, wc, site));
       };
       // O_g (+)= P_g V with V in ring item `vi`; `first` starts the accumulator.
       // The PV steps on the announced early part of P (2 K-steps per quarter)
       // go out once the softmax has announced it (parity ph), the rest after
       // the whole P.
-      auto issue_pv = [&](int g, int vi, bool first, uint32_t ph) -> bool {
-        const uint64_t vd = v_desc0 + static_cast<uint64_t>((slot_of(vi) * L::kTile) >> 4);
+      auto issue_pv = [&](int g, int vs, bool first, uint32_t ph) -> bool {
+        const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * kSlotStep;
         if (!wait(bar(L::kBarPH + g), ph, 13 + 3 * g)) return false;
         ptx::tc_fence_after();
         if (ptx::elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 2 * kPEarlyQuarters; ++kk)
             ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
-                        vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
+                        ptx::make_desc(v_lo + kk * 128u, d_hi), idesc_pv,
                         (!first || kk > 0) ? 1u : 0u);
         }
         __syncwarp();
@@ -636,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
 #pragma unroll
           for (int kk = 2 * kPEarlyQuarters; kk < kBlockN / 16; ++kk)
             ptx::mma_ts(tmem + L::tO(g), tmem + L::tP(g) + kk * 8,
-                        vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv, 1u);
+                        ptx::make_desc(v_lo + kk * 128u, d_hi), idesc_pv, 1u);
           ptx::mma_commit(bar(L::kBarO + g));
         }
         __syncwarp();
@@ -671,21 +700,37 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           // Q buffer g is released for the next item's Q tile.
           const bool g0 = it.n_kv[0] > 0;
           const bool g1 = it.n_kv[1] > 0;
+          // ring position (slot, phase) of K_j, advanced item by item instead
+          // of dividing the ring counter
+          int ks = slot_of(ring);
+          uint32_t kph = phase_of(ring);
+          auto adv = [](int& sl, uint32_t& ph) {
+            if (++sl == L::kSlots) {
+              sl = 0;
+              ph ^= 1u;
+            }
+          };
           if (n_loop > 0) {
             if (g0) ok = wait(bar(L::kBarQ), qc[0] & 1, 10);
             if (ok && g1) ok = wait(bar(L::kBarQ + 1), qc[1] & 1, 10);
-            if (ok) ok = wait(bar(L::kBarFull + slot_of(ring)), phase_of(ring), 11);
+            if (ok) ok = wait(bar(L::kBarFull + ks), kph, 11);
             if (ok) {
-              if (g0) issue_s(0, ring, q_desc0);
-              if (g1) issue_s(1, ring, q_desc1);  // K_0 is the item's first ring item
-              commit(bar(L::kBarEmpty + slot_of(ring)));  // K0 read by both groups
+              if (g0) issue_s(0, ks, q_lo0);
+              if (g1) issue_s(1, ks, q_lo1);  // K_0 is the item's first ring item
+              commit(bar(L::kBarEmpty + ks));  // K0 read by both groups
               if (it.n_kv[0] == 1) commit(bar(L::kBarQFree));
               if (it.n_kv[1] == 1) commit(bar(L::kBarQFree + 1));
             }
           }
           for (int j = 0; ok && j < n_loop; ++j) {
-            const int item_v = ring + 2 * j + 1;
-            const int item_k = ring + 2 * j + 2;  // K of tile j+1
+            int vs = ks;  // V_j
+            uint32_t vph = kph;
+            adv(vs, vph);
+            int ns = vs;  // K_{j+1}
+            uint32_t nph = vph;
+            adv(ns, nph);
+            ks = ns;
+            kph = nph;
             const bool next0 = j + 1 < it.n_kv[0];
             const bool next1 = j + 1 < it.n_kv[1];
             // V_j and K_{j+1} are waited for before the P waits, so that a
@@ -694,33 +739,31 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
             // committed in an earlier iteration, so these waits cannot depend
             // on this one.
             if (lane == 0) FA_TRACE_AT(j, 6);
-            if (!(ok = wait(bar(L::kBarFull + slot_of(item_v)), phase_of(item_v), 12))) break;
-            if ((next0 || next1) &&
-                !(ok = wait(bar(L::kBarFull + slot_of(item_k)), phase_of(item_k), 14)))
-              break;
+            if (!(ok = wait(bar(L::kBarFull + vs), vph, 12))) break;
+            if ((next0 || next1) && !(ok = wait(bar(L::kBarFull + ns), nph, 14))) break;
             if (lane == 0) FA_TRACE_AT(j, 7);
             if (j < it.n_kv[0]) {
               if (lane == 0) FA_TRACE_AT(j, 0);
-              if (!(ok = issue_pv(0, item_v, j == 0, (cnt[0] + j) & 1))) break;
+              if (!(ok = issue_pv(0, vs, j == 0, (cnt[0] + j) & 1))) break;
               if (lane == 0) FA_TRACE_AT(j, 4);
               if (next0) {
                 if (lane == 0) FA_TRACE_AT(j, 1);
-                issue_s(0, item_k, q_desc0);
+                issue_s(0, ns, q_lo0);
                 if (lane == 0) FA_TRACE_AT(j, 5);
                 if (j + 2 == it.n_kv[0]) commit(bar(L::kBarQFree));  // the item's last S0
-                if (!next1) commit(bar(L::kBarEmpty + slot_of(item_k)));
+                if (!next1) commit(bar(L::kBarEmpty + ns));
               }
             }
             if (j < it.n_kv[1]) {
               if (lane == 0) FA_TRACE_AT(j, 2);
-              if (!(ok = issue_pv(1, item_v, j == 0, (cnt[1] + j) & 1))) break;
+              if (!(ok = issue_pv(1, vs, j == 0, (cnt[1] + j) & 1))) break;
             }
-            commit(bar(L::kBarEmpty + slot_of(item_v)));  // V_j read by both groups
+            commit(bar(L::kBarEmpty + vs));  // V_j read by both groups
             if (next1) {
               if (lane == 0) FA_TRACE_AT(j, 3);
-              issue_s(1, item_k, q_desc1);
+              issue_s(1, ns, q_lo1);
               if (j + 2 == it.n_kv[1]) commit(bar(L::kBarQFree + 1));  // the item's last S1
-              commit(bar(L::kBarEmpty + slot_of(item_k)));
+              commit(bar(L::kBarEmpty + ns));
             }
           }
           if (g0) ++qc[0];
@@ -731,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
           // iteration PV0(j) S0(j+1) PV1(j) S1(j+1), items released after use.
           // Both groups read Q buffer k & 1.
           const int qb = k & 1;
-          const uint64_t qd = qb ? q_desc1 : q_desc0;
+          const uint32_t q_lo = qb ? q_lo1 : q_lo0;
           if (n_loop > 0) {
             ok = wait(bar(L::kBarQ + qb), (k >> 1) & 1, 10);
 #pragma unroll
@@ -739,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               if (!ok || it.n_kv[g] == 0) continue;
               const int ki = ring + k_item_of(it, true, g, 0);
               if (!(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 11))) break;
-              issue_s(g, ki, qd);
+              issue_s(g, slot_of(ki), q_lo);
               commit(bar(L::kBarEmpty + slot_of(ki)));
             }
           }
@@ -753,12 +796,12 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
               if (!(ok = wait(bar(L::kBarFull + slot_of(vi)), phase_of(vi), 12))) break;
               if (next && !(ok = wait(bar(L::kBarFull + slot_of(ki)), phase_of(ki), 14))) break;
               if (lane == 0) FA_TRACE_AT((cnt[g] + j) & 63, 2 * g);  // V_j and K_{j+1} landed
-              if (!(ok = issue_pv(g, vi, j == 0, (cnt[g] + j) & 1))) break;
+              if (!(ok = issue_pv(g, slot_of(vi), j == 0, (cnt[g] + j) & 1))) break;
               if (lane == 0) FA_TRACE_AT((cnt[g] + j) & 63, 4 + g);  // P(j) seen, PV issued
               commit(bar(L::kBarEmpty + slot_of(vi)));
               if (next) {
                 if (lane == 0) FA_TRACE_AT((cnt[g] + j) & 63, 1 + 2 * g);
-                issue_s(g, ki, qd);
+                issue_s(g, slot_of(ki), q_lo);
                 commit(bar(L::kBarEmpty + slot_of(ki)));
               }
             }

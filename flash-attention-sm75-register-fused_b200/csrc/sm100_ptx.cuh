@@ -517,6 +517,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// A 64-bit descriptor from its two 32-bit words.
+__device__ __forceinline__ uint64_t make_desc(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+
 // Descriptor of a K-major tile without swizzling: 8-row x 16-byte core
 // matrices, `lbo_bytes` apart along K and `sbo_bytes` apart along M/N
 // (layout field 0).
