@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dkdv_kernel(const __gri
     auto slot_of = [](int i) { return i % L::kSlots; };
     auto phase_of = [](int i) { return static_cast<uint32_t>((i / L::kSlots) & 1); };
     auto wait = [&](uint32_t bb, uint32_t ph, int site) {
-      return __all_sync(0xffffffffu, bar_wait(bb, ph, wc, site));
+      return __all_sync(0xffffffffu, bar_wait_lean(bb, ph, wc, site));
     };
     const uint64_t k_desc = ptx::smem_desc_sw128(sbase + L::kOffFix, 16, 1024);
     const uint64_t v_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
@@ -682,7 +682,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) fa_bwd_dq_kernel(const __grid_
     auto slot_of = [](int i) { return i % L::kSlots; };
     auto phase_of = [](int i) { return static_cast<uint32_t>((i / L::kSlots) & 1); };
     auto wait = [&](uint32_t bb, uint32_t ph, int site) {
-      return __all_sync(0xffffffffu, bar_wait(bb, ph, wc, site));
+      return __all_sync(0xffffffffu, bar_wait_lean(bb, ph, wc, site));
     };
     const uint64_t do_desc = ptx::smem_desc_sw128(sbase + L::kOffFix + L::kTile, 16, 1024);
     const uint64_t ring_k = ptx::smem_desc_sw128(sbase + L::kOffRing, 16, 1024);

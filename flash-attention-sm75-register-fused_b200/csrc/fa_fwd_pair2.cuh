@@ -204,11 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_pair2_kernel(const __grid_
       const uint64_t q_desc0 = ptx::smem_desc_sw128(sbase + L::kOffQ, 16, 1024);
       const uint64_t q_desc1 = ptx::smem_desc_sw128(sbase + L::kOffQ + L::kTile, 16, 1024);
       auto wait = [&](uint32_t b, uint32_t ph, int site) {
-        return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
+        return __all_sync(0xffffffffu, bar_wait_lean(b, ph, wc, site));
       };
-      auto wait_c = [&](uint32_t b, uint32_t ph, int site) {
-        return __all_sync(0xffffffffu, bar_wait(b, ph, wc, site));
-      };
+      auto wait_c = wait;
       auto commit = [&](uint32_t b) {
         if (ptx::elect_one()) ptx::mma_commit_pair(b, kBoth);
         __syncwarp();
