@@ -19,6 +19,13 @@
 namespace {
 
 std::atomic<unsigned> g_epoch{1};
+// Numbers of persistent launches with dynamically dealt last rounds (never 0:
+// a counter slot tagged 0 is unused).
+std::atomic<unsigned> g_sched{1};
+unsigned next_sched() {
+  const unsigned v = g_sched.fetch_add(1, std::memory_order_relaxed);
+  return v != 0u ? v : g_sched.fetch_add(1, std::memory_order_relaxed);
+}
 std::atomic<unsigned long long> g_timeout_ns{1000000000ull};
 std::atomic<int> g_debug_flags{0};
 std::atomic<long long*> g_trace{nullptr};
@@ -470,6 +477,22 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.trace = g_trace.load(std::memory_order_relaxed);
   p.epoch = g_epoch.fetch_add(1, std::memory_order_relaxed);
   p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+  // Persistent shared-mode launches deal their last kDynRounds rounds from a
+  // device-wide counter, so CTAs that drew lighter items take more of the
+  // last ones (measured on B200: C5 causal +1.5 %, C5 +0.9 %; 1 or 4 dynamic
+  // rounds gained less).
+  constexpr int kDynRounds = 2;
+  p.sched = 0;
+  p.sched_round = 0;
+  if (!k.decode && p.n_ctas > 0 && p.dual == 0 &&
+      (p.debug_flags & FA_DEBUG_STATIC_DEAL) == 0) {
+    const long long items = static_cast<long long>(k.n_qpairs) * B * k.heads * k.n_splits;
+    const int rounds = static_cast<int>((items + p.n_ctas - 1) / p.n_ctas);
+    if (rounds > kDynRounds) {
+      p.sched = next_sched();
+      p.sched_round = rounds - kDynRounds;
+    }
+  }
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Wave tail: a non-causal pair-kernel launch of several waves whose last
   // wave is at most half full runs those last items on the tile kernel, as
@@ -578,6 +601,8 @@ int launch_ranged(bool packed, const void* Q, const void* K, const void* V, void
   p.n_ctas = 0;
   p.item0 = 0;
   p.item_end = 0;
+  p.sched = 0;
+  p.sched_round = 0;
   p.ws_o = nullptr;
   p.ws_lse = nullptr;
   p.scale_log2 = scale * 1.4426950408889634f;

@@ -43,6 +43,12 @@ struct alignas(64) FwdParams {
   // all); a launch may cover a sub-range, e.g. the last items of a pair-kernel
   // launch handed to the tile kernel as twice as many one-tile items.
   int item0, item_end;
+  // Persistent shared-mode launches (n_ctas > 0, dual = 0) with sched != 0:
+  // rounds >= sched_round take their items from a device-wide counter (slot
+  // sched % kSchedSlots, tagged with sched) instead of the boustrophedon
+  // deal, so the CTAs that drew lighter items take more of the last ones.
+  unsigned sched;
+  int sched_round;
   float* ws_o;       // partial O [n_splits * (1 + dual)][B*heads][Nq][d] fp32 (normalised)
   float* ws_lse;     // partial LSE [n_splits * (1 + dual)][B*heads][Nq] (natural log)
   float scale_log2;  // scale * log2(e)

@@ -46,6 +46,15 @@ namespace fa {
 // Written only when a bounded wait expires; read by fa_device_status().
 __device__ unsigned long long g_fa_status = 0ull;
 
+// Work-item counters of persistent launches whose last rounds are dealt
+// dynamically: slot sched % kSchedSlots holds (sched << 32) | items handed
+// out.  A launch starts its slot by replacing a value tagged with another
+// launch's number, so no reset is needed between launches; 256 slots keep
+// launches whose CTAs run at the same time apart (the host numbers these
+// launches on their own counter).
+constexpr unsigned kSchedSlots = 256;
+__device__ unsigned long long g_fa_sched[kSchedSlots];
+
 namespace {
 
 constexpr int kBlockM = 128;  // query rows per tile (one TMEM lane each)
@@ -96,9 +105,16 @@ struct Layout {
   // early part of P_g written (kPEarlyQuarters x 32 keys): the PV MMA starts
   // on it while the softmax computes the rest (128 arrivals)
   static constexpr int kBarPH = kBarQFree + 2;          // 2
-  static constexpr int kNumBars = kBarPH + 2;
+  // dynamically dealt rounds: the producer publishes each round's work item
+  // in a 4-entry queue (full: producer arrival; empty: every softmax thread
+  // and lane 0 of the MMA warp have read it)
+  static constexpr int kItemQ = 4;
+  static constexpr int kBarItemFull = kBarPH + 2;               // kItemQ
+  static constexpr int kBarItemEmpty = kBarItemFull + kItemQ;   // kItemQ
+  static constexpr int kNumBars = kBarItemEmpty + kItemQ;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
-  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kOffItemQ = kOffMisc + 16;               // kItemQ ints
+  static constexpr int kBytes = kOffItemQ + 4 * kItemQ;
   static constexpr int kDynBytes = kBytes + 1024;  // slack for 1024-byte alignment
   // tensor memory columns
   static constexpr uint32_t kTmemCols = 512;
@@ -131,6 +147,25 @@ __device__ void record_error(unsigned epoch, int code) {
     if (prev == old) return;
     old = prev;
   }
+}
+
+// Next work-item number of launch `sched` from its counter slot (0, 1, 2, ...
+// in the order of the calls across the launch's CTAs), or -1 (error recorded,
+// CTA aborting) if the counter could not be updated after many attempts.
+__device__ int sched_take(unsigned sched, const WaitCtl& c) {
+  unsigned long long* ctr = &g_fa_sched[sched % kSchedSlots];
+  unsigned long long v = atomicAdd(ctr, 0ull);
+  for (int i = 0; i < (1 << 20); ++i) {
+    const bool mine = static_cast<unsigned>(v >> 32) == sched;
+    const unsigned long long nv =
+        mine ? v + 1ull : ((static_cast<unsigned long long>(sched) << 32) | 1ull);
+    const unsigned long long prev = atomicCAS(ctr, v, nv);
+    if (prev == v) return mine ? static_cast<int>(v & 0xffffffffull) : 0;
+    v = prev;
+  }
+  *c.abort = 1;
+  record_error(c.epoch, FA_ERR_TIMEOUT_BASE + 6);
+  return -1;
 }
 
 __device__ __forceinline__ bool bar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& c,
@@ -471,7 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       // P completes on an arrival of every thread of a softmax group
       const bool is_p = (i == L::kBarP || i == L::kBarP + 1 || i == L::kBarPH ||
                          i == L::kBarPH + 1);
-      ptx::mbar_init(bar(i), is_p ? 128u : 1u);
+      const bool is_item_empty = i >= L::kBarItemEmpty && i < L::kBarItemEmpty + L::kItemQ;
+      ptx::mbar_init(bar(i), is_p ? 128u : is_item_empty ? 257u : 1u);
     }
     ptx::fence_barrier_init();
   }
@@ -487,6 +523,46 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const WaitCtl wc{abort_flag, p.timeout_ns, p.epoch};
   if (threadIdx.x == 0) FA_TRACE_AT(kTraceTiles - 1, 30);  // CTA set up
+
+  // Rounds >= p.sched_round of a persistent shared-mode launch with
+  // p.sched != 0 are dealt dynamically: this CTA's producer takes the next
+  // number n from the launch's counter (item item0 + sched_round * G + n)
+  // when it moves on, and publishes it in a shared 4-entry queue that the
+  // MMA warp and the softmax groups read; a number >= n_work (the items ran
+  // out) ends every role's loop.  Round r uses queue entry
+  // (r - sched_round) % kItemQ.  Earlier rounds keep the static deal: CTAs
+  // that run their rounds in step read the same heads' K/V at the same time
+  // (measured: dealing every round dynamically balanced C5 causal perfectly
+  // but ran 8 % slower, 2 % of it the queue hand-offs).
+  const bool dyn = snake && p.sched != 0u;
+  volatile int* item_q = reinterpret_cast<volatile int*>(smem + L::kOffItemQ);
+  auto produce_item = [&](int round, bool& ok) -> int {
+    if (!dyn || round < p.sched_round) return work_of(round);
+    if (!ok) return n_work;
+    const int q = round - p.sched_round, qs = q % L::kItemQ;
+    if (q >= L::kItemQ &&
+        !(ok = bar_wait(bar(L::kBarItemEmpty + qs), ((q / L::kItemQ) - 1) & 1, wc, 4)))
+      return n_work;
+    const int n = sched_take(p.sched, wc);
+    if (n < 0) ok = false;
+    const int w = n < 0 ? n_work : p.item0 + p.sched_round * static_cast<int>(gridDim.x) + n;
+    item_q[qs] = w;
+    ptx::mbar_arrive(bar(L::kBarItemFull + qs));  // release: the entry is visible to waiters
+    return w;
+  };
+  // Every thread of the calling warp waits and reads; threads with `arrive`
+  // (each softmax thread, lane 0 of the MMA warp: 257 arrivals) release it.
+  auto consume_item = [&](int round, bool& ok, bool arrive) -> int {
+    if (!dyn || round < p.sched_round) return work_of(round);
+    if (!ok) return n_work;
+    const int q = round - p.sched_round, qs = q % L::kItemQ;
+    if (!(ok = __all_sync(0xffffffffu, bar_wait(bar(L::kBarItemFull + qs), (q / L::kItemQ) & 1,
+                                                wc, 5))))
+      return n_work;
+    const int w = item_q[qs];
+    if (arrive) ptx::mbar_arrive(bar(L::kBarItemEmpty + qs));
+    return w;
+  };
 
   if (warp < kWarpSoftmax0 || warp >= kWarpSoftmax0 + 8) {
    // ------------------------------------------------ producer warpgroup
@@ -511,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       int pc[2] = {0, 0};  // dual mode: tiles of group g in earlier work items (trace rows)
 #endif
       bool ok = true;
-      for (int w = w0; ok && w < n_work; w = work_of(++k)) {
+      for (int w = w0; ok && w < n_work; w = produce_item(++k, ok)) {
         WorkItem it;
         decode_item(p, w, it);
         if (!skip_q) {
@@ -687,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       int ring = 0, k = 0;
       int cnt[2] = {0, 0};
       int qc[2] = {0, 0};  // shared mode: Q loads of group g before the item
-      for (int w = w0; ok && w < n_work; w = work_of(++k)) {
+      for (int w = w0; ok && w < n_work; w = consume_item(++k, ok, lane == 0)) {
         WorkItem it;
         decode_item(p, w, it);
         const int n_loop = it.n_loop;
@@ -856,7 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const float sl = p.scale_log2;
     bool ok = true;
     int cnt = 0;  // S / P / O completions of this group before the work item
-    for (int round = 0, w = w0; ok && w < n_work; w = work_of(++round)) {
+    for (int round = 0, w = w0; ok && w < n_work; w = consume_item(++round, ok, true)) {
     WorkItem it;
     decode_item(p, w, it);
     const int n_tiles = g ? it.n_kv[1] : it.n_kv[0];

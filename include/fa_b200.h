@@ -66,8 +66,10 @@ enum {
                                 for two SMs) wherever they apply (opt-in) */
   FA_DEBUG_NO_TAIL_SPLIT = 32, /* keep a pair-kernel launch's half-empty last wave on the pair
                                  kernel instead of the tile kernel, for comparisons */
-  FA_DEBUG_NO_PERSIST = 64      /* one CTA per pair-kernel work item instead of persistent
+  FA_DEBUG_NO_PERSIST = 64,     /* one CTA per pair-kernel work item instead of persistent
                                  CTAs, for comparisons */
+  FA_DEBUG_STATIC_DEAL = 128    /* persistent pair-kernel CTAs deal every round in the fixed
+                                 boustrophedon order (the last rounds too), for comparisons */
 };
 
 /*

@@ -314,8 +314,10 @@ def test_wave_tail_items_on_the_tile_kernel(sm100, d):
 def test_persistent_pair_kernel_many_rounds(sm100, causal):
     """A launch of >= 16 rounds of pair-kernel items runs persistent CTAs that
     walk several items each (Q buffers refilled across items, barrier phases
-    running on): sampled rows of the first, middle and last heads match the
-    oracle and agree with one CTA per item."""
+    running on; the last two rounds taken from the device-wide counter):
+    sampled rows of the first, middle and last heads match the oracle and
+    agree bit for bit with one CTA per item and with every round dealt
+    statically (an item skipped or dealt twice would show)."""
     lib = abi.load()
     cfg = orc.AttnConfig("t", 2, 600, 600, 512, 64, causal)  # 2400 items = 16.2 rounds
     q, k, v = orc.make_inputs(cfg, seed=31)
@@ -327,10 +329,12 @@ def test_persistent_pair_kernel_many_rounds(sm100, causal):
                                           v[b:b + 1, h:h + 1], causal=causal, rows=rows)
         assert orc.check(o.cpu()[b:b + 1, h:h + 1, rows], ref_o)["ok"], (b, h)
         assert orc.check_lse(lse.cpu()[b:b + 1, h:h + 1, rows], ref_l)["ok"], (b, h)
-    lib.fa_set_debug_flags(64)  # FA_DEBUG_NO_PERSIST
-    try:
-        o2, lse2 = run(qd, kd, vd, causal)
-    finally:
-        lib.fa_set_debug_flags(0)
-    assert torch.equal(o, o2)
-    assert torch.equal(lse, lse2)
+    for flag in (64, 128):  # FA_DEBUG_NO_PERSIST, FA_DEBUG_STATIC_DEAL
+        lib.fa_set_debug_flags(flag)
+        try:
+            o2, lse2 = run(qd, kd, vd, causal)
+        finally:
+            lib.fa_set_debug_flags(0)
+        assert torch.equal(o, o2), flag
+        assert torch.equal(lse, lse2), flag
+    assert lib.fa_device_status(0) == 0
