@@ -498,10 +498,15 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   // wave is at most half full runs those last items on the tile kernel, as
   // twice as many one-tile items (each ~0.6 of a pair item's time), so the
   // last wave ends sooner.  (C5 sharded over 8 GPUs: 512 items, 3.46 waves.)
+  // d = 128 only: at d = 64 the tile kernel runs a tile at more than 0.6 of
+  // a pair item's time and the second launch costs more than it saves
+  // (measured: C2, 192 items = 1.3 waves, 345 TFLOPS with the last 44 items
+  // on the pair kernel against 331 with the split).
   const long long n_items = static_cast<long long>(k.n_qpairs) * B * k.heads * k.n_splits;
   const int sms = sm_count();
   const long long rem = n_items % sms;
-  const bool tail = !k.decode && !k.dual && !k.q_tile && !k.pair2 && k.n_splits == 1 &&
+  const bool tail = head_dim == 128 && !k.decode && !k.dual && !k.q_tile && !k.pair2 &&
+                    k.n_splits == 1 &&
                     p.causal == 0 && n_items > sms && rem > 0 && 2 * rem <= sms &&
                     (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_NO_TAIL_SPLIT) == 0;
   cudaError_t e;
