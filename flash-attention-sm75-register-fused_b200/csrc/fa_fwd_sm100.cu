@@ -289,7 +289,7 @@ static_assert(kPEarlyQuarters >= 1 && kPEarlyQuarters <= 3, "early part of P: 1-
 // f16/bf16 values go to TMEM (P operand of the PV MMA) in four 16-column
 // quarters, the first kPEarlyQuarters announced (`announce()`, an mbarrier
 // arrival) as soon as they are written; returns their fp32 sum.
-template <bool BF16, bool kEmulate, typename Announce>
+template <bool BF16, bool kEmulate, int kPeriod = kEmuPeriod, typename Announce>
 __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, float neg_m,
                                           uint32_t tP, Announce announce) {
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
@@ -300,7 +300,7 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
     for (int c = 0; c < 16; ++c) {
       const int i = 32 * h + 2 * c;
       float e0, e1;
-      exp2_pair<kEmulate>(c, x[i], x[i + 1], sl, neg_m, e0, e1);
+      exp2_pair<kEmulate, kPeriod>(c, x[i], x[i + 1], sl, neg_m, e0, e1);
       if (c & 1)
         ptx::fadd2(b0, b1, b0, b1, e0, e1);
       else
@@ -317,6 +317,18 @@ __device__ __forceinline__ float exp_tile(const float (&x)[kBlockN], float sl, f
   ptx::fadd2(a0, a1, a0, a1, b0, b1);
   return a0 + a1;
 }
+
+// Period of the pair kernel's exponential emulation pattern (one pair in
+// kPairEmuPeriod on the polynomial): 1 in 8 at d = 128, 1 in 4 at d = 64.
+// Measured on B200, interleaved runs: 1 in 8 against 1 in 4 gave C5 +2.5 %,
+// C4 +0.6 %, C3 (d = 64) -1.7 %; 3 in 8 and 1 in 2 were slower everywhere
+// (C5 -2 % / -11 %, C3 -7 % / -16 %): every polynomial adds softmax
+// instructions that compete with the MMA warp for issue slots.
+#ifndef FA_EMU_PERIOD_D128
+#define FA_EMU_PERIOD_D128 8
+#endif
+template <int D>
+constexpr int kPairEmuPeriod = (D == 128) ? FA_EMU_PERIOD_D128 : kEmuPeriod;
 
 // One unit of work of a CTA: a (batch*head, Q pair, key split) triple, with
 // the K/V tiles each softmax group processes.  A launch has n_work of them;
@@ -1043,7 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
       const uint32_t half_bar = bar(L::kBarPH + g);
       auto announce = [half_bar] { ptx::mbar_arrive(half_bar); };
       const float tile_sum = masked ? exp_tile<BF16, false>(x, sl_eff, neg_m, tP, announce)
-                                    : exp_tile<BF16, true>(x, sl_eff, neg_m, tP, announce);
+                                    : exp_tile<BF16, true, kPairEmuPeriod<D>>(x, sl_eff, neg_m, tP, announce);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       if (lane == 0) FA_TRACE_AT(dual ? ((cnt + j) & 63) : j, 8 + sw);

@@ -58,12 +58,14 @@ __device__ __forceinline__ float row_extreme(const float (&x)[N]) {
 // (e0, e1) = exp2(x0 * sl - m), exp2(x1 * sl - m) for pair c of a 16-pair
 // quarter (neg_m = -m): one packed FMA, then MUFU ex2 or, for the pairs the
 // emulation pattern selects (kEmulate), the degree-3 polynomial.
-template <bool kEmulate>
+// kPeriod overrides the period of the pattern (the count stays kEmuCount).
+template <bool kEmulate, int kPeriod = kEmuPeriod>
 __device__ __forceinline__ void exp2_pair(int c, float x0, float x1, float sl, float neg_m,
                                           float& e0, float& e1) {
+  static_assert(kPeriod > kEmuCount, "emulation pattern");
   float t0, t1;
   ptx::ffma2(t0, t1, x0, x1, sl, sl, neg_m, neg_m);
-  if (kEmulate && (c % kEmuPeriod) >= kEmuPeriod - kEmuCount) {
+  if (kEmulate && (c % kPeriod) >= kPeriod - kEmuCount) {
     ptx::exp2_poly2(e0, e1, t0, t1);
   } else {
     e0 = ptx::ex2_approx(t0);
