@@ -341,3 +341,30 @@ def test_persistent_pair_kernel_many_rounds(sm100, causal):
         assert torch.equal(o, o2), flag
         assert torch.equal(lse, lse2), flag
     assert lib.fa_device_status(0) == 0
+
+
+def test_persistent_two_waves_d64(sm100):
+    """A non-causal d=64 launch of between one and two waves of pair items
+    (C2's shape: 48 heads x 4 Q pairs = 192 items on 148 SMs) runs persistent
+    CTAs, some of which walk two items: every head matches the oracle on
+    sampled rows and the result equals one CTA per item bit for bit."""
+    lib = abi.load()
+    cfg = orc.AttnConfig("t", 4, 12, 12, 1024, 64, False)
+    q, k, v = orc.make_inputs(cfg, seed=33)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o, lse = run(qd, kd, vd, False)
+    rows = orc.sample_rows(1024, 16, seed=4)
+    for b in range(4):
+        for h in (0, 5, 11):
+            ref_o, ref_l = orc.attention_fp32(q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
+                                              v[b:b + 1, h:h + 1], rows=rows)
+            assert orc.check(o.cpu()[b:b + 1, h:h + 1, rows], ref_o)["ok"], (b, h)
+            assert orc.check_lse(lse.cpu()[b:b + 1, h:h + 1, rows], ref_l)["ok"], (b, h)
+    lib.fa_set_debug_flags(64)  # FA_DEBUG_NO_PERSIST
+    try:
+        o2, lse2 = run(qd, kd, vd, False)
+    finally:
+        lib.fa_set_debug_flags(0)
+    assert torch.equal(o, o2)
+    assert torch.equal(lse, lse2)
+    assert lib.fa_device_status(0) == 0
