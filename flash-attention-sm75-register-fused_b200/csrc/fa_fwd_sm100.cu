@@ -351,12 +351,10 @@ struct WorkItem {
 // the epilogue rather than kept live through the softmax loop.
 // Work item (without its split) -> (Q pair from the heavy end, batch*head).
 // Non-causal: head-major.  Causal pairs differ in work: items go pair-major
-// within groups of kFwdHeadGroup heads and head-major across groups, so each
+// within groups of p.head_group heads and head-major across groups, so each
 // group starts its heaviest pairs first while the CTAs that run together
-// still share a few heads' K/V in L2 (measured: C4 causal +12 % against
-// head-major order with groups of 8, +5 % with 4; fully pair-major order
-// loses the L2 sharing and was slower).
-constexpr int kFwdHeadGroup = 8;
+// still share a few heads' K/V in L2 (the host picks the group size:
+// kFwdHeadGroup, or all heads for launches of at most two waves).
 __device__ __forceinline__ void item_order(const FwdParams& p, int rest, int& qp_heavy, int& bh) {
   if (!p.causal) {
     qp_heavy = rest % p.n_qpairs;
@@ -364,12 +362,13 @@ __device__ __forceinline__ void item_order(const FwdParams& p, int rest, int& qp
     return;
   }
   const int n_heads = p.B * p.heads;
-  const int per_group = kFwdHeadGroup * p.n_qpairs;
+  const int hg = max(p.head_group, 1);
+  const int per_group = hg * p.n_qpairs;
   const int g = rest / per_group;
   const int r = rest % per_group;
-  const int g_heads = min(kFwdHeadGroup, n_heads - g * kFwdHeadGroup);
+  const int g_heads = min(hg, n_heads - g * hg);
   qp_heavy = r / g_heads;
-  bh = g * kFwdHeadGroup + r % g_heads;
+  bh = g * hg + r % g_heads;
 }
 
 __device__ __forceinline__ void item_out(const FwdParams& p, int w, long long& o_row0,
