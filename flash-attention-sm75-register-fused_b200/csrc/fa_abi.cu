@@ -466,12 +466,14 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   p.tiles_per_split = k.tiles_per_split;
   p.dual = k.dual ? 1 : 0;
   p.n_ctas = k.n_ctas;
-  // A non-causal d = 64 launch of more than one and at most two waves of
-  // pair items also runs persistent CTAs: the second item of a CTA loads
-  // while its first finishes, instead of a fresh CTA starting up in the
-  // second wave (measured on B200: C2, 192 items, 342-345 -> 349-357 TFLOPS;
-  // launches of 3.5 and 6.9 rounds measured no gain or a loss).
-  if (head_dim == 64 && p.causal == 0 && p.n_ctas == 0 && !k.dual && !k.decode && !k.q_tile &&
+  // A d = 64 launch of more than one and at most two waves of pair items
+  // also runs persistent CTAs: the second item of a CTA loads while its
+  // first finishes, instead of a fresh CTA starting up in the second wave;
+  // causal items (heaviest first) are dealt boustrophedon-wise, so a CTA's
+  // second item is one of the lightest (measured on B200: C2, 192 items,
+  // 342-345 -> 349-357 TFLOPS; C3 causal, 256 items, 417 -> 433;
+  // non-causal launches of 3.5 and 6.9 rounds measured no gain or a loss).
+  if (head_dim == 64 && p.n_ctas == 0 && !k.dual && !k.decode && !k.q_tile &&
       !k.pair2 && k.n_splits == 1 &&
       (g_debug_flags.load(std::memory_order_relaxed) & FA_DEBUG_NO_PERSIST) == 0) {
     const long long n_items = static_cast<long long>(k.n_qpairs) * B * k.heads;

@@ -62,9 +62,27 @@ SMALL = [
     (1, 1, 1, 257, 128, False), (2, 3, 3, 384, 64, False), (1, 2, 2, 512, 128, True),
     (1, 1, 1, 1000, 64, True), (2, 2, 2, 1024, 128, False), (1, 8, 8, 1024, 64, True),
     (1, 8, 2, 640, 128, True), (2, 6, 1, 333, 64, False), (1, 4, 4, 2048, 128, True),
-    # causal work items group 8 heads: 10 and 18 heads leave a partial last group
+    # head counts that are no multiple of the causal launch-order group
     (2, 5, 5, 700, 64, True), (3, 6, 2, 900, 128, True),
 ]
+
+
+def test_causal_partial_head_group_many_waves(sm100):
+    """A causal launch of more than two waves orders its items pair-major in
+    groups of 8 heads: 18 heads x 17 Q pairs = 306 items on 148 SMs leave a
+    partial last group of 2 heads, whose rows (and the others') match the
+    oracle on sampled rows."""
+    c = orc.AttnConfig("t", 1, 18, 6, 4352, 128, True)
+    q, k, v = orc.make_inputs(c, seed=17)
+    o, lse = run(q.cuda(), k.cuda(), v.cuda(), True)
+    o, lse = o.cpu(), lse.cpu()
+    rows = orc.sample_rows(c.N, 24, seed=5)
+    for h in (0, 7, 8, 15, 16, 17):
+        hk = h // 3
+        ref_o, ref_l = orc.attention_fp32(q[:, h:h + 1], k[:, hk:hk + 1], v[:, hk:hk + 1],
+                                          causal=True, rows=rows)
+        assert orc.check(o[:, h:h + 1, rows], ref_o)["ok"], h
+        assert orc.check_lse(lse[:, h:h + 1, rows], ref_l)["ok"], h
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,N,d,causal", SMALL)
@@ -343,26 +361,28 @@ def test_persistent_pair_kernel_many_rounds(sm100, causal):
     assert lib.fa_device_status(0) == 0
 
 
-def test_persistent_two_waves_d64(sm100):
-    """A non-causal d=64 launch of between one and two waves of pair items
-    (C2's shape: 48 heads x 4 Q pairs = 192 items on 148 SMs) runs persistent
-    CTAs, some of which walk two items: every head matches the oracle on
-    sampled rows and the result equals one CTA per item bit for bit."""
+@pytest.mark.parametrize("H,N,causal", [(12, 1024, False), (8, 2048, True)])
+def test_persistent_two_waves_d64(sm100, H, N, causal):
+    """A d=64 launch of between one and two waves of pair items (C2's shape:
+    48 heads x 4 Q pairs = 192 items; C3's causal shape: 32 heads x 8 pairs =
+    256 items, on 148 SMs) runs persistent CTAs, some of which walk two
+    items: every head matches the oracle on sampled rows and the result
+    equals one CTA per item bit for bit."""
     lib = abi.load()
-    cfg = orc.AttnConfig("t", 4, 12, 12, 1024, 64, False)
+    cfg = orc.AttnConfig("t", 4, H, H, N, 64, causal)
     q, k, v = orc.make_inputs(cfg, seed=33)
     qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
-    o, lse = run(qd, kd, vd, False)
-    rows = orc.sample_rows(1024, 16, seed=4)
+    o, lse = run(qd, kd, vd, causal)
+    rows = orc.sample_rows(N, 16, seed=4)
     for b in range(4):
-        for h in (0, 5, 11):
+        for h in (0, H // 2 - 1, H - 1):
             ref_o, ref_l = orc.attention_fp32(q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
-                                              v[b:b + 1, h:h + 1], rows=rows)
+                                              v[b:b + 1, h:h + 1], causal=causal, rows=rows)
             assert orc.check(o.cpu()[b:b + 1, h:h + 1, rows], ref_o)["ok"], (b, h)
             assert orc.check_lse(lse.cpu()[b:b + 1, h:h + 1, rows], ref_l)["ok"], (b, h)
     lib.fa_set_debug_flags(64)  # FA_DEBUG_NO_PERSIST
     try:
-        o2, lse2 = run(qd, kd, vd, False)
+        o2, lse2 = run(qd, kd, vd, causal)
     finally:
         lib.fa_set_debug_flags(0)
     assert torch.equal(o, o2)
