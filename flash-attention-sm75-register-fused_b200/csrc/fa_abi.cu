@@ -480,6 +480,28 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
     const int sms = sm_count();
     if (n_items > sms && n_items <= 2LL * sms) p.n_ctas = sms;
   }
+  // Dual-tile items (d = 64, square launches): one 128-row Q tile per item,
+  // its key tiles split between the two softmax groups and merged inside the
+  // CTA, on persistent CTAs.  Finer items than Q pairs: C2's 192 pair items
+  // (1.3 waves, two items on 44 CTAs) become 384 half-length items (2.6
+  // waves).  By default for non-causal launches of one to two waves of pair
+  // items (measured on B200: C2 348 -> 371 TFLOPS); causal items stay on Q
+  // pairs (C3 430 -> 348 with dual tiles).  FA_DEBUG_DUAL_TILES forces them
+  // wherever they apply, FA_DEBUG_PAIR_KERNEL keeps Q pairs.
+  const unsigned dbg = static_cast<unsigned>(g_debug_flags.load(std::memory_order_relaxed));
+  const long long pair_items = static_cast<long long>(k.n_qpairs) * B * k.heads;
+  const bool dual_tiles_default = p.causal == 0 && pair_items > sm_count() &&
+                                  pair_items <= 2LL * sm_count() &&
+                                  (dbg & FA_DEBUG_PAIR_KERNEL) == 0;
+  if (((dbg & FA_DEBUG_DUAL_TILES) != 0 || dual_tiles_default) && head_dim == 64 && !k.dual &&
+      !k.decode && !k.q_tile && !k.pair2 && k.n_splits == 1 && k.heads == Hq && Nq == Nk &&
+      k.n_kv_tiles >= 2) {
+    p.dual = 2;
+    p.n_qpairs = (k.rows + 127) / 128;
+    const long long items = static_cast<long long>(p.n_qpairs) * B * k.heads;
+    const int sms = sm_count();
+    p.n_ctas = items < sms ? static_cast<int>(items) : sms;
+  }
   // Causal launches of at most two waves order their items pair-major over
   // all heads (every head's heaviest pairs first), so no group of heads
   // starts its heaviest items late; larger launches keep the kernel's

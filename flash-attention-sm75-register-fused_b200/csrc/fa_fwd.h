@@ -43,6 +43,9 @@ struct alignas(64) FwdParams {
   // rows, group 0 the first half of the CTA's K/V tiles and group 1 the
   // second, each with its own K/V stream; every group writes a partial result
   // ("sub-split" 2*split + group) for the combine kernel.
+  // dual = 2 (d = 64, no split): the same split of the keys for items of one
+  // 128-row Q tile each (n_qpairs counts tiles); the groups merge their
+  // halves inside the CTA and write O and LSE directly.
   int dual;
   int n_ctas;        // CTAs launched; 0 = one per work item, fewer = persistent CTAs
   // Causal item order: pair-major within groups of head_group (batch, head)

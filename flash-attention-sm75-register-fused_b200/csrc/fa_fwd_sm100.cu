@@ -114,7 +114,11 @@ struct Layout {
   static constexpr int kNumBars = kBarItemEmpty + kItemQ;
   static constexpr int kOffMisc = kOffBar + 8 * kNumBars;
   static constexpr int kOffItemQ = kOffMisc + 16;               // kItemQ ints
-  static constexpr int kBytes = kOffItemQ + 4 * kItemQ;
+  // dual-tile items (d = 64): each softmax thread's (m, l) for the in-CTA
+  // merge of the two groups' key halves, double-buffered by work item
+  static constexpr int kOffXchg = kOffItemQ + 4 * kItemQ;
+  static constexpr int kXchgBytes = (D == 64) ? 2 * 2 * kBlockM * 8 : 0;
+  static constexpr int kBytes = kOffXchg + kXchgBytes;
   static constexpr int kDynBytes = kBytes + 1024;  // slack for 1024-byte alignment
   // tensor memory columns
   static constexpr uint32_t kTmemCols = 512;
@@ -403,7 +407,8 @@ __device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem&
   const int b = it.bh / p.heads;
   const int hq = it.bh % p.heads;
   it.bh_kv = b * p.Hkv + hq / p.group;
-  it.q_row0 = qp * 2 * kBlockM;
+  // dual-tile items (dual == 2) are one 128-row Q tile each
+  it.q_row0 = p.dual == 2 ? qp * kBlockM : qp * 2 * kBlockM;
   int n_kv_tiles = p.n_kv_tiles;
   if (p.ranges == 0) {
     it.nq = p.Nq;
@@ -437,9 +442,10 @@ __device__ __forceinline__ void decode_item(const FwdParams& p, int w, WorkItem&
   };
   const int j_begin = it.sp * p.tiles_per_split;
   if (p.dual) {
-    // both groups on Q tile 0; the split's tiles are halved between them
-    const int n =
-        max(0, min(tiles_of(2 * qp), j_begin + p.tiles_per_split) - j_begin);
+    // both groups on the item's Q tile; the split's tiles are halved
+    // between them
+    const int n = max(0, min(tiles_of(p.dual == 2 ? qp : 2 * qp), j_begin + p.tiles_per_split) -
+                             j_begin);
     it.n_kv[0] = (n + 1) / 2;
     it.n_kv[1] = n / 2;
     it.jb[0] = j_begin;
@@ -948,7 +954,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     decode_item(p, w, it);
     const int n_tiles = g ? it.n_kv[1] : it.n_kv[0];
     const int jb = g ? it.jb[1] : it.jb[0];
-    const int tile = dual ? 2 * it.qp : 2 * it.qp + g;  // global 128-row tile index
+    // global 128-row tile index
+    const int tile = dual ? (p.dual == 2 ? it.qp : 2 * it.qp) : 2 * it.qp + g;
     const int q_row = tile * kBlockM + r;
     // key limit of this row: key k is visible iff k < row_end (causal:
     // pos + causal_off + 1; always at most nk)
@@ -1072,6 +1079,74 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_kernel(const __grid_consta
     const size_t row_index = static_cast<size_t>(lse_row0) + q_row;
     T* const orow = reinterpret_cast<T*>(p.o) + o_row0 + static_cast<long long>(q_row) * p.o_rs;
     const long long lse_index = lse_row0 + q_row;
+    if constexpr (D == 64) {
+      if (p.dual == 2) {
+        // Dual-tile item: the two groups hold O, m, l of the two halves of
+        // the tile's keys on the same TMEM lanes.  Each thread publishes its
+        // row's (m, l); after a named barrier over the eight softmax warps
+        // (AND of their status, so a failed wait anywhere makes both groups
+        // skip the output together) group g merges columns [32g, 32g + 32)
+        //   O = (O0 2^(m0 - m) + O1 2^(m1 - m)) / (l0 2^(m0 - m) + l1 2^(m1 - m))
+        // and group 0 writes the row's LSE.  A second barrier keeps either
+        // group's next P (and so the next item's first PV, which overwrites
+        // O) behind both groups' O reads.
+        if (ok && n_tiles > 0)
+          ok = __all_sync(0xffffffffu,
+                          bar_wait(bar(L::kBarO + g), (cnt + n_tiles - 1) & 1, wc, 22 + g));
+        float* xs = reinterpret_cast<float*>(smem + L::kOffXchg) + (round & 1) * (4 * kBlockM);
+        xs[(g * kBlockM + r) * 2] = m;
+        xs[(g * kBlockM + r) * 2 + 1] = l;
+        const bool all_ok = ptx::bar_and(1, 256, ok);
+        if (all_ok) {
+          ptx::tc_fence_after();
+          const int o_ = (g ^ 1) * kBlockM + r;
+          const float m0 = g ? xs[2 * o_] : m, l0 = g ? xs[2 * o_ + 1] : l;
+          const float m1 = g ? m : xs[2 * o_], l1 = g ? l : xs[2 * o_ + 1];
+          const float mm = fmaxf(m0, m1);
+          const float a0 = l0 > 0.f ? ptx::ex2_approx(m0 - mm) : 0.f;
+          const float a1 = l1 > 0.f ? ptx::ex2_approx(m1 - mm) : 0.f;
+          const float lsum = l0 * a0 + l1 * a1;
+          const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
+          // a group with key tiles has written all of its O rows (warp-uniform)
+          const bool h0 = it.n_kv[0] > 0, h1 = it.n_kv[1] > 0;
+          uint32_t u0[32] = {}, u1[32] = {};
+          if (h0) ptx::tmem_ld32(tmem + lane_off + L::tO(0) + 32 * g, u0);
+          if (h1) ptx::tmem_ld32(tmem + lane_off + L::tO(1) + 32 * g, u1);
+          ptx::tmem_wait_ld();
+          pin_after_wait<32>(u0);
+          pin_after_wait<32>(u1);
+          const float b0 = a0 * inv, b1 = a1 * inv;
+          uint32_t hv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float v0 = 0.f, v1 = 0.f;
+            if (h0) {
+              v0 = __uint_as_float(u0[2 * i]) * b0;
+              v1 = __uint_as_float(u0[2 * i + 1]) * b0;
+            }
+            if (h1) {
+              v0 = fmaf(__uint_as_float(u1[2 * i]), b1, v0);
+              v1 = fmaf(__uint_as_float(u1[2 * i + 1]), b1, v1);
+            }
+            hv[i] = pack2<BF16>(v0, v1);
+          }
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * g);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
+            if (g == 0 && p.lse != nullptr)
+              p.lse[lse_index] = lsum > 0.f ? (mm + __log2f(lsum)) * 0.69314718055994530942f
+                                            : -INFINITY;
+          }
+        }
+        ok = all_ok;
+        ptx::tc_fence_before();
+        ptx::bar_and(2, 256, true);
+        cnt += n_tiles;
+        continue;
+      }
+    }
     // partial-result slot of this group (split mode) in the workspace
     const int ws_slot = dual ? 2 * it.sp + g : it.sp;
     const bool partial = p.n_splits > 1 || dual;

@@ -68,8 +68,12 @@ enum {
                                  kernel instead of the tile kernel, for comparisons */
   FA_DEBUG_NO_PERSIST = 64,     /* one CTA per pair-kernel work item instead of persistent
                                  CTAs, for comparisons */
-  FA_DEBUG_STATIC_DEAL = 128    /* persistent pair-kernel CTAs deal every round in the fixed
+  FA_DEBUG_STATIC_DEAL = 128,   /* persistent pair-kernel CTAs deal every round in the fixed
                                  boustrophedon order (the last rounds too), for comparisons */
+  FA_DEBUG_DUAL_TILES = 256     /* d = 64 square launches as one-Q-tile items whose two softmax
+                                 groups split the keys and merge in the CTA, wherever they apply
+                                 (by default only non-causal launches of one to two waves of Q
+                                 pairs; FA_DEBUG_PAIR_KERNEL keeps Q pairs there) */
 };
 
 /*

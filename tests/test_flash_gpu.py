@@ -307,9 +307,9 @@ def test_forced_kernels_bf16_and_outliers(sm100, flag, d, causal):
 def test_wave_tail_items_on_the_tile_kernel(sm100, d):
     """A non-causal launch whose pair-kernel items fill one wave of SMs plus
     a few (80 heads x 2 Q pairs = 160 items on 148 SMs) runs the last items on
-    the tile kernel at d=128 and keeps them on the pair kernel at d=64: every
-    head, those included, matches the oracle, and the result agrees with the
-    launch kept on the pair kernel (bit for bit at d=64)."""
+    the tile kernel at d=128; at d=64 the launch has no tail split (it runs
+    dual-tile items): every head, those included, matches the oracle, and the
+    result agrees with the launch without the split (bit for bit at d=64)."""
     lib = abi.load()
     cfg = orc.AttnConfig("t", 1, 80, 80, 512, d, False)
     q, k, v = orc.make_inputs(cfg, seed=21)
@@ -372,7 +372,11 @@ def test_persistent_two_waves_d64(sm100, H, N, causal):
     cfg = orc.AttnConfig("t", 4, H, H, N, 64, causal)
     q, k, v = orc.make_inputs(cfg, seed=33)
     qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
-    o, lse = run(qd, kd, vd, causal)
+    lib.fa_set_debug_flags(2)  # FA_DEBUG_PAIR_KERNEL: Q pairs, not dual-tile items
+    try:
+        o, lse = run(qd, kd, vd, causal)
+    finally:
+        lib.fa_set_debug_flags(0)
     rows = orc.sample_rows(N, 16, seed=4)
     for b in range(4):
         for h in (0, H // 2 - 1, H - 1):
@@ -380,11 +384,59 @@ def test_persistent_two_waves_d64(sm100, H, N, causal):
                                               v[b:b + 1, h:h + 1], causal=causal, rows=rows)
             assert orc.check(o.cpu()[b:b + 1, h:h + 1, rows], ref_o)["ok"], (b, h)
             assert orc.check_lse(lse.cpu()[b:b + 1, h:h + 1, rows], ref_l)["ok"], (b, h)
-    lib.fa_set_debug_flags(64)  # FA_DEBUG_NO_PERSIST
+    lib.fa_set_debug_flags(2 | 64)  # FA_DEBUG_PAIR_KERNEL | FA_DEBUG_NO_PERSIST
     try:
         o2, lse2 = run(qd, kd, vd, causal)
     finally:
         lib.fa_set_debug_flags(0)
     assert torch.equal(o, o2)
     assert torch.equal(lse, lse2)
+    assert lib.fa_device_status(0) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,causal,dtype", [
+    (1, 2, 2, 256, True, torch.float16),     # two key tiles: tile 0's second group has none
+    (2, 3, 3, 1000, False, torch.float16),   # ragged last tile
+    (1, 8, 2, 777, True, torch.float16),     # GQA, ragged, causal
+    (2, 4, 4, 640, True, torch.bfloat16),
+    (4, 12, 12, 1024, False, torch.float16),  # C2's shape: 384 items on 148 CTAs
+])
+def test_dual_tile_items_d64(sm100, B, Hq, Hkv, N, causal, dtype):
+    """d=64 launches as one-Q-tile items whose two softmax groups take halves
+    of the keys and merge them inside the CTA (FA_DEBUG_DUAL_TILES; the
+    default for C2's shape): O and LSE match the oracle, repeat bit for bit,
+    and agree with the launch on Q pairs within the kernel-to-kernel
+    tolerance; no watchdog error."""
+    lib = abi.load()
+    cfg = orc.AttnConfig("t", B, Hq, Hkv, N, 64, causal)
+    q, k, v = orc.make_inputs(cfg, seed=N + B, dtype=dtype)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    lib.fa_set_debug_flags(256)  # FA_DEBUG_DUAL_TILES
+    try:
+        o, lse = run(qd, kd, vd, causal)
+        o_again, _ = run(qd, kd, vd, causal)
+    finally:
+        lib.fa_set_debug_flags(0)
+    assert torch.equal(o, o_again)
+    rows = None if B * Hq * N <= 8192 else orc.sample_rows(N, 16, seed=6)
+    ref_o, ref_l = orc.attention_fp32(q, k, v, causal=causal, rows=rows)
+    oc, lc = o.cpu(), lse.cpu()
+    if rows is not None:
+        oc, lc = oc[:, :, rows], lc[:, :, rows]
+    if dtype == torch.bfloat16:
+        assert orc.check(oc, ref_o, atol=BF16_ATOL, rtol=BF16_RTOL)["ok"]
+    else:
+        assert orc.check(oc, ref_o)["ok"]
+    assert orc.check_lse(lc, ref_l)["ok"]
+    lib.fa_set_debug_flags(2)  # FA_DEBUG_PAIR_KERNEL
+    try:
+        o2, lse2 = run(qd, kd, vd, causal)
+    finally:
+        lib.fa_set_debug_flags(0)
+    if (B, Hq, N, causal) == (4, 12, 1024, False):
+        o3, lse3 = run(qd, kd, vd, causal)  # the default plan: dual-tile items
+        assert torch.equal(o, o3) and torch.equal(lse, lse3)
+    tol = 2 * (BF16_ATOL if dtype == torch.bfloat16 else 2e-3)
+    assert (o.float() - o2.float()).abs().max().item() <= tol
+    assert (lse - lse2).abs().max().item() <= 2e-4
     assert lib.fa_device_status(0) == 0
