@@ -482,20 +482,24 @@ int launch_attention(const void* Q, const void* K, const void* V, void* O, float
   }
   // Dual-tile items (d = 64, square launches): one 128-row Q tile per item,
   // its key tiles split between the two softmax groups and merged inside the
-  // CTA, on persistent CTAs.  Finer items than Q pairs: C2's 192 pair items
-  // (1.3 waves, two items on 44 CTAs) become 384 half-length items (2.6
-  // waves).  By default for non-causal launches of one to two waves of pair
-  // items (measured on B200: C2 348 -> 371 TFLOPS); causal items stay on Q
-  // pairs (C3 430 -> 348 with dual tiles).  FA_DEBUG_DUAL_TILES forces them
-  // wherever they apply, FA_DEBUG_PAIR_KERNEL keeps Q pairs.
+  // CTA, on persistent CTAs.  Finer items than Q pairs, shorter ones than the
+  // tile kernel's: C2's 192 pair items (1.3 waves, two items on 44 CTAs)
+  // become 384 half-length items (2.6 waves).  By default for non-causal
+  // launches of at most two waves of Q pairs (measured on B200: C2 348 ->
+  // 371 TFLOPS against persistent Q pairs; against the tile kernel below one
+  // wave, C1 5.9 -> 6.5, B=1 H=4 N=4096 382 -> 495, B=1 H=8 N=512 44 -> 50,
+  // B=2 H=8 N=1024 262 -> 267); causal items stay on Q pairs (C3 430 -> 348
+  // with dual tiles).  FA_DEBUG_DUAL_TILES forces them wherever they apply,
+  // FA_DEBUG_PAIR_KERNEL / FA_DEBUG_TILE_KERNEL keep their kernels.
   const unsigned dbg = static_cast<unsigned>(g_debug_flags.load(std::memory_order_relaxed));
-  const long long pair_items = static_cast<long long>(k.n_qpairs) * B * k.heads;
-  const bool dual_tiles_default = p.causal == 0 && pair_items > sm_count() &&
-                                  pair_items <= 2LL * sm_count() &&
-                                  (dbg & FA_DEBUG_PAIR_KERNEL) == 0;
+  const long long pair_items = static_cast<long long>((k.rows + 255) / 256) * B * k.heads;
+  const bool dual_tiles_default =
+      p.causal == 0 && pair_items <= 2LL * sm_count() &&
+      (dbg & (FA_DEBUG_PAIR_KERNEL | FA_DEBUG_TILE_KERNEL | FA_DEBUG_PAIR2_KERNEL)) == 0;
   if (((dbg & FA_DEBUG_DUAL_TILES) != 0 || dual_tiles_default) && head_dim == 64 && !k.dual &&
-      !k.decode && !k.q_tile && !k.pair2 && k.n_splits == 1 && k.heads == Hq && Nq == Nk &&
+      !k.decode && !k.pair2 && k.n_splits == 1 && k.heads == Hq && Nq == Nk &&
       k.n_kv_tiles >= 2) {
+    p.q_tile = 0;
     p.dual = 2;
     p.n_qpairs = (k.rows + 127) / 128;
     const long long items = static_cast<long long>(p.n_qpairs) * B * k.heads;

@@ -266,7 +266,8 @@ def test_parity_late_max_growth_kvcache(sm100, Nq, Nk):
 # the pair kernel (two Q tiles per CTA; the default once a launch fills a
 # wave), its CTA-pair form (one product for two SMs, d = 128; opt-in) and the
 # tile kernel (one Q tile per CTA, S double-buffered; the default for
-# launches that would leave SMs idle).
+# launches that would leave SMs idle, except non-causal d=64 ones, which run
+# dual-tile items).
 FORCED = [(1, 1, 1, 1, 64, True), (1, 2, 2, 17, 128, False), (1, 1, 1, 129, 64, False),
           (1, 2, 2, 255, 128, True), (1, 8, 2, 640, 128, True), (2, 6, 1, 333, 64, False),
           (3, 6, 2, 900, 128, True), (1, 4, 4, 2048, 128, True), (2, 5, 5, 700, 64, True)]

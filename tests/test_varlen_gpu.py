@@ -152,15 +152,23 @@ def test_padded_matches_oracle(sm100, case, mode):
 
 
 def test_padded_full_ranges_is_fa_fwd(sm100):
-    """Full ranges give fa_fwd's bits (same kernel, same tiles)."""
+    """Full ranges give fa_fwd's bits when both run the same kernel on the same
+    tiles: the tile kernel, which the padded path takes at this size and
+    FA_DEBUG_TILE_KERNEL gives fa_fwd (whose own non-causal d=64 default here
+    is dual-tile items)."""
     B, Hq, Hkv, N, d = 2, 8, 4, 1000, 64
     g = torch.Generator().manual_seed(4)
     q, k, v = (torch.randn(B, h, N, d, generator=g).half().cuda() for h in (Hq, Hkv, Hkv))
+    lib = abi.load()
     for causal in (False, True):
         o = fa.flash_attention_forward_padded(q, k, v, [0, 0], [N, N], [0, 0], [N, N],
                                               causal=causal)
         o2 = torch.empty_like(q)
-        assert abi.fa_fwd(q, k, v, o2, None, causal=causal) == 0
+        lib.fa_set_debug_flags(8)  # FA_DEBUG_TILE_KERNEL
+        try:
+            assert abi.fa_fwd(q, k, v, o2, None, causal=causal) == 0
+        finally:
+            lib.fa_set_debug_flags(0)
         assert torch.equal(o, o2)
 
 

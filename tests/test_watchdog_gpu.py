@@ -11,9 +11,10 @@ from tests import abi_ctypes as abi
 pytestmark = pytest.mark.gpu
 
 
-def test_wait_timeout_reports_status_and_context_survives(sm100):
+@pytest.mark.parametrize("d", [128, 64])  # d=64: dual-tile items (named barriers in the merge)
+def test_wait_timeout_reports_status_and_context_survives(sm100, d):
     lib = abi.load()
-    cfg = orc.AttnConfig("t", 1, 2, 2, 512, 128, False)
+    cfg = orc.AttnConfig("t", 1, 2, 2, 512, d, False)
     q, k, v = (t.cuda() for t in orc.make_inputs(cfg, seed=3))
     o = torch.empty_like(q)
     lib.fa_device_status(1)             # clear any earlier record
